@@ -1,0 +1,125 @@
+#pragma once
+// TileMix drop-in C++ API for the B200 (sm_100a) implementation.
+//
+// Same names, signatures, default arguments, constants, mask format and
+// cudaError_t contract as the reference's include/attention_fused.h:11-72, so
+// existing callers (the reference's src/main.cu and its test suite) compile
+// and behave unchanged against libtilemix_b200.so. The batched/causal entry
+// point at the end is an addition with no reference counterpart.
+//
+// Error contract (reference src/tilemix.cu:227-236,242-277):
+//   cudaErrorInvalidValue        any null/non-positive/non-finite argument,
+//                                partial quantized sets, bad routing masks
+//   cudaErrorNotSupported        d > kFusedMaxHeadDim (checked after the
+//                                InvalidValue checks), or a device that is not
+//                                sm_100 (this library carries sm_100a code only)
+//   cudaErrorInvalidConfiguration grid / shared-memory limits exceeded
+//   otherwise                    the launch status
+// All pointers are caller-owned device pointers; the library allocates nothing,
+// never writes its inputs and writes exactly M*d output floats. Every call is
+// asynchronous on `stream` and uses the calling thread's current device.
+
+#include "matmul_config.h"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+inline constexpr int kFusedMaxHeadDim = 128;
+inline constexpr int kFusedRowThreads = kThreads / kBlockM;
+inline constexpr int kTileMixQQuantRows = 128;   // one Q scale per 128 rows x d
+inline constexpr int kTileMixKQuantRows = 64;    // one K scale per 64 rows x d
+static_assert(kTileMixQQuantRows % kBlockM == 0 && kTileMixKQuantRows % kBlockN == 0);
+static_assert(kFusedRowThreads > 0 && (kFusedRowThreads & (kFusedRowThreads - 1)) == 0);
+
+// Shared-memory footprint formulas of the reference's WMMA kernel
+// (reference include/attention_fused.h:21-32). Kept with identical values for
+// source compatibility; the B200 kernel's own footprint is
+// tilemix_b200_shared_bytes().
+inline constexpr std::size_t fused_fp16_shared_bytes(int d) {
+    if (d <= 0 || d > kFusedMaxHeadDim) return 0;
+    const int padded_d = ((d + kTileK - 1) / kTileK) * kTileK;
+    return sizeof(__half) * static_cast<std::size_t>(padded_d) * (kBlockM + 2 * kBlockN)
+         + sizeof(float) * kBlockM * kBlockN;
+}
+
+inline constexpr std::size_t tilemix_shared_bytes(int d, bool quantized) {
+    if (d <= 0 || d > kFusedMaxHeadDim) return 0;
+    const int padded_d = ((d + kTileK - 1) / kTileK) * kTileK;
+    return fused_fp16_shared_bytes(d) + (quantized ? (kBlockM + kBlockN) * padded_d : 0);
+}
+
+// Routing mask format (reference include/attention_fused.h:34-45): one bit per
+// (16-row query tile, group of key_tiles_per_group 32-key tiles), packed
+// LSB-first into uint64 words, ceil(groups/64) words per query tile, query
+// tiles row-major. Bit 1 = INT8 scores, bit 0 = FP16 scores.
+inline constexpr std::size_t tilemix_routing_words_per_row(int N, int key_tiles_per_group) {
+    if (N <= 0 || key_tiles_per_group <= 0) return 0;
+    const std::size_t key_tiles = (static_cast<std::size_t>(N) - 1) / kBlockN + 1;
+    const std::size_t groups = (key_tiles - 1) / key_tiles_per_group + 1;
+    return (groups - 1) / 64 + 1;
+}
+
+inline constexpr std::size_t tilemix_routing_word_count(int M, int N, int key_tiles_per_group) {
+    if (M <= 0) return 0;
+    return ((static_cast<std::size_t>(M) - 1) / kBlockM + 1)
+         * tilemix_routing_words_per_row(N, key_tiles_per_group);
+}
+
+struct TileMixRouting {
+    const std::uint64_t* words = nullptr;   // null = every tile FP16
+    std::size_t word_count = 0;
+    int key_tiles_per_group = 1;
+    std::uint8_t* decoded_bits = nullptr;   // optional trace: [query_tiles][key_tiles] bytes
+};
+
+struct TileMixQuantized {
+    const std::int8_t* q = nullptr;         // [M, d] from quantize_tilemix_qk
+    const std::int8_t* k = nullptr;         // [N, d]
+    const __half* q_scales = nullptr;       // [ceil(M/128)]
+    const __half* k_scales = nullptr;       // [ceil(N/64)]
+    std::int32_t* score_dots = nullptr;     // optional trace: [M, N] raw INT32 dots of INT8 pairs
+};
+
+// Stage 1: per-block symmetric INT8 quantization of Q (128-row blocks) and K
+// (64-row blocks); scale = absmax/127 in fp32 (stored fp16), values rounded
+// half away from zero and clamped to +-127.
+cudaError_t quantize_tilemix_qk(const __half* Q, const __half* K,
+                                std::int8_t* Q8, std::int8_t* K8,
+                                __half* q_scales, __half* k_scales,
+                                int M, int N, int d, cudaStream_t stream = nullptr);
+
+// Stages 2-5: routed QK^T (tcgen05 kind::i8 or kind::f16), online softmax,
+// fp16 PV MMA and normalisation in one kernel. O is fp32 [M, d].
+cudaError_t launch_fused_fp16_attention(const __half* Q, const __half* K, const __half* V,
+                                        float* O, int M, int N, int d, float score_scale,
+                                        cudaStream_t stream = nullptr,
+                                        const TileMixRouting& routing = {},
+                                        const TileMixQuantized& quantized = {});
+
+// ---------------------------------------------------------------- additions
+// Shared memory the B200 attention kernel requests for head dim d (0 if d is
+// out of range).
+std::size_t tilemix_b200_shared_bytes(int d, bool quantized);
+
+// Batched quantizer over `heads` contiguous [M,d] / [N,d] slabs
+// ([B*H, S, D] layout). Scales are [heads][ceil(M/128)] and [heads][ceil(N/64)].
+cudaError_t quantize_tilemix_qk_batched(const __half* Q, const __half* K,
+                                        std::int8_t* Q8, std::int8_t* K8,
+                                        __half* q_scales, __half* k_scales,
+                                        int heads, int M, int N, int d,
+                                        cudaStream_t stream = nullptr);
+
+// Batched / causal attention over `heads` contiguous slabs. Per head the
+// semantics are exactly launch_fused_fp16_attention's; routing words, scales
+// and trace outputs are concatenated per head (routing.word_count covers all
+// heads). causal != 0 masks key > query (top-left aligned) and skips key
+// tiles that lie wholly above the diagonal.
+cudaError_t tilemix_attention_batched(const __half* Q, const __half* K, const __half* V,
+                                      float* O, int heads, int M, int N, int d,
+                                      float score_scale, bool causal,
+                                      cudaStream_t stream = nullptr,
+                                      const TileMixRouting& routing = {},
+                                      const TileMixQuantized& quantized = {});

@@ -1,0 +1,27 @@
+#!/usr/bin/env bash
+# Builds the CPU oracles -- TEST INFRASTRUCTURE ONLY.
+#   oracle/_build/libtilemix_oracle.so : the C restatement (tilemix_oracle.c)
+#   oracle/_ref/libtilemix_ref.so      : the reference's OWN CPU oracle headers
+#                                        (src/tests/reference_*.h), compiled where
+#                                        they lie, behind ref_shim.cpp
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default /root/reference)
+# The reference build is skipped, not failed, when the reference tree is absent.
+set -euo pipefail
+here="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
+ref_root="${1:-/root/reference}"
+cuda_inc="${CUDA_HOME:-/usr/local/cuda}/include"
+
+mkdir -p "$here/_build"
+gcc -std=c11 -O3 -march=x86-64-v3 -ffp-contract=off -fopenmp -fPIC -shared -Wall -Wextra \
+    "$here/tilemix_oracle.c" -o "$here/_build/libtilemix_oracle.so" -lm
+
+if [[ -f "$ref_root/src/tests/reference_tilemix.h" ]]; then
+    mkdir -p "$here/_ref"
+    g++ -std=c++17 -O3 -march=x86-64-v3 -ffp-contract=off -fopenmp -fPIC -shared \
+        -I"$cuda_inc" -I"$ref_root/src/tests" -I"$ref_root/include" \
+        "$here/ref_shim.cpp" -o "$here/_ref/libtilemix_ref.so"
+    echo "built $here/_ref/libtilemix_ref.so from $ref_root/src/tests"
+else
+    echo "reference tree not found at $ref_root; oracle/_ref not rebuilt"
+fi
+echo "built $here/_build/libtilemix_oracle.so"

@@ -1,0 +1,205 @@
+// Drop-in API layer: argument validation with the reference's error contract
+// (src/tilemix.cu:223-278), device checks, and the extern "C" ABI of
+// include/tilemix_c_api.h. Kernels live in quantize.cu and attention.cu.
+#include "attention_fused.h"
+#include "kernels.cuh"
+#include "tilemix_c_api.h"
+
+#include <cmath>
+#include <cstddef>
+#include <cstdint>
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+// sm_100 check, cached per device (the reference queries cudaDeviceProp on
+// every launch, src/tilemix.cu:254-260; one attribute query per device here).
+cudaError_t check_device() {
+    static int state[kMaxDevices] = {0};   // 0 unknown, 1 supported, 2 not supported
+    int device = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status != cudaSuccess) return status;
+    if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (state[device] == 0) {
+        int major = 0;
+        status = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+        if (status != cudaSuccess) return status;
+        state[device] = major == 10 ? 1 : 2;
+    }
+    return state[device] == 1 ? cudaSuccess : cudaErrorNotSupported;
+}
+
+bool fits(long long heads, long long rows, long long d) {
+    return heads > 0 && rows > 0 && d > 0 && heads * rows <= (1ll << 40) / d;
+}
+
+cudaError_t quantize_impl(const __half* Q, const __half* K, std::int8_t* Q8, std::int8_t* K8,
+                          __half* q_scales, __half* k_scales, int heads, int M, int N, int d,
+                          cudaStream_t stream) {
+    if (!Q || !K || !Q8 || !K8 || !q_scales || !k_scales || heads <= 0 || M <= 0 || N <= 0 || d <= 0) {
+        return cudaErrorInvalidValue;
+    }
+    if (d > kFusedMaxHeadDim) return cudaErrorNotSupported;
+    if (!fits(heads, M, d) || !fits(heads, N, d)) return cudaErrorInvalidValue;
+    const cudaError_t status = check_device();
+    if (status != cudaSuccess) return status;
+    return tilemix::launch_quantize(Q, K, Q8, K8, q_scales, k_scales, heads, M, N, d, stream);
+}
+
+cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, float* O, int heads,
+                           int M, int N, int d, float score_scale, bool causal, cudaStream_t stream,
+                           const TileMixRouting& routing, const TileMixQuantized& quantized) {
+    // Same checks, same order as src/tilemix.cu:242-253.
+    if (!Q || !K || !V || !O || heads <= 0 || M <= 0 || N <= 0 || d <= 0 ||
+        !std::isfinite(score_scale) || routing.key_tiles_per_group <= 0 ||
+        (!routing.words && routing.word_count != 0)) {
+        return cudaErrorInvalidValue;
+    }
+    if (d > kFusedMaxHeadDim) return cudaErrorNotSupported;
+    const std::size_t per_head = tilemix_routing_word_count(M, N, routing.key_tiles_per_group);
+    if (routing.words && routing.word_count / static_cast<std::size_t>(heads) < per_head) {
+        return cudaErrorInvalidValue;
+    }
+    const bool has_quantized = quantized.q && quantized.k && quantized.q_scales && quantized.k_scales;
+    const bool any_quantized = quantized.q || quantized.k || quantized.q_scales || quantized.k_scales ||
+                               quantized.score_dots;
+    if ((any_quantized && !has_quantized) || (routing.words && !has_quantized)) return cudaErrorInvalidValue;
+    if (!fits(heads, M, d) || !fits(heads, N, d)) return cudaErrorInvalidValue;
+    cudaError_t status = check_device();
+    if (status != cudaSuccess) return status;
+    if (static_cast<long long>((M - 1) / 128 + 1) * heads > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+
+    tilemix::AttentionProblem prob{};
+    prob.q = Q; prob.k = K; prob.v = V; prob.o = O;
+    prob.words = routing.words;
+    prob.decoded_bits = routing.decoded_bits;
+    prob.key_tiles_per_group = routing.key_tiles_per_group;
+    if (has_quantized) {
+        prob.q8 = quantized.q; prob.k8 = quantized.k;
+        prob.q_scales = quantized.q_scales; prob.k_scales = quantized.k_scales;
+        prob.score_dots = quantized.score_dots;
+    }
+    prob.heads = heads; prob.M = M; prob.N = N; prob.d = d;
+    prob.score_scale = score_scale;
+    prob.causal = causal;
+    return tilemix::launch_attention(prob, stream);
+}
+
+TileMixRouting to_cpp(const tilemix_routing* r) {
+    TileMixRouting out{};
+    if (r) {
+        out.words = r->words;
+        out.word_count = r->word_count;
+        out.key_tiles_per_group = r->key_tiles_per_group;
+        out.decoded_bits = r->decoded_bits;
+    }
+    return out;
+}
+
+TileMixQuantized to_cpp(const tilemix_quantized* q) {
+    TileMixQuantized out{};
+    if (q) {
+        out.q = q->q;
+        out.k = q->k;
+        out.q_scales = static_cast<const __half*>(q->q_scales);
+        out.k_scales = static_cast<const __half*>(q->k_scales);
+        out.score_dots = q->score_dots;
+    }
+    return out;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- C++ drop-in API
+cudaError_t quantize_tilemix_qk(const __half* Q, const __half* K, std::int8_t* Q8, std::int8_t* K8,
+                                __half* q_scales, __half* k_scales, int M, int N, int d,
+                                cudaStream_t stream) {
+    return quantize_impl(Q, K, Q8, K8, q_scales, k_scales, 1, M, N, d, stream);
+}
+
+cudaError_t launch_fused_fp16_attention(const __half* Q, const __half* K, const __half* V, float* O,
+                                        int M, int N, int d, float score_scale, cudaStream_t stream,
+                                        const TileMixRouting& routing, const TileMixQuantized& quantized) {
+    return attention_impl(Q, K, V, O, 1, M, N, d, score_scale, false, stream, routing, quantized);
+}
+
+std::size_t tilemix_b200_shared_bytes(int d, bool quantized) {
+    (void)quantized;   // the kernel reserves the INT8 tiles either way
+    return tilemix::attention_smem_bytes(d);
+}
+
+cudaError_t quantize_tilemix_qk_batched(const __half* Q, const __half* K, std::int8_t* Q8,
+                                        std::int8_t* K8, __half* q_scales, __half* k_scales,
+                                        int heads, int M, int N, int d, cudaStream_t stream) {
+    return quantize_impl(Q, K, Q8, K8, q_scales, k_scales, heads, M, N, d, stream);
+}
+
+cudaError_t tilemix_attention_batched(const __half* Q, const __half* K, const __half* V, float* O,
+                                      int heads, int M, int N, int d, float score_scale, bool causal,
+                                      cudaStream_t stream, const TileMixRouting& routing,
+                                      const TileMixQuantized& quantized) {
+    return attention_impl(Q, K, V, O, heads, M, N, d, score_scale, causal, stream, routing, quantized);
+}
+
+// ---------------------------------------------------------------------- C-ABI
+extern "C" {
+
+int tilemix_abi_version(void) { return TILEMIX_ABI_VERSION; }
+
+int tilemix_quantize_qk(const void* Q, const void* K, int8_t* Q8, int8_t* K8, void* q_scales,
+                        void* k_scales, int M, int N, int d, void* stream) {
+    return static_cast<int>(quantize_impl(static_cast<const __half*>(Q), static_cast<const __half*>(K),
+                                          Q8, K8, static_cast<__half*>(q_scales),
+                                          static_cast<__half*>(k_scales), 1, M, N, d,
+                                          static_cast<cudaStream_t>(stream)));
+}
+
+int tilemix_fused_attention(const void* Q, const void* K, const void* V, float* O, int M, int N,
+                            int d, float score_scale, void* stream, const tilemix_routing* routing,
+                            const tilemix_quantized* quantized) {
+    return static_cast<int>(attention_impl(static_cast<const __half*>(Q), static_cast<const __half*>(K),
+                                           static_cast<const __half*>(V), O, 1, M, N, d, score_scale,
+                                           false, static_cast<cudaStream_t>(stream), to_cpp(routing),
+                                           to_cpp(quantized)));
+}
+
+int tilemix_quantize_qk_batched(const void* Q, const void* K, int8_t* Q8, int8_t* K8, void* q_scales,
+                                void* k_scales, int heads, int M, int N, int d, void* stream) {
+    return static_cast<int>(quantize_impl(static_cast<const __half*>(Q), static_cast<const __half*>(K),
+                                          Q8, K8, static_cast<__half*>(q_scales),
+                                          static_cast<__half*>(k_scales), heads, M, N, d,
+                                          static_cast<cudaStream_t>(stream)));
+}
+
+int tilemix_attention_batched(const void* Q, const void* K, const void* V, float* O, int heads,
+                              int M, int N, int d, float score_scale, int causal, void* stream,
+                              const tilemix_routing* routing, const tilemix_quantized* quantized) {
+    return static_cast<int>(attention_impl(static_cast<const __half*>(Q), static_cast<const __half*>(K),
+                                           static_cast<const __half*>(V), O, heads, M, N, d,
+                                           score_scale, causal != 0, static_cast<cudaStream_t>(stream),
+                                           to_cpp(routing), to_cpp(quantized)));
+}
+
+size_t tilemix_routing_word_count_c(int M, int N, int key_tiles_per_group) {
+    return tilemix_routing_word_count(M, N, key_tiles_per_group);
+}
+
+size_t tilemix_routing_words_per_row_c(int N, int key_tiles_per_group) {
+    return tilemix_routing_words_per_row(N, key_tiles_per_group);
+}
+
+size_t tilemix_reference_shared_bytes(int d, int quantized) {
+    return tilemix_shared_bytes(d, quantized != 0);
+}
+
+size_t tilemix_b200_shared_bytes_c(int d, int quantized) {
+    return tilemix_b200_shared_bytes(d, quantized != 0);
+}
+
+int tilemix_read_and_clear_status(unsigned int* status) {
+    if (!status) return static_cast<int>(cudaErrorInvalidValue);
+    return static_cast<int>(tilemix::read_and_clear_status(status));
+}
+
+}  // extern "C"

@@ -1,0 +1,748 @@
+// Stages 2-5 of TileMix in one sm_100a kernel: routed QK^T on tcgen05 tensor
+// cores (kind::i8 with s32 accumulators, or kind::f16 with f32 accumulators),
+// online softmax, fp16 PV MMA and output normalisation. The S x S score matrix
+// only ever lives in TMEM.
+//
+// Semantics per head follow the reference kernel (src/tilemix.cu:51-220):
+//   * routing bit per (16-row query tile, 32-key tile), decoded exactly as
+//     src/tilemix.cu:99-103;
+//   * INT8 score = float(dot) * q_scale(row/128) * k_scale(key/64) * score_scale,
+//     FP16 score = (q . k in fp32) * score_scale (src/tilemix.cu:151-165);
+//   * softmax over all keys < N (plus the causal extension key <= query);
+//   * O = (sum_k p_k v_k) / (sum_k p_k) in fp32 (src/tilemix.cu:213-219).
+// Differences that stay inside the parity tolerance: exp2 with log2(e) folded
+// into the score scale, P rounded to fp16 for the PV tensor-core MMA, and the
+// running max only moved when it grows by more than 2^8 (the final result is
+// unchanged mathematically; P stays <= 256, well inside fp16).
+//
+// CTA = one 128-row query tile of one head; 256 threads, warp-specialised:
+//   warp 0     producer: TMA (or, for head dims TMA cannot address, plain
+//              loads) of Q, Q8 once and K/K8, V per 128-key block into
+//              2-stage rings, 128-byte swizzled K-major tiles
+//   warp 1     MMA issuer (one lane) + TMEM owner (512 columns:
+//              S0 | S1 | O): QK^T of block j into S[j%2], PV of block j-1
+//   warps 4-7  softmax: thread t owns query row t = TMEM lane t; dequantises,
+//              masks, exponentiates, writes P (fp16) over S in TMEM, rescales
+//              O in TMEM when the max moves, final normalise + store
+//
+// Routing inside a 128-row tile: for each 32-key tile the 8 routing bits of
+// the tile's 16-row query tiles form a pattern. Runs of key tiles with equal
+// patterns are issued as one MMA per precision with N = 32 * run length; the
+// FP16 MMA disables the TMEM lanes of INT8 rows and vice versa (tcgen05.mma
+// disable-output-lane), so both kinds share one accumulator. A uniform tile
+// costs one MMA; a mixed one costs one of each.
+//
+// Every mbarrier wait is bounded (1 s of %globaltimer). A wait that runs out
+// records a code in g_tilemix_status, raises a CTA-wide abort flag and every
+// role returns; in-flight TMA loads and MMAs are drained (again bounded)
+// before TMEM is freed, so a protocol bug surfaces as an error status instead
+// of a hung GPU.
+#include "kernels.cuh"
+#include "sm100.cuh"
+
+#include <cuda.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+namespace tilemix {
+
+__device__ unsigned int g_tilemix_status = 0;
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kTileRows = 128;
+constexpr int kTileKeys = 128;
+constexpr int kKStages = 2;
+constexpr int kVStages = 2;
+constexpr int kAttnThreads = 256;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS1 = 128;           // S0 at column 0, S1 at 128
+constexpr uint32_t kColO = 256;
+constexpr uint32_t kAtomBytes = 128 * 128;   // 128 rows x 128 bytes
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;    // log2 units: rescale only if max grows by > 2^8
+
+// Watchdog codes (bit positions say which wait gave up).
+enum : unsigned int {
+    kStatusProducer = 1u << 0,
+    kStatusMma = 1u << 1,
+    kStatusSoftmax = 1u << 2,
+    kStatusDrain = 1u << 3,
+};
+
+template <int kAtoms>
+struct SmemLayout {
+    static constexpr uint32_t kQ = 0;
+    static constexpr uint32_t kQ8 = kQ + kAtoms * kAtomBytes;
+    static constexpr uint32_t kK = kQ8 + kAtomBytes;
+    static constexpr uint32_t kKStride = kAtoms * kAtomBytes;
+    static constexpr uint32_t kK8 = kK + kKStages * kKStride;
+    static constexpr uint32_t kV = kK8 + kKStages * kAtomBytes;
+    static constexpr uint32_t kVStride = kAtoms * kAtomBytes;
+    static constexpr uint32_t kBars = kV + kVStages * kVStride;
+    // barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2],
+    //           s_full[2], p_full[2], pv_done, drain
+    static constexpr uint32_t kNumBars = 15;
+    static constexpr uint32_t kMisc = kBars + kNumBars * 8;   // tmem base, abort flag
+    static constexpr uint32_t kEnd = kMisc + 16;
+    static constexpr uint32_t kBytes = kEnd + 1024;           // + alignment slack
+};
+
+enum Bar : int {
+    kBarQFull = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7,
+    kBarSFull = 9, kBarPFull = 11, kBarPvDone = 13, kBarDrain = 14,
+};
+
+struct Params {
+    const __half* q;
+    const __half* k;
+    const __half* v;
+    const std::int8_t* q8;
+    const std::int8_t* k8;
+    const __half* q_scales;
+    const __half* k_scales;
+    float* o;
+    const std::uint64_t* words;
+    std::uint8_t* decoded_bits;
+    std::int32_t* score_dots;
+    int heads, M, N, d;
+    int q_tiles, kv_blocks, q16_tiles, k32_tiles;
+    int group;
+    int words_per_row;
+    long long words_per_head;
+    int q_scale_blocks, k_scale_blocks;
+    float scale_log2;
+    int causal;
+    int routed;
+    int f16_ksteps, i8_ksteps, pv_n;
+    int o_vec;
+};
+
+// Bounded wait, called by all 32 lanes of a warp; returns a warp-uniform
+// verdict. On timeout it records `code` and raises the CTA abort flag.
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                         unsigned int code) {
+    bool ok = mbar_try_wait(bar, parity);
+    if (!ok) {
+        const uint64_t start = global_timer_ns();
+        while (true) {
+            if (mbar_try_wait(bar, parity)) { ok = true; break; }
+            if (*abort_flag) break;
+            if (global_timer_ns() - start > kWaitLimitNs) {
+                *abort_flag = 1;
+                atomicOr(&g_tilemix_status, code);
+                break;
+            }
+        }
+    }
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Routing summary of KV block j for this CTA's 8 query tiles, computed by a
+// whole warp: pat[kt] bit t = INT8 for (query tile t, key tile kt).
+struct BlockRoute {
+    uint32_t pat[4];
+    uint32_t valid_rows;   // bit t = query tile t exists (t < 8)
+    int ktiles;            // key tiles of this block that exist (1..4)
+    bool need_f16;
+    bool need_i8;
+};
+
+__device__ __forceinline__ bool route_bit(const Params& p, int head, int q16, int gkt) {
+    const long long group = gkt / p.group;
+    const std::uint64_t word = __ldg(p.words + head * p.words_per_head
+                                     + static_cast<long long>(q16) * p.words_per_row + group / 64);
+    return ((word >> (group % 64)) & 1ull) != 0;
+}
+
+__device__ __forceinline__ BlockRoute block_route(const Params& p, int head, int qt, int j,
+                                                  uint32_t lane) {
+    BlockRoute r;
+    const int q16 = qt * (kTileRows / 16) + static_cast<int>(lane);
+    const bool q_valid = lane < 8 && q16 < p.q16_tiles;
+    r.valid_rows = __ballot_sync(0xffffffffu, q_valid);
+    r.ktiles = min(4, p.k32_tiles - 4 * j);
+    r.need_f16 = false;
+    r.need_i8 = false;
+    #pragma unroll
+    for (int kt = 0; kt < 4; ++kt) {
+        const bool bit = p.routed && q_valid && kt < r.ktiles && route_bit(p, head, q16, 4 * j + kt);
+        r.pat[kt] = __ballot_sync(0xffffffffu, bit);
+        if (kt < r.ktiles) {
+            r.need_i8 |= r.pat[kt] != 0;
+            r.need_f16 |= (~r.pat[kt] & r.valid_rows) != 0;
+        }
+    }
+    return r;
+}
+
+__device__ __forceinline__ void lane_mask(uint32_t tiles, uint32_t (&m)[4]) {
+    #pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        m[w] = ((tiles >> (2 * w)) & 1u ? 0x0000ffffu : 0u) | ((tiles >> (2 * w + 1)) & 1u ? 0xffff0000u : 0u);
+    }
+}
+
+// Plain-load fallback for head dims TMA cannot address (d % 16 != 0 or
+// unaligned bases): writes the same 128-byte-swizzled K-major layout TMA
+// produces, zero-filling rows >= rows_total and columns >= d.
+__device__ void manual_tile_f16(uint8_t* dst, const __half* src, int row0, int rows_total, int d,
+                                int atoms, uint32_t lane) {
+    const uint16_t* s = reinterpret_cast<const uint16_t*>(src);
+    for (int c = lane; c < atoms * kTileRows * 8; c += 32) {
+        const int atom = c / (kTileRows * 8), rem = c % (kTileRows * 8);
+        const int row = rem / 8, chunk = rem % 8;
+        const int col0 = atom * 64 + chunk * 8, grow = row0 + row;
+        uint32_t w[4];
+        #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            uint32_t lo = 0, hi = 0;
+            const int c0 = col0 + 2 * e;
+            if (grow < rows_total) {
+                const std::size_t base = static_cast<std::size_t>(grow) * d;
+                if (c0 < d) lo = s[base + c0];
+                if (c0 + 1 < d) hi = s[base + c0 + 1];
+            }
+            w[e] = lo | (hi << 16);
+        }
+        const uint32_t off = atom * kAtomBytes + row * 128 + ((chunk ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst + off) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+__device__ void manual_tile_i8(uint8_t* dst, const std::int8_t* src, int row0, int rows_total,
+                               int d, uint32_t lane) {
+    const uint8_t* s = reinterpret_cast<const uint8_t*>(src);
+    for (int c = lane; c < kTileRows * 8; c += 32) {
+        const int row = c / 8, chunk = c % 8;
+        const int col0 = chunk * 16, grow = row0 + row;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        if (grow < rows_total) {
+            const std::size_t base = static_cast<std::size_t>(grow) * d;
+            #pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const int col = col0 + e;
+                if (col < d) w[e >> 2] |= static_cast<uint32_t>(s[base + col]) << ((e & 3) * 8);
+            }
+        }
+        const uint32_t off = row * 128 + ((chunk ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst + off) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+template <int kAtoms, bool kUseTma, bool kTrace>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v,
+                         const __grid_constant__ CUtensorMap tm_q8,
+                         const __grid_constant__ CUtensorMap tm_k8,
+                         const Params p) {
+    using L = SmemLayout<kAtoms>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    const uint32_t pad = ((raw_u32 + 1023u) & ~1023u) - raw_u32;
+    uint8_t* smem = smem_raw + pad;
+    const uint32_t sbase = raw_u32 + pad;
+    auto bar = [&](int i) -> uint32_t { return sbase + L::kBars + 8u * static_cast<uint32_t>(i); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31u;
+
+    // Work item: heaviest (last) query tiles first so causal tails are short.
+    const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x) / p.heads;
+    const int head = static_cast<int>(blockIdx.x) % p.heads;
+    const int nblk = p.causal ? min(p.kv_blocks, qt + 1) : p.kv_blocks;
+    const int load_i8 = p.routed;
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar(kBarQFull), 1);
+        for (int s = 0; s < kKStages; ++s) { mbar_init(bar(kBarKFull + s), 1); mbar_init(bar(kBarKEmpty + s), 1); }
+        for (int s = 0; s < kVStages; ++s) { mbar_init(bar(kBarVFull + s), 1); mbar_init(bar(kBarVEmpty + s), 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(bar(kBarSFull + b), 1); mbar_init(bar(kBarPFull + b), 128); }
+        mbar_init(bar(kBarPvDone), 1);
+        mbar_init(bar(kBarDrain), 1);
+        *abort_flag = 0;
+        mbar_init_fence();
+        fence_proxy_async_smem();
+    }
+    if (warp == 1) {
+        tmem_alloc(sbase + L::kMisc, kTmemCols);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (kUseTma && lane == 0) {
+            tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_k); tma_prefetch_desc(&tm_v);
+            if (load_i8) { tma_prefetch_desc(&tm_q8); tma_prefetch_desc(&tm_k8); }
+        }
+        const std::size_t q_off = static_cast<std::size_t>(head) * p.M * p.d;
+        const std::size_t kv_off = static_cast<std::size_t>(head) * p.N * p.d;
+        if (kUseTma) {
+            if (lane == 0) {
+                mbar_arrive_expect_tx(bar(kBarQFull), kAtoms * kAtomBytes + (load_i8 ? kAtomBytes : 0u));
+                for (int a = 0; a < kAtoms; ++a) {
+                    tma_load_3d(sbase + L::kQ + a * kAtomBytes, &tm_q, bar(kBarQFull), a * 64, qt * kTileRows, head);
+                }
+                if (load_i8) tma_load_3d(sbase + L::kQ8, &tm_q8, bar(kBarQFull), 0, qt * kTileRows, head);
+            }
+        } else {
+            manual_tile_f16(smem + L::kQ, p.q + q_off, qt * kTileRows, p.M, p.d, kAtoms, lane);
+            if (load_i8) manual_tile_i8(smem + L::kQ8, p.q8 + q_off, qt * kTileRows, p.M, p.d, lane);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarQFull));
+        }
+        int issued_k = 0, issued_v = 0;
+        for (int j = 0; j < nblk; ++j) {
+            const BlockRoute r = block_route(p, head, qt, j, lane);
+            const int ks = j % kKStages;
+            if (!wait_bar(bar(kBarKEmpty + ks), ((j / kKStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
+            const uint32_t k_dst = sbase + L::kK + ks * L::kKStride;
+            const uint32_t k8_dst = sbase + L::kK8 + ks * kAtomBytes;
+            if (kUseTma) {
+                if (lane == 0) {
+                    const uint32_t bytes = (r.need_f16 ? kAtoms * kAtomBytes : 0u) + (r.need_i8 ? kAtomBytes : 0u);
+                    mbar_arrive_expect_tx(bar(kBarKFull + ks), bytes);
+                    if (r.need_f16) {
+                        for (int a = 0; a < kAtoms; ++a) {
+                            tma_load_3d(k_dst + a * kAtomBytes, &tm_k, bar(kBarKFull + ks), a * 64, j * kTileKeys, head);
+                        }
+                    }
+                    if (r.need_i8) tma_load_3d(k8_dst, &tm_k8, bar(kBarKFull + ks), 0, j * kTileKeys, head);
+                }
+            } else {
+                if (r.need_f16) manual_tile_f16(smem + L::kK + ks * L::kKStride, p.k + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
+                if (r.need_i8) manual_tile_i8(smem + L::kK8 + ks * kAtomBytes, p.k8 + kv_off, j * kTileKeys, p.N, p.d, lane);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kBarKFull + ks));
+            }
+            issued_k = j + 1;
+            const int vs = j % kVStages;
+            if (!wait_bar(bar(kBarVEmpty + vs), ((j / kVStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
+            const uint32_t v_dst = sbase + L::kV + vs * L::kVStride;
+            if (kUseTma) {
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(bar(kBarVFull + vs), kAtoms * kAtomBytes);
+                    for (int a = 0; a < kAtoms; ++a) {
+                        tma_load_3d(v_dst + a * kAtomBytes, &tm_v, bar(kBarVFull + vs), a * 64, j * kTileKeys, head);
+                    }
+                }
+            } else {
+                manual_tile_f16(smem + L::kV + vs * L::kVStride, p.v + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kBarVFull + vs));
+            }
+            issued_v = j + 1;
+        }
+        // Drain: the newest load into each stage must have landed before the
+        // CTA may exit (normally long complete; matters only after an abort).
+        if (kUseTma) {
+            wait_bar(bar(kBarQFull), 0, abort_flag, kStatusDrain);
+            for (int j = max(0, issued_k - kKStages); j < issued_k; ++j) {
+                wait_bar(bar(kBarKFull + j % kKStages), (j / kKStages) & 1, abort_flag, kStatusDrain);
+            }
+            for (int j = max(0, issued_v - kVStages); j < issued_v; ++j) {
+                wait_bar(bar(kBarVFull + j % kVStages), (j / kVStages) & 1, abort_flag, kStatusDrain);
+            }
+        }
+    } else if (warp == 1) {
+        // ----------------------------------------------------------------- MMA
+        const uint32_t q_addr = sbase + L::kQ, q8_addr = sbase + L::kQ8;
+        const uint32_t pv_idesc = idesc_f16_f32(kTileRows, p.pv_n, true);
+        bool ok = wait_bar(bar(kBarQFull), 0, abort_flag, kStatusMma);
+        auto issue_pv = [&](int i) -> bool {
+            if (!wait_bar(bar(kBarPFull + (i & 1)), (i >> 1) & 1, abort_flag, kStatusMma)) return false;
+            const int vs = i % kVStages;
+            if (!wait_bar(bar(kBarVFull + vs), (i / kVStages) & 1, abort_flag, kStatusMma)) return false;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t v_addr = sbase + L::kV + vs * L::kVStride;
+                const uint32_t p_tmem = tmem + ((i & 1) ? kColS1 : 0u);
+                #pragma unroll
+                for (int s = 0; s < kTileKeys / 16; ++s) {
+                    // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
+                    // 8-key groups 1024 B apart; each K step covers 16 keys.
+                    const uint64_t b_desc = smem_desc_sw128(v_addr + s * 2048, kAtomBytes, 1024);
+                    mma_f16_ts(tmem + kColO, p_tmem + s * 8, b_desc, pv_idesc, (i > 0 || s > 0) ? 1u : 0u);
+                }
+                tc_commit(bar(kBarVEmpty + vs));
+                tc_commit(bar(kBarPvDone));
+            }
+            __syncwarp();
+            return true;
+        };
+        for (int j = 0; ok && j < nblk; ++j) {
+            const BlockRoute r = block_route(p, head, qt, j, lane);
+            const int ks = j % kKStages;
+            if (!wait_bar(bar(kBarKFull + ks), (j / kKStages) & 1, abort_flag, kStatusMma)) { ok = false; break; }
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t s_tmem = tmem + ((j & 1) ? kColS1 : 0u);
+                const uint32_t k_addr = sbase + L::kK + ks * L::kKStride;
+                const uint32_t k8_addr = sbase + L::kK8 + ks * kAtomBytes;
+                int kt = 0;
+                while (kt < r.ktiles) {
+                    int end = kt + 1;
+                    while (end < r.ktiles && r.pat[end] == r.pat[kt]) ++end;
+                    const uint32_t i8_rows = r.pat[kt] & r.valid_rows;
+                    const uint32_t f16_rows = ~r.pat[kt] & r.valid_rows & 0xffu;
+                    const int n = 32 * (end - kt);
+                    if (f16_rows) {
+                        uint32_t off[4];
+                        lane_mask(i8_rows, off);
+                        const uint32_t idesc = idesc_f16_f32(kTileRows, n, false);
+                        for (int s = 0; s < p.f16_ksteps; ++s) {
+                            const uint32_t koff = (s >> 2) * kAtomBytes + (s & 3) * 32;
+                            const uint64_t a_desc = smem_desc_sw128(q_addr + koff, 16, 1024);
+                            const uint64_t b_desc = smem_desc_sw128(k_addr + koff + kt * 4096, 16, 1024);
+                            mma_f16_ss(s_tmem + 32 * kt, a_desc, b_desc, idesc, off, s > 0 ? 1u : 0u);
+                        }
+                    }
+                    if (i8_rows) {
+                        uint32_t off[4];
+                        lane_mask(f16_rows, off);
+                        const uint32_t idesc = idesc_s8_s32(kTileRows, n);
+                        for (int s = 0; s < p.i8_ksteps; ++s) {
+                            const uint64_t a_desc = smem_desc_sw128(q8_addr + s * 32, 16, 1024);
+                            const uint64_t b_desc = smem_desc_sw128(k8_addr + s * 32 + kt * 4096, 16, 1024);
+                            mma_i8_ss(s_tmem + 32 * kt, a_desc, b_desc, idesc, off, s > 0 ? 1u : 0u);
+                        }
+                    }
+                    kt = end;
+                }
+                tc_commit(bar(kBarKEmpty + ks));
+                tc_commit(bar(kBarSFull + (j & 1)));
+            }
+            __syncwarp();
+            if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+        }
+        if (ok && nblk > 0) issue_pv(nblk - 1);
+        // Drain every MMA this thread issued before TMEM can be released.
+        if (lane == 0) tc_commit(bar(kBarDrain));
+        __syncwarp();
+        wait_bar(bar(kBarDrain), 0, abort_flag, kStatusDrain);
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------- softmax
+        const int row = static_cast<int>(threadIdx.x) - 128;          // 0..127 = TMEM lane
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const int q_row = qt * kTileRows + row;
+        const bool row_valid = q_row < p.M;
+        const int q16 = qt * (kTileRows / 16) + row / 16;
+        const bool q16_valid = q16 < p.q16_tiles;
+        const float q_scale = p.routed ? __half2float(p.q_scales[head * p.q_scale_blocks + qt]) : 0.0f;
+        const __half* k_scales = p.routed ? p.k_scales + static_cast<std::size_t>(head) * p.k_scale_blocks : nullptr;
+        float m_run = -INFINITY;   // running max (log2 units), possibly stale by < 2^8
+        float l_run = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nblk; ++j) {
+            const int b = j & 1;
+            // Per-key-tile routing bit and score multiplier for this row.
+            uint32_t bits = 0;
+            float mult[4];
+            #pragma unroll
+            for (int kt = 0; kt < 4; ++kt) {
+                const int gkt = 4 * j + kt;
+                const bool bit = p.routed && q16_valid && gkt < p.k32_tiles && route_bit(p, head, q16, gkt);
+                bits |= static_cast<uint32_t>(bit) << kt;
+                mult[kt] = p.scale_log2;
+                if (bit) mult[kt] = q_scale * __half2float(k_scales[gkt >> 1]) * p.scale_log2;
+            }
+            if (kTrace && p.decoded_bits && row % 16 == 0 && q16_valid) {
+                #pragma unroll
+                for (int kt = 0; kt < 4; ++kt) {
+                    const int gkt = 4 * j + kt;
+                    if (gkt < p.k32_tiles) {
+                        p.decoded_bits[(static_cast<std::size_t>(head) * p.q16_tiles + q16) * p.k32_tiles + gkt] =
+                            static_cast<uint8_t>((bits >> kt) & 1u);
+                    }
+                }
+            }
+            if (!wait_bar(bar(kBarSFull + b), (j >> 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t x[128];
+            {
+                uint32_t (&x0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[0]);
+                uint32_t (&x1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[32]);
+                uint32_t (&x2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[64]);
+                uint32_t (&x3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[96]);
+                const uint32_t s_addr = tmem + lane_base + (b ? kColS1 : 0u);
+                tmem_ld32(s_addr + 0, x0);
+                tmem_ld32(s_addr + 32, x1);
+                tmem_ld32(s_addr + 64, x2);
+                tmem_ld32(s_addr + 96, x3);
+                tc_wait_ld();
+            }
+            const int key0 = j * kTileKeys;
+            if (kTrace && p.score_dots && row_valid) {
+                #pragma unroll
+                for (int kt = 0; kt < 4; ++kt) {
+                    if ((bits >> kt) & 1u) {
+                        #pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int key = key0 + kt * 32 + i;
+                            if (key < p.N) {
+                                p.score_dots[(static_cast<std::size_t>(head) * p.M + q_row) * p.N + key] =
+                                    static_cast<int32_t>(x[kt * 32 + i]);
+                            }
+                        }
+                    }
+                }
+            }
+            // Dequantise (INT8 tiles: exact s32 -> f32 via the 1.5 * 2^23 bias,
+            // |dot| <= 127^2 * 128 < 2^22) and scale into log2 units.
+            float s[128];
+            #pragma unroll
+            for (int kt = 0; kt < 4; ++kt) {
+                const bool is_i8 = (bits >> kt) & 1u;
+                const uint32_t bias = is_i8 ? 0x4B400000u : 0u;
+                const float sub = is_i8 ? 12582912.0f : 0.0f;
+                #pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    s[kt * 32 + i] = (__uint_as_float(x[kt * 32 + i] + bias) - sub) * mult[kt];
+                }
+            }
+            const bool edge = key0 + kTileKeys > p.N || (p.causal && key0 + kTileKeys > q_row);
+            if (edge) {
+                const int limit = p.causal ? min(p.N, q_row + 1) : p.N;
+                #pragma unroll
+                for (int i = 0; i < 128; ++i) {
+                    if (key0 + i >= limit) s[i] = -INFINITY;
+                }
+            }
+            float block_max = s[0];
+            #pragma unroll
+            for (int i = 1; i < 128; ++i) block_max = fmaxf(block_max, s[i]);
+            float alpha = 1.0f;
+            if (block_max > m_run + kRescaleThreshold) {   // also true on the first block
+                const float m_new = fmaxf(m_run, block_max);
+                alpha = ex2(m_run - m_new);       // 0 on the first block
+                m_run = m_new;
+            }
+            const float m_use = m_run == -INFINITY ? 0.0f : m_run;
+            float sum = 0.0f;
+            uint32_t packed[64];
+            #pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                const float p0 = ex2(s[2 * i] - m_use);
+                const float p1 = ex2(s[2 * i + 1] - m_use);
+                sum += p0 + p1;
+                packed[i] = pack_half2(p0, p1);
+            }
+            l_run = l_run * alpha + sum;
+            {
+                const uint32_t p_addr = tmem + lane_base + (b ? kColS1 : 0u);
+                tmem_st32(p_addr, *reinterpret_cast<const uint32_t(*)[32]>(&packed[0]));
+                tmem_st32(p_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(&packed[32]));
+            }
+            if (j > 0) {
+                // O may only be rescaled once PV of the previous block landed.
+                if (!wait_bar(bar(kBarPvDone), (j - 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+                    const uint32_t o_addr = tmem + lane_base + kColO;
+                    for (int c = 0; c < p.pv_n; c += 32) {
+                        uint32_t ov[32];
+                        tmem_ld32(o_addr + c, ov);
+                        tc_wait_ld();
+                        #pragma unroll
+                        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                        tmem_st32(o_addr + c, ov);
+                    }
+                }
+            }
+            tc_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(kBarPFull + b));
+        }
+        if (ok && nblk > 0 && wait_bar(bar(kBarPvDone), (nblk - 1) & 1, abort_flag, kStatusSoftmax)) {
+            tc_fence_after();
+            const float inv_l = 1.0f / l_run;
+            const uint32_t o_addr = tmem + lane_base + kColO;
+            float* out = p.o + (static_cast<std::size_t>(head) * p.M + q_row) * p.d;
+            for (int c = 0; c < p.pv_n; c += 32) {
+                uint32_t ov[32];
+                tmem_ld32(o_addr + c, ov);
+                tc_wait_ld();
+                if (row_valid) {
+                    if (p.o_vec) {
+                        #pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            if (c + i < p.d) {
+                                reinterpret_cast<float4*>(out + c + i)[0] = make_float4(
+                                    __uint_as_float(ov[i]) * inv_l, __uint_as_float(ov[i + 1]) * inv_l,
+                                    __uint_as_float(ov[i + 2]) * inv_l, __uint_as_float(ov[i + 3]) * inv_l);
+                            }
+                        }
+                    } else {
+                        #pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (c + i < p.d) out[c + i] = __uint_as_float(ov[i]) * inv_l;
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------- host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult status;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &status) == cudaSuccess &&
+            status == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+        }
+    });
+    return fn;
+}
+
+// 3-D map over [heads][rows][d] with a 128-byte-swizzled {box_x, 128, 1} box.
+bool encode_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int elem_bytes,
+                int heads, int rows, int d, int box_x) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(heads)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * elem_bytes,
+                                   static_cast<cuuint64_t>(rows) * d * elem_bytes};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_x), 128u, 1u};
+    const cuuint32_t elem_strides[3] = {1u, 1u, 1u};
+    return fn(map, type, 3, const_cast<void*>(base), dims, strides, box, elem_strides,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int kAtoms, bool kUseTma, bool kTrace>
+cudaError_t launch_variant(const CUtensorMap* maps, const Params& p, unsigned grid, cudaStream_t stream) {
+    auto kernel = tilemix_attention_kernel<kAtoms, kUseTma, kTrace>;
+    const int smem = static_cast<int>(SmemLayout<kAtoms>::kBytes);
+    // The opt-in attribute is per device; set it on every launch path that has
+    // not seen the current device yet.
+    static int configured[64] = {0};
+    int device = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status != cudaSuccess) return status;
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+    if (!configured[device]) {
+        status = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (status != cudaSuccess) return status;
+        configured[device] = 1;
+    }
+    kernel<<<grid, kAttnThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], p);
+    return cudaGetLastError();
+}
+
+bool aligned16(const void* ptr) {
+    return (reinterpret_cast<std::uintptr_t>(ptr) & 15u) == 0;
+}
+
+}  // namespace
+
+std::size_t attention_smem_bytes(int d) {
+    if (d <= 0 || d > kMaxHeadDim) return 0;
+    return d <= 64 ? SmemLayout<1>::kBytes : SmemLayout<2>::kBytes;
+}
+
+cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) {
+    Params p{};
+    p.q = prob.q; p.k = prob.k; p.v = prob.v;
+    p.q8 = prob.q8; p.k8 = prob.k8;
+    p.q_scales = prob.q_scales; p.k_scales = prob.k_scales;
+    p.o = prob.o;
+    p.words = prob.words;
+    p.decoded_bits = prob.decoded_bits;
+    p.score_dots = prob.score_dots;
+    p.heads = prob.heads; p.M = prob.M; p.N = prob.N; p.d = prob.d;
+    p.q_tiles = (prob.M - 1) / kTileRows + 1;
+    p.kv_blocks = (prob.N - 1) / kTileKeys + 1;
+    p.q16_tiles = (prob.M - 1) / 16 + 1;
+    p.k32_tiles = (prob.N - 1) / 32 + 1;
+    // Group sizes beyond the key-tile count behave like one group per row.
+    p.group = std::min(prob.key_tiles_per_group, p.k32_tiles);
+    const long long groups = (p.k32_tiles - 1) / prob.key_tiles_per_group + 1;
+    p.words_per_row = static_cast<int>((groups - 1) / 64 + 1);
+    p.words_per_head = static_cast<long long>(p.q16_tiles) * p.words_per_row;
+    p.q_scale_blocks = (prob.M - 1) / kQuantQRows + 1;
+    p.k_scale_blocks = (prob.N - 1) / kQuantKRows + 1;
+    p.scale_log2 = prob.score_scale * kLog2e;
+    p.causal = prob.causal ? 1 : 0;
+    p.routed = prob.words != nullptr ? 1 : 0;
+    p.f16_ksteps = (prob.d + 15) / 16;
+    p.i8_ksteps = (prob.d + 31) / 32;
+    p.pv_n = (prob.d + 15) / 16 * 16;
+    p.o_vec = (prob.d % 4 == 0 && aligned16(prob.o)) ? 1 : 0;
+
+    const long long grid = static_cast<long long>(p.q_tiles) * p.heads;
+    if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    const int atoms = prob.d <= 64 ? 1 : 2;
+    const bool trace = prob.decoded_bits != nullptr || prob.score_dots != nullptr;
+
+    CUtensorMap maps[5];
+    std::memset(maps, 0, sizeof(maps));
+    bool tma = prob.d % 16 == 0 && aligned16(prob.q) && aligned16(prob.k) && aligned16(prob.v) &&
+               (!p.routed || (aligned16(prob.q8) && aligned16(prob.k8)));
+    if (tma) {
+        tma = encode_map(&maps[0], prob.q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.heads, p.M, p.d, 64) &&
+              encode_map(&maps[1], prob.k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.heads, p.N, p.d, 64) &&
+              encode_map(&maps[2], prob.v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.heads, p.N, p.d, 64);
+        if (tma && p.routed) {
+            tma = encode_map(&maps[3], prob.q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.heads, p.M, p.d, 128) &&
+                  encode_map(&maps[4], prob.k8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.heads, p.N, p.d, 128);
+        }
+    }
+    const unsigned g = static_cast<unsigned>(grid);
+    if (atoms == 1) {
+        if (tma) return trace ? launch_variant<1, true, true>(maps, p, g, stream)
+                              : launch_variant<1, true, false>(maps, p, g, stream);
+        return trace ? launch_variant<1, false, true>(maps, p, g, stream)
+                     : launch_variant<1, false, false>(maps, p, g, stream);
+    }
+    if (tma) return trace ? launch_variant<2, true, true>(maps, p, g, stream)
+                          : launch_variant<2, true, false>(maps, p, g, stream);
+    return trace ? launch_variant<2, false, true>(maps, p, g, stream)
+                 : launch_variant<2, false, false>(maps, p, g, stream);
+}
+
+cudaError_t read_and_clear_status(unsigned int* status) {
+    unsigned int zero = 0;
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) return err;
+    err = cudaMemcpyFromSymbol(status, g_tilemix_status, sizeof(unsigned int));
+    if (err != cudaSuccess) return err;
+    return cudaMemcpyToSymbol(g_tilemix_status, &zero, sizeof(unsigned int));
+}
+
+}  // namespace tilemix

@@ -1,0 +1,49 @@
+// Internal launcher declarations shared by the kernels and the API layer.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace tilemix {
+
+constexpr int kQuantQRows = 128;   // reference include/attention_fused.h:13
+constexpr int kQuantKRows = 64;    // reference include/attention_fused.h:14
+constexpr int kMaxHeadDim = 128;
+
+// Quantize Q [heads, M, d] (128-row blocks) and K [heads, N, d] (64-row
+// blocks) in one launch. Arguments are assumed validated.
+cudaError_t launch_quantize(const __half* Q, const __half* K, std::int8_t* Q8, std::int8_t* K8,
+                            __half* q_scales, __half* k_scales, int heads, int M, int N, int d,
+                            cudaStream_t stream);
+
+struct AttentionProblem {
+    const __half* q;
+    const __half* k;
+    const __half* v;
+    const std::int8_t* q8;       // null when not routed
+    const std::int8_t* k8;
+    const __half* q_scales;
+    const __half* k_scales;
+    float* o;
+    const std::uint64_t* words;  // null = all FP16
+    std::uint8_t* decoded_bits;  // optional trace
+    std::int32_t* score_dots;    // optional trace
+    int heads, M, N, d;
+    int key_tiles_per_group;
+    float score_scale;
+    bool causal;
+};
+
+// Shared memory the attention kernel requests for head dim d.
+std::size_t attention_smem_bytes(int d);
+
+// Launch the fused attention kernel (arguments assumed validated, d <= 128).
+cudaError_t launch_attention(const AttentionProblem& problem, cudaStream_t stream);
+
+// Read and clear the device watchdog word of the current device.
+cudaError_t read_and_clear_status(unsigned int* status);
+
+}  // namespace tilemix

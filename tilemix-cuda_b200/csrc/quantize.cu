@@ -1,0 +1,135 @@
+// Stage 1: per-block symmetric INT8 quantizer for Q (128-row blocks) and K
+// (64-row blocks), one launch for both tensors and all heads.
+//
+// Semantics follow the reference (src/tilemix.cu:16-49,
+// src/tests/reference_tilemix.h:16-41) bit for bit:
+//   absmax  = max |x| in fp32 over the block (NaN never replaces the max)
+//   scale   = __fdiv_rn(absmax, 127)            (fp32, stored as fp16 RN)
+//   q       = clamp(rz(x/scale + copysign(0.5, x/scale)), -127, 127),
+//             x/scale by __fdiv_rn, 0 when scale == 0
+// i.e. round half AWAY from zero on the fp32 quotient.
+//
+// B200 design: the block is read from HBM once. Each CTA owns one block
+// (<= 128 x 128 fp16 = 32 KB), its 256 threads hold the block in registers
+// (up to 8 x 16-byte loads each), reduce the absmax with warp shuffles, then
+// quantize from registers and write 8-byte stores: 3 bytes of HBM traffic per
+// element, the algorithmic minimum. Unaligned pointers or d % 8 != 0 take a
+// scalar two-pass path (the second pass hits L2).
+#include "kernels.cuh"
+
+#include <cstdint>
+
+namespace tilemix {
+namespace {
+
+constexpr int kQuantThreads = 256;
+constexpr int kMaxChunksPerThread = 8;   // 128 rows x 128 d / 8 halves / 256 threads
+
+__device__ __forceinline__ std::int8_t quantize_one(float x, float scale) {
+    const float normalized = scale > 0.0f ? __fdiv_rn(x, scale) : 0.0f;
+    const int rounded = __float2int_rz(__fadd_rn(normalized, copysignf(0.5f, normalized)));
+    return static_cast<std::int8_t>(max(-127, min(127, rounded)));
+}
+
+__device__ __forceinline__ float block_max(float value, float* scratch) {
+    #pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) {
+        value = fmaxf(value, __shfl_xor_sync(0xffffffffu, value, offset));
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) scratch[warp] = value;
+    __syncthreads();
+    float total = 0.0f;
+    #pragma unroll
+    for (int w = 0; w < kQuantThreads / 32; ++w) total = fmaxf(total, scratch[w]);
+    return total;
+}
+
+struct QuantTensor {
+    const __half* x;
+    std::int8_t* values;
+    __half* scales;
+    int rows;
+    int block_rows;
+    int blocks;      // per head
+    bool vector_ok;  // 16-byte aligned input, 8-byte aligned output, d % 8 == 0
+};
+
+__global__ void __launch_bounds__(kQuantThreads)
+quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
+    __shared__ float scratch[kQuantThreads / 32];
+    const int q_ctas = heads * qt.blocks;
+    const bool is_q = static_cast<int>(blockIdx.x) < q_ctas;
+    const QuantTensor& t = is_q ? qt : kt;
+    const int cta = is_q ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) - q_ctas;
+    const int head = cta / t.blocks, block = cta % t.blocks;
+    const int first_row = block * t.block_rows;
+    const int rows_here = min(t.block_rows, t.rows - first_row);
+    const std::size_t base = (static_cast<std::size_t>(head) * t.rows + first_row) * d;
+    const int count = rows_here * d;
+    const __half* src = t.x + base;
+    std::int8_t* dst = t.values + base;
+
+    if (t.vector_ok) {
+        uint4 chunk[kMaxChunksPerThread];
+        const int chunks = count >> 3;
+        float local = 0.0f;
+        #pragma unroll
+        for (int i = 0; i < kMaxChunksPerThread; ++i) {
+            const int c = threadIdx.x + i * kQuantThreads;
+            if (c < chunks) {
+                chunk[i] = __ldg(reinterpret_cast<const uint4*>(src) + c);
+                const __half* h = reinterpret_cast<const __half*>(&chunk[i]);
+                #pragma unroll
+                for (int e = 0; e < 8; ++e) local = fmaxf(local, fabsf(__half2float(h[e])));
+            }
+        }
+        const float scale = __fdiv_rn(block_max(local, scratch), 127.0f);
+        if (threadIdx.x == 0) t.scales[static_cast<std::size_t>(head) * t.blocks + block] = __float2half_rn(scale);
+        #pragma unroll
+        for (int i = 0; i < kMaxChunksPerThread; ++i) {
+            const int c = threadIdx.x + i * kQuantThreads;
+            if (c < chunks) {
+                const __half* h = reinterpret_cast<const __half*>(&chunk[i]);
+                uint32_t packed[2] = {0u, 0u};
+                #pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const uint32_t byte = static_cast<uint8_t>(quantize_one(__half2float(h[e]), scale));
+                    packed[e >> 2] |= byte << ((e & 3) * 8);
+                }
+                reinterpret_cast<uint2*>(dst)[c] = make_uint2(packed[0], packed[1]);
+            }
+        }
+    } else {
+        float local = 0.0f;
+        for (int i = threadIdx.x; i < count; i += kQuantThreads) {
+            local = fmaxf(local, fabsf(__half2float(src[i])));
+        }
+        const float scale = __fdiv_rn(block_max(local, scratch), 127.0f);
+        if (threadIdx.x == 0) t.scales[static_cast<std::size_t>(head) * t.blocks + block] = __float2half_rn(scale);
+        for (int i = threadIdx.x; i < count; i += kQuantThreads) {
+            dst[i] = quantize_one(__half2float(src[i]), scale);
+        }
+    }
+}
+
+bool aligned(const void* p, std::uintptr_t bytes) {
+    return (reinterpret_cast<std::uintptr_t>(p) & (bytes - 1)) == 0;
+}
+
+}  // namespace
+
+cudaError_t launch_quantize(const __half* Q, const __half* K, std::int8_t* Q8, std::int8_t* K8,
+                            __half* q_scales, __half* k_scales, int heads, int M, int N, int d,
+                            cudaStream_t stream) {
+    QuantTensor qt{Q, Q8, q_scales, M, kQuantQRows, (M - 1) / kQuantQRows + 1,
+                   d % 8 == 0 && aligned(Q, 16) && aligned(Q8, 8)};
+    QuantTensor kt{K, K8, k_scales, N, kQuantKRows, (N - 1) / kQuantKRows + 1,
+                   d % 8 == 0 && aligned(K, 16) && aligned(K8, 8)};
+    const long long ctas = static_cast<long long>(heads) * (qt.blocks + kt.blocks);
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    quantize_blocks_kernel<<<static_cast<unsigned>(ctas), kQuantThreads, 0, stream>>>(qt, kt, heads, d);
+    return cudaGetLastError();
+}
+
+}  // namespace tilemix
