@@ -1,0 +1,406 @@
+#!/usr/bin/env python
+"""TileMix B200 benchmark: effective attention TFLOP/s on a BASELINE config.
+
+One step = the TileMix hot path over one batch: stage-1 INT8 quantization of Q
+and K, then the fused routed attention kernel (quantize_tilemix_qk_batched +
+tilemix_attention_batched through the C-ABI). Default workload: BASELINE
+config 3 (B8 H32 S4096 D128, causal, 1% x20 outlier channels, INT8 routing
+Bernoulli(0.75) over 64x64 tiles) -- the configuration the north-star target is
+quoted on.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--p P]
+  python bench.py --impl reference ...   (the reference's CPU path, rank 0)
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own full batch
+of heads (independent (b, h) shards, no collective on the data path; weak
+scaling); NCCL is used only for the start/stop barriers and the max-over-ranks
+reduction of the device times. Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for p in (REPO, REPO / "tilemix-cuda_b200"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+METRIC = "effective attention TFLOP/s and % of mix-weighted tensor peak, 1/2/4/8 B200"
+L2_BYTES = 126 * 2**20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="tilemix", choices=["tilemix", "reference"])
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--p", type=float, default=None, help="override the INT8 routing fraction")
+    ap.add_argument("--cpu-seconds", type=float, default=6.0,
+                    help="target CPU time of one reference-arm sample")
+    return ap.parse_args()
+
+
+def measured_peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"bf16_tflops": d["bf16_tflops"], "bf16_tflops_sustained": d["bf16_tflops_sustained"],
+                "hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def profiled_traffic() -> dict:
+    """ncu DRAM bytes per unit of work for the attention kernel, from the
+    committed summary under profiles/ (null when absent)."""
+    out = {}
+    for path in sorted((REPO / "profiles").glob("*.txt")):
+        for line in path.read_text().splitlines():
+            if line.startswith("bench_traffic_per_head "):
+                _, cfg, value = line.split()
+                out[cfg] = float(value)
+    return out
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+        self.gpu = gpu_index
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        power = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(power) if power else None}
+
+
+# -------------------------------------------------------------- distributed
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        if args.impl == "tilemix":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                    device_id=torch.device(f"cuda:{local}"))
+        else:
+            dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    elif args.impl == "tilemix":
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def reduce_max(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------- CPU baseline
+def cpu_reference_sample(w_host: dict, cfg: dict, target_s: float) -> dict:
+    """Time the reference's own CPU path (oracle/_ref: reference_quantize and
+    reference_tilemix from src/tests/reference_tilemix.h; a causal row runs the
+    reference on its key prefix) on a bounded sample of the workload -- whole
+    heads, all rows, on all host cores -- and extrapolate to the full batch.
+    Falls back to the C restatement (kind "port") without the reference build."""
+    import numpy as np
+    import oracle
+    if not oracle.ORACLE_SO.exists() or (not oracle.ref_available() and Path("/root/reference").exists()):
+        oracle.build()
+    kind = "reference" if oracle.ref_available() else "port"
+    use_ref = kind == "reference"
+    q, k, v = w_host["q"], w_host["k"], w_host["v"]
+    avail, S, D = q.shape
+    H = cfg["B"] * cfg["H"]            # heads of the whole workload
+    causal = cfg["causal"]
+    wc = w_host["words"].size // avail
+    rows = np.arange(S, dtype=np.int32)
+    keys = np.minimum(rows + 1, S) if causal else np.full(S, S)
+    head_flops = float((4.0 * keys * D).sum())
+    threads = oracle.ref_lib().ref_max_threads() if use_ref else oracle.max_threads()
+
+    def run_head(h):
+        sl = slice(h, h + 1)
+        t = time.perf_counter()
+        if use_ref:
+            q8, qs = oracle.ref_quantize(q[h], 128)
+            k8, ks = oracle.ref_quantize(k[h], 64)
+        else:
+            q8, qs = oracle.quantize(q[h], 128)
+            k8, ks = oracle.quantize(k[h], 64)
+        t_quant = time.perf_counter() - t
+        bits = oracle.decode_routing(w_host["words"][h * wc:(h + 1) * wc], S, S, 2)[None]
+        t = time.perf_counter()
+        oracle.tilemix_sampled(q[sl], k[sl], v[sl], q8[None], k8[None], qs[None], ks[None], bits,
+                               np.array([0], np.int32), rows, 1.0 / math.sqrt(D), causal,
+                               use_reference=use_ref)
+        return t_quant, time.perf_counter() - t
+
+    tq, ta = run_head(0)
+    n_heads = int(max(1, min(avail, math.ceil(target_s / max(ta + tq, 1e-6)))))
+    for h in range(1, n_heads):
+        a, b = run_head(h)
+        tq += a
+        ta += b
+    rate = n_heads * head_flops / ta                       # attention FLOP/s on all threads
+    quant_per_head = tq / n_heads                          # seconds, one thread
+    from tilemix_b200 import workloads
+    f_eff = workloads.effective_flops(cfg)
+    step_s = f_eff / rate + quant_per_head * H / threads   # quantization parallel over heads
+    return {"value": f_eff / step_s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+            "sample": (f"{n_heads} whole head(s) of S={S} through reference_quantize (1 thread) and "
+                       f"reference_tilemix ({'causal: each row on its key prefix, ' if causal else ''}"
+                       f"{threads} OpenMP threads over rows; {ta + tq:.1f} s), extrapolated to all {H} heads"),
+            "step_seconds": step_s}
+
+
+# ------------------------------------------------------------------ our arm
+def run_tilemix(args, rank, world, local):
+    import numpy as np
+    import torch
+    import tilemix_b200 as tm
+    from tilemix_b200 import workloads
+
+    cfg0 = workloads.config(args.config, p=args.p)
+    w = workloads.make_inputs(args.config, p=args.p, seed=cfg0["seed"] + 1000 * rank, device="cuda")
+    cfg, H, S, D = w["cfg"], w["heads"], w["S"], w["D"]
+    q, k, v = w["q"], w["k"], w["v"]
+    words = w["words"].cuda()
+    q8 = torch.empty_like(q, dtype=torch.int8)
+    k8 = torch.empty_like(k, dtype=torch.int8)
+    qs = torch.empty((H, (S - 1) // 128 + 1), dtype=torch.float16, device="cuda")
+    ks = torch.empty((H, (S - 1) // 64 + 1), dtype=torch.float16, device="cuda")
+    out = torch.empty((H, S, D), dtype=torch.float32, device="cuda")
+    routing = tm.TileMixRouting(words, words.numel(), 2)
+    quantized = tm.TileMixQuantized(q8, k8, qs, ks)
+    stream = torch.cuda.current_stream()
+    f_eff = workloads.effective_flops(cfg)
+    f_real = workloads.realised_int8_fraction(w["mask"], cfg["causal"])
+
+    def quantize():
+        tm.check(tm.quantize_tilemix_qk_batched(q, k, q8, k8, qs, ks, H, S, S, D, stream), "quantize")
+
+    def attend():
+        tm.check(tm.tilemix_attention_batched(q, k, v, out, H, S, S, D, w["score_scale"], cfg["causal"],
+                                              stream, routing, quantized), "attention")
+
+    for _ in range(args.warmup):
+        quantize(); attend()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)                     # let the sampler attach before the timed region
+    n = args.steps
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * n + 2)]
+    barrier(world)
+    torch.cuda.synchronize()
+    ev[0].record(stream)
+    for i in range(n):
+        quantize()
+        ev[1 + 2 * i].record(stream)
+        attend()
+        ev[2 + 2 * i].record(stream)
+    ev[-1].record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    total_ms = ev[0].elapsed_time(ev[-1])
+    attn_ms = [ev[1 + 2 * i].elapsed_time(ev[2 + 2 * i]) for i in range(n)]
+    quant_ms = [(ev[0] if i == 0 else ev[2 * i]).elapsed_time(ev[1 + 2 * i]) for i in range(n)]
+    err, status = tm.read_and_clear_status()
+    tm.check(err, "status")
+    if status:
+        raise SystemExit(f"kernel watchdog reported status {status:#x}")
+    step_ms = reduce_max(total_ms / n, world)
+    attn_avg = reduce_max(sum(attn_ms) / n, world)
+    quant_avg = reduce_max(sum(quant_ms) / n, world)
+
+    # end to end through the C-ABI with host buffers: H2D inputs + mask, both
+    # kernels, D2H of the fp32 output, every step.
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hwords = w["words"].pin_memory()
+    hout = torch.empty((H, S, D), dtype=torch.float32).pin_memory()
+    e2e_steps = max(1, min(n, 5))
+
+    def e2e_step():
+        q.copy_(hq, non_blocking=True); k.copy_(hk, non_blocking=True); v.copy_(hv, non_blocking=True)
+        words.copy_(hwords, non_blocking=True)
+        quantize(); attend()
+        hout.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = reduce_max(e0.elapsed_time(e1) / e2e_steps, world)
+    h2d = 3 * q.numel() * 2 + words.numel() * 8
+    d2h = out.numel() * 4
+
+    cpu = None
+    if rank == 0 and world == 1:
+        nh = min(H, 32)
+        host = {"q": hq.numpy()[:nh].copy(), "k": hk.numpy()[:nh].copy(), "v": hv.numpy()[:nh].copy(),
+                "words": w["words"].numpy()[: nh * (w["words"].numel() // H)].copy()}
+        c = cpu_reference_sample(host, cfg, args.cpu_seconds)
+        cpu = {key: c[key] for key in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank != 0:
+        return
+    peaks = measured_peaks()
+    achieved = f_eff / (attn_avg * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"]
+    traffic_per_head = profiled_traffic().get(args.config)
+    value = world * f_eff / (step_ms * 1e-3) / 1e12
+    p_mix = workloads.mix_peak(f_eff, f_real) / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": n, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16+i8 (f32 accumulate)", "data": "synthetic",
+        "config": {"workload": f"{args.config}: B{cfg['B']} H{cfg['H']} S{S} D{D}"
+                               f"{' causal' if cfg['causal'] else ''}, INT8 routing p={cfg['p']}"
+                               f"{', x20 outlier channels' if cfg['outliers'] else ''}",
+                   "B": cfg["B"], "H": cfg["H"], "S": S, "D": D, "causal": cfg["causal"],
+                   "int8_fraction_requested": cfg["p"], "int8_fraction_realised": round(f_real, 4),
+                   "per_gpu_heads": H, "parallelism": f"batch x head shards, {world} rank(s), no collective",
+                   "l2": f"inputs {3 * q.numel() * 2 / 2**20:.0f} MiB > L2 {L2_BYTES / 2**20:.0f} MiB; no flush"},
+        "pct_of_mix_peak": round(100 * value / world / p_mix, 2),
+        "mix_peak_tflops": round(p_mix, 1),
+        "attention_ms": round(attn_avg, 4), "quantize_ms": round(quant_avg, 4),
+        "quantize_gbs": round(3 * 2 * H * S * D / (quant_avg * 1e-3) / 1e9, 1),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4),
+                     "peak_source": f"{peaks['source']} bf16 dense (burst), MEASURED_PEAKS.json",
+                     "traffic": None if traffic_per_head is None else traffic_per_head * H,
+                     "kernel": "tilemix_attention_kernel",
+                     "work": "F_eff = 4*B*H*S^2*D/2 (causal) algorithmic FLOPs per launch"},
+        "e2e": {"value": round(world * f_eff / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
+        "clocks": clk,
+        "gpu_launches": 2 * n,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    """The reference's own CPU implementation of the path on the host cores,
+    on this arm's config/metric; each step is a bounded sample."""
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    from tilemix_b200 import workloads
+    cfg = workloads.config(args.config, p=args.p)
+    # a few heads of the workload, drawn with the CPU generator (the sample uses whole heads)
+    w = workloads.make_inputs(args.config, p=args.p, batch=1, heads=min(cfg["H"], 16))
+    host = {"q": w["q"].numpy(), "k": w["k"].numpy(), "v": w["v"].numpy(), "words": w["words"].numpy()}
+    values = []
+    last = None
+    for i in range(args.warmup + args.steps):
+        last = cpu_reference_sample(host, cfg, args.cpu_seconds)
+        if i >= args.warmup:
+            values.append(last["step_seconds"])
+    step_s = statistics.median(values)
+    f_eff = workloads.effective_flops(cfg)
+    value = f_eff / step_s / 1e12
+    cpu = {"value": round(value, 6), "unit": "TFLOP/s", "cores": last["cores"], "kind": last["kind"],
+           "sample": last["sample"]}
+    line = {"metric": METRIC, "impl": "reference", "value": round(value, 6), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(step_s * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64 (reference CPU emulation)", "data": "synthetic",
+            "config": {"workload": f"{args.config}: B{cfg['B']} H{cfg['H']} S{cfg['S']} D{cfg['D']}"
+                                   f"{' causal' if cfg['causal'] else ''}, INT8 routing p={cfg['p']}",
+                       "B": cfg["B"], "H": cfg["H"], "S": cfg["S"], "D": cfg["D"], "causal": cfg["causal"]},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_tilemix(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

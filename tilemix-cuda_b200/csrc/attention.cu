@@ -11,7 +11,8 @@
 //   * softmax over all keys < N (plus the causal extension key <= query);
 //   * O = (sum_k p_k v_k) / (sum_k p_k) in fp32 (src/tilemix.cu:213-219).
 // Differences that stay inside the parity tolerance: exp2 with log2(e) folded
-// into the score scale, P rounded to fp16 for the PV tensor-core MMA, and the
+// into the score scale, P carried as two fp16 terms (hi + lo) through two PV
+// tensor-core MMAs (~2^-22 relative, vs the reference's fp32 P), and the
 // running max only moved when it grows by more than 2^8 (the final result is
 // unchanged mathematically; P stays <= 256, well inside fp16).
 //
@@ -22,7 +23,7 @@
 //   warp 1     MMA issuer (one lane) + TMEM owner (512 columns:
 //              S0 | S1 | O): QK^T of block j into S[j%2], PV of block j-1
 //   warps 4-7  softmax: thread t owns query row t = TMEM lane t; dequantises,
-//              masks, exponentiates, writes P (fp16) over S in TMEM, rescales
+//              masks, exponentiates, writes P (fp16 hi + lo) over S in TMEM, rescales
 //              O in TMEM when the max moves, final normalise + store
 //
 // Routing inside a 128-row tile: for each 32-key tile the 8 routing bits of
@@ -379,8 +380,10 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 for (int s = 0; s < kTileKeys / 16; ++s) {
                     // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
                     // 8-key groups 1024 B apart; each K step covers 16 keys.
+                    // P_hi (columns [0,64)) and P_lo ([64,128)) share the V step.
                     const uint64_t b_desc = smem_desc_sw128(v_addr + s * 2048, kAtomBytes, 1024);
                     mma_f16_ts(tmem + kColO, p_tmem + s * 8, b_desc, pv_idesc, (i > 0 || s > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem + kColO, p_tmem + 64 + s * 8, b_desc, pv_idesc, 1u);
                 }
                 tc_commit(bar(kBarVEmpty + vs));
                 tc_commit(bar(kBarPvDone));
@@ -536,21 +539,32 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 m_run = m_new;
             }
             const float m_use = m_run == -INFINITY ? 0.0f : m_run;
+            // P = P_hi + P_lo, both fp16: P_hi is p rounded to fp16, P_lo the
+            // (exactly computed) residual rounded to fp16. The two PV MMAs make
+            // the product accurate to ~2^-22 relative instead of fp16's 2^-11,
+            // which the parity tolerance needs once V has large-magnitude
+            // (outlier) channels. P_hi goes to columns [0,64) of the S buffer,
+            // P_lo to [64,128); the scores were already read into registers.
             float sum = 0.0f;
-            uint32_t packed[64];
+            const uint32_t p_addr = tmem + lane_base + (b ? kColS1 : 0u);
             #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                const float p0 = ex2(s[2 * i] - m_use);
-                const float p1 = ex2(s[2 * i + 1] - m_use);
-                sum += p0 + p1;
-                packed[i] = pack_half2(p0, p1);
+            for (int c = 0; c < 4; ++c) {
+                uint32_t hi[16], lo[16];
+                #pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int e = c * 32 + 2 * i;
+                    const float p0 = ex2(s[e] - m_use);
+                    const float p1 = ex2(s[e + 1] - m_use);
+                    sum += p0 + p1;
+                    const __half2 h = __floats2half2_rn(p0, p1);
+                    const float2 back = __half22float2(h);
+                    hi[i] = *reinterpret_cast<const uint32_t*>(&h);
+                    lo[i] = pack_half2(p0 - back.x, p1 - back.y);
+                }
+                tmem_st16(p_addr + 16 * c, hi);
+                tmem_st16(p_addr + 64 + 16 * c, lo);
             }
             l_run = l_run * alpha + sum;
-            {
-                const uint32_t p_addr = tmem + lane_base + (b ? kColS1 : 0u);
-                tmem_st32(p_addr, *reinterpret_cast<const uint32_t(*)[32]>(&packed[0]));
-                tmem_st32(p_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(&packed[32]));
-            }
             if (j > 0) {
                 // O may only be rescaled once PV of the previous block landed.
                 if (!wait_bar(bar(kBarPvDone), (j - 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }

@@ -54,29 +54,33 @@ def pack_block_mask64(block_mask: np.ndarray, S_q: int, S_k: int) -> np.ndarray:
 
 
 def make_inputs(name: str, p: float | None = None, batch: int | None = None,
-                heads: int | None = None, seq: int | None = None, seed: int | None = None) -> dict:
-    """Host (CPU) tensors for a config. Returns q, k, v fp16 [B*H, S, D], the
-    64x64 block mask [B*H, S/64, S/64] uint8, routing words, score scale and
-    the config dict. Overrides shrink a config for tests (same generator)."""
+                heads: int | None = None, seq: int | None = None, seed: int | None = None,
+                device: str = "cpu") -> dict:
+    """Tensors for a config. Returns q, k, v fp16 [B*H, S, D], the 64x64 block
+    mask [B*H, S/64, S/64] uint8, routing words (host), score scale and the
+    config dict. Overrides shrink a config for tests (same generator order).
+    device="cuda" draws with a CUDA generator instead (same distributions,
+    different numbers; used by the benchmark to avoid minutes of host RNG)."""
     cfg = config(name, p=p, B=batch, H=heads, S=seq, seed=seed)
     B, H, S, D = cfg["B"], cfg["H"], cfg["S"], cfg["D"]
-    g = torch.Generator(device="cpu").manual_seed(cfg["seed"])
-    q = torch.randn((B, H, S, D), generator=g) * cfg["sigma"]
-    k = torch.randn((B, H, S, D), generator=g) * cfg["sigma"]
-    v = torch.randn((B, H, S, D), generator=g) * cfg["sigma"]
+    g = torch.Generator(device=device).manual_seed(cfg["seed"])
+    q = torch.randn((B, H, S, D), generator=g, device=device) * cfg["sigma"]
+    k = torch.randn((B, H, S, D), generator=g, device=device) * cfg["sigma"]
+    v = torch.randn((B, H, S, D), generator=g, device=device) * cfg["sigma"]
     if cfg["outliers"]:
         n_out = math.ceil(0.01 * D)
-        channels = torch.randperm(D, generator=g)[:n_out]
+        channels = torch.randperm(D, generator=g, device=device)[:n_out]
         for t in (q, k, v):
             t[..., channels] *= 20.0
     qb = (S + 63) // 64
-    mask = (torch.rand((B, H, qb, qb), generator=g) < cfg["p"]).to(torch.uint8)
+    mask = (torch.rand((B, H, qb, qb), generator=g, device=device) < cfg["p"]).to(torch.uint8)
     if cfg["band"]:
-        idx = torch.arange(qb)
+        idx = torch.arange(qb, device=device)
         band = (idx[None, :] == idx[:, None]) | (idx[None, :] == idx[:, None] - 1)
         mask[..., band] = 0
     q16, k16, v16 = (t.to(torch.float16).reshape(B * H, S, D).contiguous() for t in (q, k, v))
-    mask = mask.reshape(B * H, qb, qb).contiguous()
+    del q, k, v
+    mask = mask.reshape(B * H, qb, qb).contiguous().cpu()
     words = torch.from_numpy(pack_block_mask64(mask.numpy(), S, S))
     return dict(q=q16, k=k16, v=v16, mask=mask, words=words, score_scale=1.0 / math.sqrt(D),
                 cfg=cfg, heads=B * H, S=S, D=D)
