@@ -95,7 +95,7 @@ def test_c3_full_sampled_rows_and_properties():
     oc = tm.attention(q, k, vc, q8=q8, k8=k8, q_scales=qs, k_scales=ks, words=w["words"].cuda(),
                       score_scale=w["score_scale"], causal=True)
     torch.cuda.synchronize()
-    assert (oc - 0.75).abs().max().item() <= 1e-5
+    assert (oc - 0.75).abs().max().item() <= 1e-4   # fp32 accumulation over <= 4096 keys
 
 
 @pytest.mark.parametrize("p", [0.0, 0.5, 1.0])

@@ -16,15 +16,21 @@
 // running max only moved when it grows by more than 2^8 (the final result is
 // unchanged mathematically; P stays <= 256, well inside fp16).
 //
-// CTA = one 128-row query tile of one head; 256 threads, warp-specialised:
-//   warp 0     producer: TMA (or, for head dims TMA cannot address, plain
-//              loads) of Q, Q8 once and K/K8, V per 128-key block into
-//              2-stage rings, 128-byte swizzled K-major tiles
-//   warp 1     MMA issuer (one lane) + TMEM owner (512 columns:
-//              S0 | S1 | O): QK^T of block j into S[j%2], PV of block j-1
-//   warps 4-7  softmax: thread t owns query row t = TMEM lane t; dequantises,
-//              masks, exponentiates, writes P (fp16 hi + lo) over S in TMEM, rescales
-//              O in TMEM when the max moves, final normalise + store
+// CTA = two 128-row query tiles (256 rows) of one head, 384 threads:
+//   warps 0-3  softmax of query tile 0   (thread t = query row t = TMEM lane t)
+//   warps 4-7  softmax of query tile 1
+//   warp 8     MMA issuer (one lane) + TMEM owner: S0 | S1 | O0 | O1
+//              (4 x 128 columns); QK^T of tile t into S_t, PV into O_t
+//   warp 9     producer: TMA (or, for head dims TMA cannot address, plain
+//              loads) of Q/Q8 for both tiles once, then per 128-key block
+//              K/K8 (one stage) and V (two stages), 128-byte swizzled
+//   warps 10-11 idle (complete the third warpgroup for the register split)
+// The MMA warp issues, per key block j:  PV(0, j-1), QK(0, j), PV(1, j-1),
+// QK(1, j).  Each tile's chain is QK -> softmax -> PV -> next QK, and the two
+// tiles' chains interleave on the tensor pipe, so one tile's softmax runs while
+// the other tile's MMAs execute ("ping-pong"). P (fp16 hi in columns [0,64),
+// lo in [64,128)) overwrites S in TMEM and is consumed by TMEM-A MMAs; the
+// in-order tensor pipe guarantees PV(t, j-1) reads P before QK(t, j) rewrites S.
 //
 // Routing inside a 128-row tile: for each 32-key tile the 8 routing bits of
 // the tile's 16-row query tiles form a pattern. Runs of key tiles with equal
@@ -57,18 +63,29 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kTileRows = 128;
-constexpr int kTileKeys = 128;
-constexpr int kKStages = 2;
+constexpr int kTileRows = 128;               // rows per query tile (tcgen05 M)
+constexpr int kTilesPerCta = 2;
+constexpr int kCtaRows = kTileRows * kTilesPerCta;
+constexpr int kTileKeys = 128;               // keys per block
 constexpr int kVStages = 2;
-constexpr int kAttnThreads = 256;
+constexpr int kMmaWarp = 8;
+constexpr int kProducerWarp = 9;
+constexpr int kAttnThreads = 384;             // warps 10-11 only take part in the register split
+// Register split (setmaxnreg): the two softmax warpgroups hold a 128-wide
+// score row each and grow to kSoftmaxRegs; the MMA/producer warpgroup shrinks
+// to kOtherRegs. The launch must provide at least the split's total, which the
+// host checks against the compiled register count before every first launch.
+constexpr int kSoftmaxRegs = 200;
+constexpr int kOtherRegs = 96;
+constexpr int kSplitRegs = 256 * kSoftmaxRegs + 128 * kOtherRegs;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS1 = 128;           // S0 at column 0, S1 at 128
-constexpr uint32_t kColO = 256;
 constexpr uint32_t kAtomBytes = 128 * 128;   // 128 rows x 128 bytes
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescaleThreshold = 8.0f;    // log2 units: rescale only if max grows by > 2^8
+constexpr float kRescaleLog2 = 8.0f;         // rescale only when the max grows by > 2^8
+
+__device__ __forceinline__ uint32_t col_s(int t) { return static_cast<uint32_t>(t) * 128u; }
+__device__ __forceinline__ uint32_t col_o(int t) { return 256u + static_cast<uint32_t>(t) * 128u; }
 
 // Watchdog codes (bit positions say which wait gave up).
 enum : unsigned int {
@@ -80,25 +97,22 @@ enum : unsigned int {
 
 template <int kAtoms>
 struct SmemLayout {
-    static constexpr uint32_t kQ = 0;
-    static constexpr uint32_t kQ8 = kQ + kAtoms * kAtomBytes;
-    static constexpr uint32_t kK = kQ8 + kAtomBytes;
-    static constexpr uint32_t kKStride = kAtoms * kAtomBytes;
-    static constexpr uint32_t kK8 = kK + kKStages * kKStride;
-    static constexpr uint32_t kV = kK8 + kKStages * kAtomBytes;
-    static constexpr uint32_t kVStride = kAtoms * kAtomBytes;
-    static constexpr uint32_t kBars = kV + kVStages * kVStride;
-    // barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2],
-    //           s_full[2], p_full[2], pv_done, drain
-    static constexpr uint32_t kNumBars = 15;
-    static constexpr uint32_t kMisc = kBars + kNumBars * 8;   // tmem base, abort flag
+    static constexpr uint32_t kTileF16 = kAtoms * kAtomBytes;
+    static constexpr uint32_t kQ = 0;                                   // [2 tiles] fp16
+    static constexpr uint32_t kQ8 = kQ + kTilesPerCta * kTileF16;       // [2 tiles] int8
+    static constexpr uint32_t kK = kQ8 + kTilesPerCta * kAtomBytes;     // one stage
+    static constexpr uint32_t kK8 = kK + kTileF16;
+    static constexpr uint32_t kV = kK8 + kAtomBytes;                    // [2 stages]
+    static constexpr uint32_t kBars = kV + kVStages * kTileF16;
+    static constexpr uint32_t kNumBars = 16;
+    static constexpr uint32_t kMisc = kBars + kNumBars * 8;            // tmem base, abort flag
     static constexpr uint32_t kEnd = kMisc + 16;
-    static constexpr uint32_t kBytes = kEnd + 1024;           // + alignment slack
+    static constexpr uint32_t kBytes = kEnd + 1024;                     // + alignment slack
 };
 
 enum Bar : int {
-    kBarQFull = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7,
-    kBarSFull = 9, kBarPFull = 11, kBarPvDone = 13, kBarDrain = 14,
+    kBarQFull = 0, kBarKFull = 1, kBarKEmpty = 2, kBarVFull = 3, kBarVEmpty = 5,
+    kBarSFull = 7, kBarPFull = 9, kBarPvDone = 11, kBarDrain = 13,
 };
 
 struct Params {
@@ -114,7 +128,7 @@ struct Params {
     std::uint8_t* decoded_bits;
     std::int32_t* score_dots;
     int heads, M, N, d;
-    int q_tiles, kv_blocks, q16_tiles, k32_tiles;
+    int cta_tiles, kv_blocks, q16_tiles, k32_tiles;
     int group;
     int words_per_row;
     long long words_per_head;
@@ -124,6 +138,7 @@ struct Params {
     int routed;
     int f16_ksteps, i8_ksteps, pv_n;
     int o_vec;
+    int head_group;      // heads scheduled together (their K/V stay L2-resident)
 };
 
 // Bounded wait, called by all 32 lanes of a warp; returns a warp-uniform
@@ -146,16 +161,6 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
     return __all_sync(0xffffffffu, ok);
 }
 
-// Routing summary of KV block j for this CTA's 8 query tiles, computed by a
-// whole warp: pat[kt] bit t = INT8 for (query tile t, key tile kt).
-struct BlockRoute {
-    uint32_t pat[4];
-    uint32_t valid_rows;   // bit t = query tile t exists (t < 8)
-    int ktiles;            // key tiles of this block that exist (1..4)
-    bool need_f16;
-    bool need_i8;
-};
-
 __device__ __forceinline__ bool route_bit(const Params& p, int head, int q16, int gkt) {
     const long long group = gkt / p.group;
     const std::uint64_t word = __ldg(p.words + head * p.words_per_head
@@ -163,12 +168,24 @@ __device__ __forceinline__ bool route_bit(const Params& p, int head, int q16, in
     return ((word >> (group % 64)) & 1ull) != 0;
 }
 
-__device__ __forceinline__ BlockRoute block_route(const Params& p, int head, int qt, int j,
-                                                  uint32_t lane) {
+// Routing summary of key block j for the CTA's 16 query tiles (8 per
+// 128-row tile), computed by a whole warp. pat[kt] bit l = INT8 for query
+// tile l and key tile kt; valid bit l = query tile l exists and its 128-row
+// tile processes block j. need_f16/need_i8 say which K operands block j needs.
+struct BlockRoute {
+    uint32_t pat[4];
+    uint32_t valid;
+    int ktiles;
+    bool need_f16;
+    bool need_i8;
+};
+
+__device__ __forceinline__ BlockRoute block_route(const Params& p, int head, int cta_tile, int j,
+                                                  const int (&nblk)[2], uint32_t lane) {
     BlockRoute r;
-    const int q16 = qt * (kTileRows / 16) + static_cast<int>(lane);
-    const bool q_valid = lane < 8 && q16 < p.q16_tiles;
-    r.valid_rows = __ballot_sync(0xffffffffu, q_valid);
+    const int q16 = cta_tile * (kCtaRows / 16) + static_cast<int>(lane);
+    const bool q_valid = lane < 16 && q16 < p.q16_tiles && j < nblk[(lane >> 3) & 1];
+    r.valid = __ballot_sync(0xffffffffu, q_valid);
     r.ktiles = min(4, p.k32_tiles - 4 * j);
     r.need_f16 = false;
     r.need_i8 = false;
@@ -178,7 +195,7 @@ __device__ __forceinline__ BlockRoute block_route(const Params& p, int head, int
         r.pat[kt] = __ballot_sync(0xffffffffu, bit);
         if (kt < r.ktiles) {
             r.need_i8 |= r.pat[kt] != 0;
-            r.need_f16 |= (~r.pat[kt] & r.valid_rows) != 0;
+            r.need_f16 |= (~r.pat[kt] & r.valid) != 0;
         }
     }
     return r;
@@ -238,6 +255,12 @@ __device__ void manual_tile_i8(uint8_t* dst, const std::int8_t* src, int row0, i
     }
 }
 
+// Exact s32 -> f32 for |x| < 2^22 (|dot| <= 127^2 * 128 < 2^22): add the
+// 1.5 * 2^23 bias in the integer domain, subtract it in fp32.
+__device__ __forceinline__ float s32_to_f32(uint32_t x) {
+    return __uint_as_float(x + 0x4B400000u) - 12582912.0f;
+}
+
 template <int kAtoms, bool kUseTma, bool kTrace>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -259,24 +282,41 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31u;
 
-    // Work item: heaviest (last) query tiles first so causal tails are short.
-    const int qt = p.q_tiles - 1 - static_cast<int>(blockIdx.x) / p.heads;
-    const int head = static_cast<int>(blockIdx.x) % p.heads;
-    const int nblk = p.causal ? min(p.kv_blocks, qt + 1) : p.kv_blocks;
+    // Work item: heads are scheduled in groups (their K/V stay in L2 while the
+    // group runs); inside a group the heaviest (last) 256-row tiles go first.
+    const int bid = static_cast<int>(blockIdx.x);
+    const int per_group = p.head_group * p.cta_tiles;
+    const int group0 = (bid / per_group) * p.head_group;
+    const int group_heads = min(p.head_group, p.heads - group0);
+    const int in_group = bid - (bid / per_group) * per_group;
+    const int cta_tile = p.cta_tiles - 1 - in_group / group_heads;
+    const int head = group0 + in_group % group_heads;
+    int nblk[2];
+    #pragma unroll
+    for (int t = 0; t < kTilesPerCta; ++t) {
+        const int qt = cta_tile * kTilesPerCta + t;             // 128-row tile index
+        const bool exists = qt * kTileRows < p.M;
+        nblk[t] = !exists ? 0 : (p.causal ? min(p.kv_blocks, qt + 1) : p.kv_blocks);
+    }
+    const int nblk_max = max(nblk[0], nblk[1]);
     const int load_i8 = p.routed;
 
     if (threadIdx.x == 0) {
         mbar_init(bar(kBarQFull), 1);
-        for (int s = 0; s < kKStages; ++s) { mbar_init(bar(kBarKFull + s), 1); mbar_init(bar(kBarKEmpty + s), 1); }
+        mbar_init(bar(kBarKFull), 1);
+        mbar_init(bar(kBarKEmpty), 1);
         for (int s = 0; s < kVStages; ++s) { mbar_init(bar(kBarVFull + s), 1); mbar_init(bar(kBarVEmpty + s), 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(bar(kBarSFull + b), 1); mbar_init(bar(kBarPFull + b), 128); }
-        mbar_init(bar(kBarPvDone), 1);
+        for (int t = 0; t < kTilesPerCta; ++t) {
+            mbar_init(bar(kBarSFull + t), 1);
+            mbar_init(bar(kBarPFull + t), 128);
+            mbar_init(bar(kBarPvDone + t), 1);
+        }
         mbar_init(bar(kBarDrain), 1);
         *abort_flag = 0;
         mbar_init_fence();
         fence_proxy_async_smem();
     }
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tmem_alloc(sbase + L::kMisc, kTmemCols);
         tmem_relinquish();
         tc_fence_before();
@@ -285,7 +325,8 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
+    if (warp >= 8) reg_dealloc<kOtherRegs>();   // warpgroup 2: MMA, producer, two idle warps
+    if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer
         if (kUseTma && lane == 0) {
             tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_k); tma_prefetch_desc(&tm_v);
@@ -295,177 +336,211 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         const std::size_t kv_off = static_cast<std::size_t>(head) * p.N * p.d;
         if (kUseTma) {
             if (lane == 0) {
-                mbar_arrive_expect_tx(bar(kBarQFull), kAtoms * kAtomBytes + (load_i8 ? kAtomBytes : 0u));
-                for (int a = 0; a < kAtoms; ++a) {
-                    tma_load_3d(sbase + L::kQ + a * kAtomBytes, &tm_q, bar(kBarQFull), a * 64, qt * kTileRows, head);
+                uint32_t bytes = 0;
+                for (int t = 0; t < kTilesPerCta; ++t) {
+                    if (nblk[t] > 0) bytes += L::kTileF16 + (load_i8 ? kAtomBytes : 0u);
                 }
-                if (load_i8) tma_load_3d(sbase + L::kQ8, &tm_q8, bar(kBarQFull), 0, qt * kTileRows, head);
+                mbar_arrive_expect_tx(bar(kBarQFull), bytes);
+                for (int t = 0; t < kTilesPerCta; ++t) {
+                    if (nblk[t] == 0) continue;
+                    const int row0 = (cta_tile * kTilesPerCta + t) * kTileRows;
+                    for (int a = 0; a < kAtoms; ++a) {
+                        tma_load_3d(sbase + L::kQ + t * L::kTileF16 + a * kAtomBytes, &tm_q, bar(kBarQFull),
+                                    a * 64, row0, head);
+                    }
+                    if (load_i8) tma_load_3d(sbase + L::kQ8 + t * kAtomBytes, &tm_q8, bar(kBarQFull), 0, row0, head);
+                }
             }
         } else {
-            manual_tile_f16(smem + L::kQ, p.q + q_off, qt * kTileRows, p.M, p.d, kAtoms, lane);
-            if (load_i8) manual_tile_i8(smem + L::kQ8, p.q8 + q_off, qt * kTileRows, p.M, p.d, lane);
+            for (int t = 0; t < kTilesPerCta; ++t) {
+                if (nblk[t] == 0) continue;
+                const int row0 = (cta_tile * kTilesPerCta + t) * kTileRows;
+                manual_tile_f16(smem + L::kQ + t * L::kTileF16, p.q + q_off, row0, p.M, p.d, kAtoms, lane);
+                if (load_i8) manual_tile_i8(smem + L::kQ8 + t * kAtomBytes, p.q8 + q_off, row0, p.M, p.d, lane);
+            }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarQFull));
         }
-        int issued_k = 0, issued_v = 0;
-        for (int j = 0; j < nblk; ++j) {
-            const BlockRoute r = block_route(p, head, qt, j, lane);
-            const int ks = j % kKStages;
-            if (!wait_bar(bar(kBarKEmpty + ks), ((j / kKStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
-            const uint32_t k_dst = sbase + L::kK + ks * L::kKStride;
-            const uint32_t k8_dst = sbase + L::kK8 + ks * kAtomBytes;
+        int k_issued = 0, v_issued = 0;
+        for (int j = 0; j < nblk_max; ++j) {
+            const BlockRoute r = block_route(p, head, cta_tile, j, nblk, lane);
+            if (!wait_bar(bar(kBarKEmpty), (j & 1) ^ 1, abort_flag, kStatusProducer)) break;
             if (kUseTma) {
                 if (lane == 0) {
-                    const uint32_t bytes = (r.need_f16 ? kAtoms * kAtomBytes : 0u) + (r.need_i8 ? kAtomBytes : 0u);
-                    mbar_arrive_expect_tx(bar(kBarKFull + ks), bytes);
+                    const uint32_t bytes = (r.need_f16 ? L::kTileF16 : 0u) + (r.need_i8 ? kAtomBytes : 0u);
+                    mbar_arrive_expect_tx(bar(kBarKFull), bytes);
                     if (r.need_f16) {
                         for (int a = 0; a < kAtoms; ++a) {
-                            tma_load_3d(k_dst + a * kAtomBytes, &tm_k, bar(kBarKFull + ks), a * 64, j * kTileKeys, head);
+                            tma_load_3d(sbase + L::kK + a * kAtomBytes, &tm_k, bar(kBarKFull), a * 64, j * kTileKeys, head);
                         }
                     }
-                    if (r.need_i8) tma_load_3d(k8_dst, &tm_k8, bar(kBarKFull + ks), 0, j * kTileKeys, head);
+                    if (r.need_i8) tma_load_3d(sbase + L::kK8, &tm_k8, bar(kBarKFull), 0, j * kTileKeys, head);
                 }
             } else {
-                if (r.need_f16) manual_tile_f16(smem + L::kK + ks * L::kKStride, p.k + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
-                if (r.need_i8) manual_tile_i8(smem + L::kK8 + ks * kAtomBytes, p.k8 + kv_off, j * kTileKeys, p.N, p.d, lane);
+                if (r.need_f16) manual_tile_f16(smem + L::kK, p.k + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
+                if (r.need_i8) manual_tile_i8(smem + L::kK8, p.k8 + kv_off, j * kTileKeys, p.N, p.d, lane);
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar(kBarKFull + ks));
+                if (lane == 0) mbar_arrive(bar(kBarKFull));
             }
-            issued_k = j + 1;
+            k_issued = j + 1;
             const int vs = j % kVStages;
             if (!wait_bar(bar(kBarVEmpty + vs), ((j / kVStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
-            const uint32_t v_dst = sbase + L::kV + vs * L::kVStride;
+            const uint32_t v_dst = sbase + L::kV + vs * L::kTileF16;
             if (kUseTma) {
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(bar(kBarVFull + vs), kAtoms * kAtomBytes);
+                    mbar_arrive_expect_tx(bar(kBarVFull + vs), L::kTileF16);
                     for (int a = 0; a < kAtoms; ++a) {
                         tma_load_3d(v_dst + a * kAtomBytes, &tm_v, bar(kBarVFull + vs), a * 64, j * kTileKeys, head);
                     }
                 }
             } else {
-                manual_tile_f16(smem + L::kV + vs * L::kVStride, p.v + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
+                manual_tile_f16(smem + L::kV + vs * L::kTileF16, p.v + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kBarVFull + vs));
             }
-            issued_v = j + 1;
+            v_issued = j + 1;
         }
-        // Drain: the newest load into each stage must have landed before the
+        // Drain: the newest load into each buffer must have landed before the
         // CTA may exit (normally long complete; matters only after an abort).
         if (kUseTma) {
             wait_bar(bar(kBarQFull), 0, abort_flag, kStatusDrain);
-            for (int j = max(0, issued_k - kKStages); j < issued_k; ++j) {
-                wait_bar(bar(kBarKFull + j % kKStages), (j / kKStages) & 1, abort_flag, kStatusDrain);
-            }
-            for (int j = max(0, issued_v - kVStages); j < issued_v; ++j) {
+            if (k_issued > 0) wait_bar(bar(kBarKFull), (k_issued - 1) & 1, abort_flag, kStatusDrain);
+            for (int j = max(0, v_issued - kVStages); j < v_issued; ++j) {
                 wait_bar(bar(kBarVFull + j % kVStages), (j / kVStages) & 1, abort_flag, kStatusDrain);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == kMmaWarp) {
         // ----------------------------------------------------------------- MMA
-        const uint32_t q_addr = sbase + L::kQ, q8_addr = sbase + L::kQ8;
         const uint32_t pv_idesc = idesc_f16_f32(kTileRows, p.pv_n, true);
         bool ok = wait_bar(bar(kBarQFull), 0, abort_flag, kStatusMma);
-        auto issue_pv = [&](int i) -> bool {
-            if (!wait_bar(bar(kBarPFull + (i & 1)), (i >> 1) & 1, abort_flag, kStatusMma)) return false;
+        // PV of tile t for block i: O_t (+)= (P_hi + P_lo) V_i.
+        auto issue_pv = [&](int t, int i) -> bool {
+            if (!wait_bar(bar(kBarPFull + t), i & 1, abort_flag, kStatusMma)) return false;
             const int vs = i % kVStages;
             if (!wait_bar(bar(kBarVFull + vs), (i / kVStages) & 1, abort_flag, kStatusMma)) return false;
             tc_fence_after();
             if (lane == 0) {
-                const uint32_t v_addr = sbase + L::kV + vs * L::kVStride;
-                const uint32_t p_tmem = tmem + ((i & 1) ? kColS1 : 0u);
+                const uint32_t v_addr = sbase + L::kV + vs * L::kTileF16;
+                const uint32_t p_tmem = tmem + col_s(t);
                 #pragma unroll
                 for (int s = 0; s < kTileKeys / 16; ++s) {
                     // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
                     // 8-key groups 1024 B apart; each K step covers 16 keys.
-                    // P_hi (columns [0,64)) and P_lo ([64,128)) share the V step.
                     const uint64_t b_desc = smem_desc_sw128(v_addr + s * 2048, kAtomBytes, 1024);
-                    mma_f16_ts(tmem + kColO, p_tmem + s * 8, b_desc, pv_idesc, (i > 0 || s > 0) ? 1u : 0u);
-                    mma_f16_ts(tmem + kColO, p_tmem + 64 + s * 8, b_desc, pv_idesc, 1u);
+                    mma_f16_ts(tmem + col_o(t), p_tmem + s * 8, b_desc, pv_idesc, (i > 0 || s > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem + col_o(t), p_tmem + 64 + s * 8, b_desc, pv_idesc, 1u);
                 }
-                tc_commit(bar(kBarVEmpty + vs));
-                tc_commit(bar(kBarPvDone));
+                tc_commit(bar(kBarPvDone + t));
             }
             __syncwarp();
             return true;
         };
-        for (int j = 0; ok && j < nblk; ++j) {
-            const BlockRoute r = block_route(p, head, qt, j, lane);
-            const int ks = j % kKStages;
-            if (!wait_bar(bar(kBarKFull + ks), (j / kKStages) & 1, abort_flag, kStatusMma)) { ok = false; break; }
-            tc_fence_after();
-            if (lane == 0) {
-                const uint32_t s_tmem = tmem + ((j & 1) ? kColS1 : 0u);
-                const uint32_t k_addr = sbase + L::kK + ks * L::kKStride;
-                const uint32_t k8_addr = sbase + L::kK8 + ks * kAtomBytes;
-                int kt = 0;
-                while (kt < r.ktiles) {
-                    int end = kt + 1;
-                    while (end < r.ktiles && r.pat[end] == r.pat[kt]) ++end;
-                    const uint32_t i8_rows = r.pat[kt] & r.valid_rows;
-                    const uint32_t f16_rows = ~r.pat[kt] & r.valid_rows & 0xffu;
-                    const int n = 32 * (end - kt);
-                    if (f16_rows) {
-                        uint32_t off[4];
-                        lane_mask(i8_rows, off);
-                        const uint32_t idesc = idesc_f16_f32(kTileRows, n, false);
-                        for (int s = 0; s < p.f16_ksteps; ++s) {
-                            const uint32_t koff = (s >> 2) * kAtomBytes + (s & 3) * 32;
-                            const uint64_t a_desc = smem_desc_sw128(q_addr + koff, 16, 1024);
-                            const uint64_t b_desc = smem_desc_sw128(k_addr + koff + kt * 4096, 16, 1024);
-                            mma_f16_ss(s_tmem + 32 * kt, a_desc, b_desc, idesc, off, s > 0 ? 1u : 0u);
-                        }
+        // QK^T of tile t for block j into S_t.
+        auto issue_qk = [&](int t, const BlockRoute& r) {
+            const uint32_t s_tmem = tmem + col_s(t);
+            const uint32_t q_addr = sbase + L::kQ + t * L::kTileF16;
+            const uint32_t q8_addr = sbase + L::kQ8 + t * kAtomBytes;
+            const uint32_t k_addr = sbase + L::kK, k8_addr = sbase + L::kK8;
+            const uint32_t valid = (r.valid >> (8 * t)) & 0xffu;
+            int kt = 0;
+            while (kt < r.ktiles) {
+                const uint32_t pat = (r.pat[kt] >> (8 * t)) & 0xffu;
+                int end = kt + 1;
+                while (end < r.ktiles && ((r.pat[end] >> (8 * t)) & 0xffu) == pat) ++end;
+                const uint32_t i8_rows = pat & valid;
+                const uint32_t f16_rows = ~pat & valid;
+                const int n = 32 * (end - kt);
+                if (f16_rows) {
+                    uint32_t off[4];
+                    lane_mask(i8_rows, off);
+                    const uint32_t idesc = idesc_f16_f32(kTileRows, n, false);
+                    for (int s = 0; s < p.f16_ksteps; ++s) {
+                        const uint32_t koff = (s >> 2) * kAtomBytes + (s & 3) * 32;
+                        const uint64_t a_desc = smem_desc_sw128(q_addr + koff, 16, 1024);
+                        const uint64_t b_desc = smem_desc_sw128(k_addr + koff + kt * 4096, 16, 1024);
+                        mma_f16_ss(s_tmem + 32 * kt, a_desc, b_desc, idesc, off, s > 0 ? 1u : 0u);
                     }
-                    if (i8_rows) {
-                        uint32_t off[4];
-                        lane_mask(f16_rows, off);
-                        const uint32_t idesc = idesc_s8_s32(kTileRows, n);
-                        for (int s = 0; s < p.i8_ksteps; ++s) {
-                            const uint64_t a_desc = smem_desc_sw128(q8_addr + s * 32, 16, 1024);
-                            const uint64_t b_desc = smem_desc_sw128(k8_addr + s * 32 + kt * 4096, 16, 1024);
-                            mma_i8_ss(s_tmem + 32 * kt, a_desc, b_desc, idesc, off, s > 0 ? 1u : 0u);
-                        }
-                    }
-                    kt = end;
                 }
-                tc_commit(bar(kBarKEmpty + ks));
-                tc_commit(bar(kBarSFull + (j & 1)));
+                if (i8_rows) {
+                    uint32_t off[4];
+                    lane_mask(f16_rows, off);
+                    const uint32_t idesc = idesc_s8_s32(kTileRows, n);
+                    for (int s = 0; s < p.i8_ksteps; ++s) {
+                        const uint64_t a_desc = smem_desc_sw128(q8_addr + s * 32, 16, 1024);
+                        const uint64_t b_desc = smem_desc_sw128(k8_addr + s * 32 + kt * 4096, 16, 1024);
+                        mma_i8_ss(s_tmem + 32 * kt, a_desc, b_desc, idesc, off, s > 0 ? 1u : 0u);
+                    }
+                }
+                kt = end;
+            }
+            tc_commit(bar(kBarSFull + t));
+        };
+        for (int j = 0; ok && j < nblk_max; ++j) {
+            const BlockRoute r = block_route(p, head, cta_tile, j, nblk, lane);
+            if (!wait_bar(bar(kBarKFull), j & 1, abort_flag, kStatusMma)) { ok = false; break; }
+            tc_fence_after();
+            for (int t = 0; t < kTilesPerCta && ok; ++t) {
+                if (j > 0 && j - 1 < nblk[t] && !issue_pv(t, j - 1)) { ok = false; break; }
+                if (j < nblk[t]) {
+                    if (lane == 0) issue_qk(t, r);
+                    __syncwarp();
+                }
+            }
+            if (!ok) break;
+            if (lane == 0) {
+                tc_commit(bar(kBarKEmpty));
+                if (j > 0) tc_commit(bar(kBarVEmpty + (j - 1) % kVStages));
             }
             __syncwarp();
-            if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
         }
-        if (ok && nblk > 0) issue_pv(nblk - 1);
+        if (ok && nblk_max > 0) {
+            for (int t = 0; t < kTilesPerCta && ok; ++t) {
+                if (nblk_max - 1 < nblk[t]) ok = issue_pv(t, nblk_max - 1);
+            }
+            if (ok && lane == 0) tc_commit(bar(kBarVEmpty + (nblk_max - 1) % kVStages));
+            __syncwarp();
+        }
         // Drain every MMA this thread issued before TMEM can be released.
         if (lane == 0) tc_commit(bar(kBarDrain));
         __syncwarp();
         wait_bar(bar(kBarDrain), 0, abort_flag, kStatusDrain);
-    } else if (warp >= 4) {
+    } else if (warp < 8) {
         // ------------------------------------------------------------- softmax
-        const int row = static_cast<int>(threadIdx.x) - 128;          // 0..127 = TMEM lane
+        reg_alloc<kSoftmaxRegs>();
+        const int t = warp >> 2;                                     // query tile
+        const int row = static_cast<int>(threadIdx.x) - 128 * t;     // TMEM lane
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const int qt = cta_tile * kTilesPerCta + t;
         const int q_row = qt * kTileRows + row;
         const bool row_valid = q_row < p.M;
         const int q16 = qt * (kTileRows / 16) + row / 16;
         const bool q16_valid = q16 < p.q16_tiles;
-        const float q_scale = p.routed ? __half2float(p.q_scales[head * p.q_scale_blocks + qt]) : 0.0f;
+        const float q_scale = p.routed && nblk[t] > 0 ? __half2float(p.q_scales[head * p.q_scale_blocks + qt]) : 0.0f;
         const __half* k_scales = p.routed ? p.k_scales + static_cast<std::size_t>(head) * p.k_scale_blocks : nullptr;
-        float m_run = -INFINITY;   // running max (log2 units), possibly stale by < 2^8
+        // Scores are kept in "raw" units r with score_log2 = r * c_exp: FP16
+        // tiles give r = q.k directly when score_scale > 0 (no multiply); INT8
+        // tiles give r = dot * q_scale * k_scale.
+        const bool pos_scale = p.scale_log2 > 0.0f;
+        const float c_exp = pos_scale ? p.scale_log2 : 1.0f;
+        const float a_f16 = pos_scale ? 1.0f : p.scale_log2;
+        const float threshold = kRescaleLog2 / c_exp;
+        float m_run = -INFINITY;    // running max (raw units), possibly stale by < 2^8 in p
         float l_run = 0.0f;
         bool ok = true;
-        for (int j = 0; j < nblk; ++j) {
-            const int b = j & 1;
-            // Per-key-tile routing bit and score multiplier for this row.
+        const uint32_t s_addr = tmem + lane_base + col_s(t);
+        const uint32_t o_addr = tmem + lane_base + col_o(t);
+        for (int j = 0; j < nblk[t]; ++j) {
             uint32_t bits = 0;
-            float mult[4];
+            float ratio[4];
             #pragma unroll
             for (int kt = 0; kt < 4; ++kt) {
                 const int gkt = 4 * j + kt;
                 const bool bit = p.routed && q16_valid && gkt < p.k32_tiles && route_bit(p, head, q16, gkt);
                 bits |= static_cast<uint32_t>(bit) << kt;
-                mult[kt] = p.scale_log2;
-                if (bit) mult[kt] = q_scale * __half2float(k_scales[gkt >> 1]) * p.scale_log2;
+                ratio[kt] = bit ? q_scale * __half2float(k_scales[gkt >> 1]) * a_f16 : a_f16;
             }
             if (kTrace && p.decoded_bits && row % 16 == 0 && q16_valid) {
                 #pragma unroll
@@ -477,21 +552,14 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     }
                 }
             }
-            if (!wait_bar(bar(kBarSFull + b), (j >> 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
+            if (!wait_bar(bar(kBarSFull + t), j & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
             tc_fence_after();
             uint32_t x[128];
-            {
-                uint32_t (&x0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[0]);
-                uint32_t (&x1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[32]);
-                uint32_t (&x2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[64]);
-                uint32_t (&x3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&x[96]);
-                const uint32_t s_addr = tmem + lane_base + (b ? kColS1 : 0u);
-                tmem_ld32(s_addr + 0, x0);
-                tmem_ld32(s_addr + 32, x1);
-                tmem_ld32(s_addr + 64, x2);
-                tmem_ld32(s_addr + 96, x3);
-                tc_wait_ld();
-            }
+            tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+            tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
+            tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&x[64]));
+            tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&x[96]));
+            tc_wait_ld();
             const int key0 = j * kTileKeys;
             if (kTrace && p.score_dots && row_valid) {
                 #pragma unroll
@@ -508,69 +576,82 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     }
                 }
             }
-            // Dequantise (INT8 tiles: exact s32 -> f32 via the 1.5 * 2^23 bias,
-            // |dot| <= 127^2 * 128 < 2^22) and scale into log2 units.
-            float s[128];
+            // Raw scores, in place (x[] reinterpreted as floats).
+            float* r = reinterpret_cast<float*>(x);
             #pragma unroll
             for (int kt = 0; kt < 4; ++kt) {
                 const bool is_i8 = (bits >> kt) & 1u;
-                const uint32_t bias = is_i8 ? 0x4B400000u : 0u;
-                const float sub = is_i8 ? 12582912.0f : 0.0f;
-                #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    s[kt * 32 + i] = (__uint_as_float(x[kt * 32 + i] + bias) - sub) * mult[kt];
+                const bool all_f16 = __all_sync(0xffffffffu, !is_i8);
+                const bool all_i8 = __all_sync(0xffffffffu, is_i8);
+                if (all_f16) {
+                    if (!pos_scale) {
+                        #pragma unroll
+                        for (int i = 0; i < 32; ++i) r[kt * 32 + i] *= a_f16;
+                    }
+                } else if (all_i8) {
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) r[kt * 32 + i] = s32_to_f32(x[kt * 32 + i]) * ratio[kt];
+                } else {
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float as_f16 = __uint_as_float(x[kt * 32 + i]);
+                        const float as_i8 = s32_to_f32(x[kt * 32 + i]);
+                        r[kt * 32 + i] = (is_i8 ? as_i8 : as_f16) * ratio[kt];
+                    }
                 }
             }
-            const bool edge = key0 + kTileKeys > p.N || (p.causal && key0 + kTileKeys > q_row);
-            if (edge) {
+            if (key0 + kTileKeys > p.N || (p.causal && key0 + kTileKeys > q_row)) {
                 const int limit = p.causal ? min(p.N, q_row + 1) : p.N;
                 #pragma unroll
                 for (int i = 0; i < 128; ++i) {
-                    if (key0 + i >= limit) s[i] = -INFINITY;
+                    if (key0 + i >= limit) r[i] = -INFINITY;
                 }
             }
-            float block_max = s[0];
+            float mx0 = r[0], mx1 = r[1], mx2 = r[2], mx3 = r[3];
             #pragma unroll
-            for (int i = 1; i < 128; ++i) block_max = fmaxf(block_max, s[i]);
-            float alpha = 1.0f;
-            if (block_max > m_run + kRescaleThreshold) {   // also true on the first block
-                const float m_new = fmaxf(m_run, block_max);
-                alpha = ex2(m_run - m_new);       // 0 on the first block
-                m_run = m_new;
+            for (int i = 4; i < 128; i += 4) {
+                mx0 = fmaxf(mx0, r[i]); mx1 = fmaxf(mx1, r[i + 1]);
+                mx2 = fmaxf(mx2, r[i + 2]); mx3 = fmaxf(mx3, r[i + 3]);
             }
-            const float m_use = m_run == -INFINITY ? 0.0f : m_run;
-            // P = P_hi + P_lo, both fp16: P_hi is p rounded to fp16, P_lo the
-            // (exactly computed) residual rounded to fp16. The two PV MMAs make
-            // the product accurate to ~2^-22 relative instead of fp16's 2^-11,
-            // which the parity tolerance needs once V has large-magnitude
-            // (outlier) channels. P_hi goes to columns [0,64) of the S buffer,
-            // P_lo to [64,128); the scores were already read into registers.
-            float sum = 0.0f;
-            const uint32_t p_addr = tmem + lane_base + (b ? kColS1 : 0u);
+            const float block_max = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+            float alpha = 1.0f;
+            if (block_max > m_run + threshold) {             // also true on the first block
+                alpha = ex2((m_run - block_max) * c_exp);    // 0 on the first block
+                m_run = block_max;
+            }
+            const float neg_m = m_run == -INFINITY ? 0.0f : -m_run * c_exp;
+            // P = P_hi + P_lo, both fp16: P_hi keeps the top 11 significant bits
+            // of p (exact in fp16), P_lo = p - P_hi (exact) rounded to fp16. The
+            // two PV MMAs make the product accurate to ~2^-22 relative instead
+            // of fp16's 2^-11, which the parity tolerance needs once V has
+            // large-magnitude (outlier) channels. P_hi goes to columns [0,64)
+            // of the S buffer, P_lo to [64,128).
+            float sum0 = 0.0f, sum1 = 0.0f;
             #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t hi[16], lo[16];
                 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int e = c * 32 + 2 * i;
-                    const float p0 = ex2(s[e] - m_use);
-                    const float p1 = ex2(s[e + 1] - m_use);
-                    sum += p0 + p1;
-                    const __half2 h = __floats2half2_rn(p0, p1);
-                    const float2 back = __half22float2(h);
-                    hi[i] = *reinterpret_cast<const uint32_t*>(&h);
-                    lo[i] = pack_half2(p0 - back.x, p1 - back.y);
+                    const float p0 = ex2(fmaf(r[e], c_exp, neg_m));
+                    const float p1 = ex2(fmaf(r[e + 1], c_exp, neg_m));
+                    sum0 += p0;
+                    sum1 += p1;
+                    const float h0 = __uint_as_float(__float_as_uint(p0) & 0xFFFFE000u);
+                    const float h1 = __uint_as_float(__float_as_uint(p1) & 0xFFFFE000u);
+                    hi[i] = pack_half2(h0, h1);
+                    lo[i] = pack_half2(p0 - h0, p1 - h1);
                 }
-                tmem_st16(p_addr + 16 * c, hi);
-                tmem_st16(p_addr + 64 + 16 * c, lo);
+                tmem_st16(s_addr + 16 * c, hi);
+                tmem_st16(s_addr + 64 + 16 * c, lo);
             }
-            l_run = l_run * alpha + sum;
+            l_run = l_run * alpha + (sum0 + sum1);
             if (j > 0) {
-                // O may only be rescaled once PV of the previous block landed.
-                if (!wait_bar(bar(kBarPvDone), (j - 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
+                // O may only be rescaled once PV of the previous block landed
+                // (it was issued before this block's QK, so it has).
+                if (!wait_bar(bar(kBarPvDone + t), (j - 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-                    const uint32_t o_addr = tmem + lane_base + kColO;
                     for (int c = 0; c < p.pv_n; c += 32) {
                         uint32_t ov[32];
                         tmem_ld32(o_addr + c, ov);
@@ -583,12 +664,11 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             }
             tc_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(kBarPFull + b));
+            mbar_arrive(bar(kBarPFull + t));
         }
-        if (ok && nblk > 0 && wait_bar(bar(kBarPvDone), (nblk - 1) & 1, abort_flag, kStatusSoftmax)) {
+        if (ok && nblk[t] > 0 && wait_bar(bar(kBarPvDone + t), (nblk[t] - 1) & 1, abort_flag, kStatusSoftmax)) {
             tc_fence_after();
             const float inv_l = 1.0f / l_run;
-            const uint32_t o_addr = tmem + lane_base + kColO;
             float* out = p.o + (static_cast<std::size_t>(head) * p.M + q_row) * p.d;
             for (int c = 0; c < p.pv_n; c += 32) {
                 uint32_t ov[32];
@@ -617,7 +697,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
@@ -663,14 +743,19 @@ template <int kAtoms, bool kUseTma, bool kTrace>
 cudaError_t launch_variant(const CUtensorMap* maps, const Params& p, unsigned grid, cudaStream_t stream) {
     auto kernel = tilemix_attention_kernel<kAtoms, kUseTma, kTrace>;
     const int smem = static_cast<int>(SmemLayout<kAtoms>::kBytes);
-    // The opt-in attribute is per device; set it on every launch path that has
-    // not seen the current device yet.
+    // The opt-in attribute is per device; set it the first time a device is seen.
     static int configured[64] = {0};
     int device = 0;
     cudaError_t status = cudaGetDevice(&device);
     if (status != cudaSuccess) return status;
     if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
     if (!configured[device]) {
+        // The in-kernel register split must fit in what the launch provides;
+        // otherwise the softmax warpgroups' setmaxnreg.inc could never complete.
+        cudaFuncAttributes attr{};
+        status = cudaFuncGetAttributes(&attr, kernel);
+        if (status != cudaSuccess) return status;
+        if (attr.numRegs * kAttnThreads < kSplitRegs) return cudaErrorInvalidConfiguration;
         status = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (status != cudaSuccess) return status;
         configured[device] = 1;
@@ -700,7 +785,7 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     p.decoded_bits = prob.decoded_bits;
     p.score_dots = prob.score_dots;
     p.heads = prob.heads; p.M = prob.M; p.N = prob.N; p.d = prob.d;
-    p.q_tiles = (prob.M - 1) / kTileRows + 1;
+    p.cta_tiles = (prob.M - 1) / kCtaRows + 1;
     p.kv_blocks = (prob.N - 1) / kTileKeys + 1;
     p.q16_tiles = (prob.M - 1) / 16 + 1;
     p.k32_tiles = (prob.N - 1) / 32 + 1;
@@ -718,8 +803,9 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     p.i8_ksteps = (prob.d + 31) / 32;
     p.pv_n = (prob.d + 15) / 16 * 16;
     p.o_vec = (prob.d % 4 == 0 && aligned16(prob.o)) ? 1 : 0;
+    p.head_group = std::min(prob.heads, 8);
 
-    const long long grid = static_cast<long long>(p.q_tiles) * p.heads;
+    const long long grid = static_cast<long long>(p.cta_tiles) * p.heads;
     if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     const int atoms = prob.d <= 64 ? 1 : 2;
     const bool trace = prob.decoded_bits != nullptr || prob.score_dots != nullptr;

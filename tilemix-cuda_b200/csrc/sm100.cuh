@@ -211,6 +211,16 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
 #undef TILEMIX_R8
 #undef TILEMIX_W8
 
+// Warpgroup register reallocation (all 128 threads of the warpgroup execute it).
+template <int kRegs>
+__device__ __forceinline__ void reg_alloc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" :: "n"(kRegs));
+}
+template <int kRegs>
+__device__ __forceinline__ void reg_dealloc() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(kRegs));
+}
+
 // 2^x on the MUFU pipe (PTX ex2.approx.ftz.f32; ex2(-inf) = +0).
 __device__ __forceinline__ float ex2(float x) {
     float y;
