@@ -16,7 +16,7 @@
 // running max only moved when it grows by more than 2^8 (the final result is
 // unchanged mathematically; P stays <= 256, well inside fp16).
 //
-// CTA = two 128-row query tiles (256 rows) of one head, 384 threads:
+// CTA = two 128-row query tiles (256 rows) of one head, 320 threads:
 //   warps 0-3  softmax of query tile 0   (thread t = query row t = TMEM lane t)
 //   warps 4-7  softmax of query tile 1
 //   warp 8     MMA issuer (one lane) + TMEM owner: S0 | S1 | O0 | O1
@@ -24,20 +24,23 @@
 //   warp 9     producer: TMA (or, for head dims TMA cannot address, plain
 //              loads) of Q/Q8 for both tiles once, then per 128-key block
 //              K/K8 (one stage) and V (two stages), 128-byte swizzled
-//   warps 10-11 idle (complete the third warpgroup for the register split)
 // The MMA warp issues, per key block j:  PV(0, j-1), QK(0, j), PV(1, j-1),
 // QK(1, j).  Each tile's chain is QK -> softmax -> PV -> next QK, and the two
 // tiles' chains interleave on the tensor pipe, so one tile's softmax runs while
-// the other tile's MMAs execute ("ping-pong"). P (fp16 hi in columns [0,64),
-// lo in [64,128)) overwrites S in TMEM and is consumed by TMEM-A MMAs; the
-// in-order tensor pipe guarantees PV(t, j-1) reads P before QK(t, j) rewrites S.
+// the other tile's MMAs execute ("ping-pong"). P overwrites S in TMEM (per
+// 32-key chunk: fp16 hi in the chunk's first 16 columns, lo in the last 16) and
+// is consumed by TMEM-A MMAs; the in-order tensor pipe guarantees PV(t, j-1)
+// reads P before QK(t, j) rewrites S.
 //
 // Routing inside a 128-row tile: for each 32-key tile the 8 routing bits of
-// the tile's 16-row query tiles form a pattern. Runs of key tiles with equal
-// patterns are issued as one MMA per precision with N = 32 * run length; the
-// FP16 MMA disables the TMEM lanes of INT8 rows and vice versa (tcgen05.mma
-// disable-output-lane), so both kinds share one accumulator. A uniform tile
-// costs one MMA; a mixed one costs one of each.
+// the tile's 16-row query tiles select INT8 or FP16 per 16 rows. A uniform
+// block is one full-width MMA (N = 128) of its precision. A mixed block is one
+// full-width "base" MMA of one precision for all rows, then "overlay" MMAs of
+// the other precision over the key-tile runs that need it, with the TMEM lanes
+// of rows that keep the base result disabled (tcgen05.mma disable-output-lane);
+// the in-order tensor pipe makes the overlay overwrite the base exactly where
+// routed. The base precision is the one that leaves the fewer overlay runs
+// (narrow MMAs are shared-memory bound, so they cost nearly a full one).
 //
 // Every mbarrier wait is bounded (1 s of %globaltimer). A wait that runs out
 // records a code in g_tilemix_status, raises a CTA-wide abort flag and every
@@ -68,19 +71,14 @@ constexpr int kTilesPerCta = 2;
 constexpr int kCtaRows = kTileRows * kTilesPerCta;
 constexpr int kTileKeys = 128;               // keys per block
 constexpr int kVStages = 2;
+constexpr int kRouteSlots = 8;               // producer runs at most ~2 blocks ahead
 constexpr int kMmaWarp = 8;
 constexpr int kProducerWarp = 9;
-constexpr int kAttnThreads = 384;             // warps 10-11 only take part in the register split
-// Register split (setmaxnreg): the two softmax warpgroups hold a 128-wide
-// score row each and grow to kSoftmaxRegs; the MMA/producer warpgroup shrinks
-// to kOtherRegs. The launch must provide at least the split's total, which the
-// host checks against the compiled register count before every first launch.
-constexpr int kSoftmaxRegs = 200;
-constexpr int kOtherRegs = 96;
-constexpr int kSplitRegs = 256 * kSoftmaxRegs + 128 * kOtherRegs;
+constexpr int kAttnThreads = 320;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAtomBytes = 128 * 128;   // 128 rows x 128 bytes
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
+constexpr uint32_t kSuspendNs = 200000;        // per try_wait suspension (wakes early on completion)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;         // rescale only when the max grows by > 2^8
 
@@ -103,8 +101,9 @@ struct SmemLayout {
     static constexpr uint32_t kK = kQ8 + kTilesPerCta * kAtomBytes;     // one stage
     static constexpr uint32_t kK8 = kK + kTileF16;
     static constexpr uint32_t kV = kK8 + kAtomBytes;                    // [2 stages]
-    static constexpr uint32_t kBars = kV + kVStages * kTileF16;
-    static constexpr uint32_t kNumBars = 16;
+    static constexpr uint32_t kRoute = kV + kVStages * kTileF16;      // [kRouteSlots] x 16 B
+    static constexpr uint32_t kBars = kRoute + kRouteSlots * 16;
+    static constexpr uint32_t kNumBars = 16 + kRouteSlots;
     static constexpr uint32_t kMisc = kBars + kNumBars * 8;            // tmem base, abort flag
     static constexpr uint32_t kEnd = kMisc + 16;
     static constexpr uint32_t kBytes = kEnd + 1024;                     // + alignment slack
@@ -112,7 +111,19 @@ struct SmemLayout {
 
 enum Bar : int {
     kBarQFull = 0, kBarKFull = 1, kBarKEmpty = 2, kBarVFull = 3, kBarVEmpty = 5,
-    kBarSFull = 7, kBarPFull = 9, kBarPvDone = 11, kBarDrain = 13,
+    kBarSFull = 7, kBarPFull = 9, kBarPvDone = 11, kBarDrain = 13, kBarRoute = 16,
+};
+
+// Per-block routing summary published by the producer in a shared-memory ring
+// (global loads issued from the softmax loop proved far costlier than their
+// latency; only the producer touches the routing words and K scales):
+//   pats   bits [16 kt, 16 kt + 16): INT8 bit of the CTA's 16 query tiles for key tile kt
+//   valid  bits [0,16) query tiles that exist and process the block, [16,24) key tiles
+//   scales the block's two 64-key K scales (fp16, 0 when unrouted)
+struct RouteSlot {
+    std::uint64_t pats;
+    uint32_t valid;
+    uint32_t scales;
 };
 
 struct Params {
@@ -149,7 +160,7 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
     if (!ok) {
         const uint64_t start = global_timer_ns();
         while (true) {
-            if (mbar_try_wait(bar, parity)) { ok = true; break; }
+            if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) { ok = true; break; }
             if (*abort_flag) break;
             if (global_timer_ns() - start > kWaitLimitNs) {
                 *abort_flag = 1;
@@ -161,10 +172,16 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
     return __all_sync(0xffffffffu, ok);
 }
 
-__device__ __forceinline__ bool route_bit(const Params& p, int head, int q16, int gkt) {
+// Routing words are read one key block ahead and decoded in the next
+// iteration: decoding right after the load would stall the in-order warp on
+// global-load latency every block.
+__device__ __forceinline__ std::uint64_t route_word(const Params& p, int head, int q16, int gkt) {
     const long long group = gkt / p.group;
-    const std::uint64_t word = __ldg(p.words + head * p.words_per_head
-                                     + static_cast<long long>(q16) * p.words_per_row + group / 64);
+    return __ldg(p.words + head * p.words_per_head + static_cast<long long>(q16) * p.words_per_row + group / 64);
+}
+
+__device__ __forceinline__ bool route_word_bit(const Params& p, std::uint64_t word, int gkt) {
+    const long long group = gkt / p.group;
     return ((word >> (group % 64)) & 1ull) != 0;
 }
 
@@ -180,19 +197,15 @@ struct BlockRoute {
     bool need_i8;
 };
 
-__device__ __forceinline__ BlockRoute block_route(const Params& p, int head, int cta_tile, int j,
-                                                  const int (&nblk)[2], uint32_t lane) {
+__device__ __forceinline__ BlockRoute unpack_route(const RouteSlot& slot) {
     BlockRoute r;
-    const int q16 = cta_tile * (kCtaRows / 16) + static_cast<int>(lane);
-    const bool q_valid = lane < 16 && q16 < p.q16_tiles && j < nblk[(lane >> 3) & 1];
-    r.valid = __ballot_sync(0xffffffffu, q_valid);
-    r.ktiles = min(4, p.k32_tiles - 4 * j);
+    r.valid = slot.valid & 0xffffu;
+    r.ktiles = static_cast<int>((slot.valid >> 16) & 0xffu);
     r.need_f16 = false;
     r.need_i8 = false;
     #pragma unroll
     for (int kt = 0; kt < 4; ++kt) {
-        const bool bit = p.routed && q_valid && kt < r.ktiles && route_bit(p, head, q16, 4 * j + kt);
-        r.pat[kt] = __ballot_sync(0xffffffffu, bit);
+        r.pat[kt] = static_cast<uint32_t>(slot.pats >> (16 * kt)) & 0xffffu;
         if (kt < r.ktiles) {
             r.need_i8 |= r.pat[kt] != 0;
             r.need_f16 |= (~r.pat[kt] & r.valid) != 0;
@@ -200,6 +213,43 @@ __device__ __forceinline__ BlockRoute block_route(const Params& p, int head, int
     }
     return r;
 }
+
+// Lane l < 16 reads the words of query tile l for the four key tiles of a block.
+struct RoutePrefetch {
+    std::uint64_t w[4];
+
+    __device__ __forceinline__ void fetch(const Params& p, int head, int cta_tile, int j,
+                                          const int (&nblk)[2], uint32_t lane) {
+        const int q16 = cta_tile * (kCtaRows / 16) + static_cast<int>(lane);
+        const bool q_valid = lane < 16 && q16 < p.q16_tiles && j < nblk[(lane >> 3) & 1];
+        #pragma unroll
+        for (int kt = 0; kt < 4; ++kt) {
+            const int gkt = 4 * j + kt;
+            w[kt] = p.routed && q_valid && gkt < p.k32_tiles ? route_word(p, head, q16, gkt) : 0ull;
+        }
+    }
+
+    __device__ __forceinline__ BlockRoute decode(const Params& p, int cta_tile, int j,
+                                                 const int (&nblk)[2], uint32_t lane) const {
+        BlockRoute r;
+        const int q16 = cta_tile * (kCtaRows / 16) + static_cast<int>(lane);
+        const bool q_valid = lane < 16 && q16 < p.q16_tiles && j < nblk[(lane >> 3) & 1];
+        r.valid = __ballot_sync(0xffffffffu, q_valid);
+        r.ktiles = min(4, p.k32_tiles - 4 * j);
+        r.need_f16 = false;
+        r.need_i8 = false;
+        #pragma unroll
+        for (int kt = 0; kt < 4; ++kt) {
+            const bool bit = q_valid && kt < r.ktiles && route_word_bit(p, w[kt], 4 * j + kt);
+            r.pat[kt] = __ballot_sync(0xffffffffu, bit);
+            if (kt < r.ktiles) {
+                r.need_i8 |= r.pat[kt] != 0;
+                r.need_f16 |= (~r.pat[kt] & r.valid) != 0;
+            }
+        }
+        return r;
+    }
+};
 
 __device__ __forceinline__ void lane_mask(uint32_t tiles, uint32_t (&m)[4]) {
     #pragma unroll
@@ -312,6 +362,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             mbar_init(bar(kBarPvDone + t), 1);
         }
         mbar_init(bar(kBarDrain), 1);
+        for (int r = 0; r < kRouteSlots; ++r) mbar_init(bar(kBarRoute + r), 1);
         *abort_flag = 0;
         mbar_init_fence();
         fence_proxy_async_smem();
@@ -325,7 +376,6 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp >= 8) reg_dealloc<kOtherRegs>();   // warpgroup 2: MMA, producer, two idle warps
     if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer
         if (kUseTma && lane == 0) {
@@ -363,8 +413,30 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             if (lane == 0) mbar_arrive(bar(kBarQFull));
         }
         int k_issued = 0, v_issued = 0;
+        RoutePrefetch pre;
+        pre.fetch(p, head, cta_tile, 0, nblk, lane);
+        const __half* k_scales = p.routed ? p.k_scales + static_cast<std::size_t>(head) * p.k_scale_blocks : nullptr;
+        RouteSlot* ring = reinterpret_cast<RouteSlot*>(smem + L::kRoute);
         for (int j = 0; j < nblk_max; ++j) {
-            const BlockRoute r = block_route(p, head, cta_tile, j, nblk, lane);
+            const BlockRoute r = pre.decode(p, cta_tile, j, nblk, lane);
+            pre.fetch(p, head, cta_tile, j + 1, nblk, lane);
+            if (lane == 0) {
+                uint32_t scales = 0;
+                if (p.routed) {
+                    const uint32_t s0 = 2 * j < p.k_scale_blocks ? __half_as_ushort(k_scales[2 * j]) : 0u;
+                    const uint32_t s1 = 2 * j + 1 < p.k_scale_blocks ? __half_as_ushort(k_scales[2 * j + 1]) : 0u;
+                    scales = s0 | (s1 << 16);
+                }
+                RouteSlot slot;
+                slot.pats = 0;
+                #pragma unroll
+                for (int kt = 0; kt < 4; ++kt) slot.pats |= static_cast<std::uint64_t>(r.pat[kt] & 0xffffu) << (16 * kt);
+                slot.valid = (r.valid & 0xffffu) | (static_cast<uint32_t>(r.ktiles) << 16);
+                slot.scales = scales;
+                ring[j % kRouteSlots] = slot;
+                mbar_arrive(bar(kBarRoute + j % kRouteSlots));   // release: slot visible to its waiters
+            }
+            __syncwarp();
             if (!wait_bar(bar(kBarKEmpty), (j & 1) ^ 1, abort_flag, kStatusProducer)) break;
             if (kUseTma) {
                 if (lane == 0) {
@@ -430,8 +502,9 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
                     // 8-key groups 1024 B apart; each K step covers 16 keys.
                     const uint64_t b_desc = smem_desc_sw128(v_addr + s * 2048, kAtomBytes, 1024);
-                    mma_f16_ts(tmem + col_o(t), p_tmem + s * 8, b_desc, pv_idesc, (i > 0 || s > 0) ? 1u : 0u);
-                    mma_f16_ts(tmem + col_o(t), p_tmem + 64 + s * 8, b_desc, pv_idesc, 1u);
+                    const uint32_t a_hi = p_tmem + 32 * (s >> 1) + 8 * (s & 1);
+                    mma_f16_ts(tmem + col_o(t), a_hi, b_desc, pv_idesc, (i > 0 || s > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem + col_o(t), a_hi + 16, b_desc, pv_idesc, 1u);
                 }
                 tc_commit(bar(kBarPvDone + t));
             }
@@ -441,50 +514,89 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         // QK^T of tile t for block j into S_t.
         auto issue_qk = [&](int t, const BlockRoute& r) {
             const uint32_t s_tmem = tmem + col_s(t);
-            const uint32_t q_addr = sbase + L::kQ + t * L::kTileF16;
-            const uint32_t q8_addr = sbase + L::kQ8 + t * kAtomBytes;
-            const uint32_t k_addr = sbase + L::kK, k8_addr = sbase + L::kK8;
+            const uint64_t qf = smem_desc_sw128(sbase + L::kQ + t * L::kTileF16, 16, 1024);
+            const uint64_t qi = smem_desc_sw128(sbase + L::kQ8 + t * kAtomBytes, 16, 1024);
+            const uint64_t kf = smem_desc_sw128(sbase + L::kK, 16, 1024);
+            const uint64_t ki = smem_desc_sw128(sbase + L::kK8, 16, 1024);
             const uint32_t valid = (r.valid >> (8 * t)) & 0xffu;
-            int kt = 0;
-            while (kt < r.ktiles) {
-                const uint32_t pat = (r.pat[kt] >> (8 * t)) & 0xffu;
-                int end = kt + 1;
-                while (end < r.ktiles && ((r.pat[end] >> (8 * t)) & 0xffu) == pat) ++end;
-                const uint32_t i8_rows = pat & valid;
-                const uint32_t f16_rows = ~pat & valid;
-                const int n = 32 * (end - kt);
-                if (f16_rows) {
-                    uint32_t off[4];
-                    lane_mask(i8_rows, off);
-                    const uint32_t idesc = idesc_f16_f32(kTileRows, n, false);
-                    for (int s = 0; s < p.f16_ksteps; ++s) {
-                        const uint32_t koff = (s >> 2) * kAtomBytes + (s & 3) * 32;
-                        const uint64_t a_desc = smem_desc_sw128(q_addr + koff, 16, 1024);
-                        const uint64_t b_desc = smem_desc_sw128(k_addr + koff + kt * 4096, 16, 1024);
-                        mma_f16_ss(s_tmem + 32 * kt, a_desc, b_desc, idesc, off, s > 0 ? 1u : 0u);
+            // Row sets per key tile packed one byte per key tile.
+            uint32_t i8set = 0, f16set = 0;
+            #pragma unroll
+            for (int kt = 0; kt < 4; ++kt) {
+                if (kt < r.ktiles) {
+                    i8set |= ((r.pat[kt] >> (8 * t)) & valid) << (8 * kt);
+                    f16set |= (~(r.pat[kt] >> (8 * t)) & valid) << (8 * kt);
+                }
+            }
+            // One precision over key tiles [kt0, kt0 + nkt), TMEM lanes of the
+            // 16-row tiles outside `rows` left untouched (descriptor start
+            // addresses advance by byte offset >> 4).
+            auto mma_run = [&](bool int8, uint32_t rows, int kt0, int nkt) {
+                uint32_t off[4];
+                lane_mask(~rows & 0xffu, off);
+                const uint32_t d_tmem = s_tmem + 32 * kt0;
+                const uint64_t kofs = static_cast<uint64_t>(kt0 * 4096) >> 4;
+                if (int8) {
+                    const uint32_t idesc = idesc_s8_s32(kTileRows, 32 * nkt);
+                    for (int ks = 0; ks < p.i8_ksteps; ++ks) {
+                        mma_i8_ss(d_tmem, qi + 2 * ks, ki + kofs + 2 * ks, idesc, off, ks > 0 ? 1u : 0u);
+                    }
+                } else {
+                    const uint32_t idesc = idesc_f16_f32(kTileRows, 32 * nkt, false);
+                    for (int ks = 0; ks < p.f16_ksteps; ++ks) {
+                        const uint64_t ko = static_cast<uint64_t>((ks >> 2) * kAtomBytes + (ks & 3) * 32) >> 4;
+                        mma_f16_ss(d_tmem, qf + ko, kf + kofs + ko, idesc, off, ks > 0 ? 1u : 0u);
                     }
                 }
-                if (i8_rows) {
-                    uint32_t off[4];
-                    lane_mask(f16_rows, off);
-                    const uint32_t idesc = idesc_s8_s32(kTileRows, n);
-                    for (int s = 0; s < p.i8_ksteps; ++s) {
-                        const uint64_t a_desc = smem_desc_sw128(q8_addr + s * 32, 16, 1024);
-                        const uint64_t b_desc = smem_desc_sw128(k8_addr + s * 32 + kt * 4096, 16, 1024);
-                        mma_i8_ss(s_tmem + 32 * kt, a_desc, b_desc, idesc, off, s > 0 ? 1u : 0u);
+            };
+            // Overlay runs: maximal runs of key tiles whose row sets are equal and non-empty.
+            auto overlay_runs = [&](uint32_t sets, bool issue, bool int8) -> int {
+                int runs = 0, kt = 0;
+                while (kt < r.ktiles) {
+                    const uint32_t set = (sets >> (8 * kt)) & 0xffu;
+                    int end = kt + 1;
+                    while (end < r.ktiles && ((sets >> (8 * end)) & 0xffu) == set) ++end;
+                    if (set) {
+                        ++runs;
+                        if (issue) mma_run(int8, set, kt, end - kt);
                     }
+                    kt = end;
                 }
-                kt = end;
+                return runs;
+            };
+            if (!i8set || !f16set) {
+                mma_run(i8set != 0, 0xffu, 0, r.ktiles);
+            } else {
+                const int f16_runs = overlay_runs(f16set, false, false);
+                const int i8_runs = overlay_runs(i8set, false, true);
+                if (f16_runs <= i8_runs) {        // INT8 base, FP16 overlays
+                    mma_run(true, 0xffu, 0, r.ktiles);
+                    overlay_runs(f16set, true, false);
+                } else {                          // FP16 base, INT8 overlays
+                    mma_run(false, 0xffu, 0, r.ktiles);
+                    overlay_runs(i8set, true, true);
+                }
             }
             tc_commit(bar(kBarSFull + t));
         };
+        const RouteSlot* ring = reinterpret_cast<const RouteSlot*>(smem + L::kRoute);
         for (int j = 0; ok && j < nblk_max; ++j) {
-            const BlockRoute r = block_route(p, head, cta_tile, j, nblk, lane);
-            if (!wait_bar(bar(kBarKFull), j & 1, abort_flag, kStatusMma)) { ok = false; break; }
-            tc_fence_after();
+            if (!wait_bar(bar(kBarRoute + j % kRouteSlots), (j / kRouteSlots) & 1, abort_flag, kStatusMma)) {
+                ok = false;
+                break;
+            }
+            const BlockRoute r = unpack_route(ring[j % kRouteSlots]);
+            bool k_ready = false;
             for (int t = 0; t < kTilesPerCta && ok; ++t) {
+                // PV of the previous block first: it only needs P and V, so the
+                // load of this block's K is off the tensor pipe's critical path.
                 if (j > 0 && j - 1 < nblk[t] && !issue_pv(t, j - 1)) { ok = false; break; }
                 if (j < nblk[t]) {
+                    if (!k_ready) {
+                        if (!wait_bar(bar(kBarKFull), j & 1, abort_flag, kStatusMma)) { ok = false; break; }
+                        tc_fence_after();
+                        k_ready = true;
+                    }
                     if (lane == 0) issue_qk(t, r);
                     __syncwarp();
                 }
@@ -509,7 +621,11 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         wait_bar(bar(kBarDrain), 0, abort_flag, kStatusDrain);
     } else if (warp < 8) {
         // ------------------------------------------------------------- softmax
-        reg_alloc<kSoftmaxRegs>();
+        // Two passes over the 128-column S row in 32-column TMEM chunks (the
+        // next chunk's load overlaps the current chunk's math): pass 1
+        // dequantises INT8 chunks into raw fp32 units, applies the key mask on
+        // edge blocks, writes modified chunks back and takes the row max;
+        // pass 2 exponentiates and writes P (hi, lo) over the chunk.
         const int t = warp >> 2;                                     // query tile
         const int row = static_cast<int>(threadIdx.x) - 128 * t;     // TMEM lane
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
@@ -519,7 +635,6 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         const int q16 = qt * (kTileRows / 16) + row / 16;
         const bool q16_valid = q16 < p.q16_tiles;
         const float q_scale = p.routed && nblk[t] > 0 ? __half2float(p.q_scales[head * p.q_scale_blocks + qt]) : 0.0f;
-        const __half* k_scales = p.routed ? p.k_scales + static_cast<std::size_t>(head) * p.k_scale_blocks : nullptr;
         // Scores are kept in "raw" units r with score_log2 = r * c_exp: FP16
         // tiles give r = q.k directly when score_scale > 0 (no multiply); INT8
         // tiles give r = dot * q_scale * k_scale.
@@ -532,15 +647,83 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         bool ok = true;
         const uint32_t s_addr = tmem + lane_base + col_s(t);
         const uint32_t o_addr = tmem + lane_base + col_o(t);
+        const RouteSlot* ring = reinterpret_cast<const RouteSlot*>(smem + L::kRoute);
+        const int qlocal = 8 * t + row / 16;                          // query tile within the CTA
+        uint32_t bufa[32], bufb[32];
         for (int j = 0; j < nblk[t]; ++j) {
+            // The route slot of block j was published before its K load, so it
+            // is complete by the time S is; the wait only orders the read.
+            if (!wait_bar(bar(kBarRoute + j % kRouteSlots), (j / kRouteSlots) & 1, abort_flag, kStatusSoftmax)) {
+                ok = false;
+                break;
+            }
+            const RouteSlot slot = ring[j % kRouteSlots];
             uint32_t bits = 0;
-            float ratio[4];
             #pragma unroll
             for (int kt = 0; kt < 4; ++kt) {
-                const int gkt = 4 * j + kt;
-                const bool bit = p.routed && q16_valid && gkt < p.k32_tiles && route_bit(p, head, q16, gkt);
-                bits |= static_cast<uint32_t>(bit) << kt;
-                ratio[kt] = bit ? q_scale * __half2float(k_scales[gkt >> 1]) * a_f16 : a_f16;
+                bits |= static_cast<uint32_t>((slot.pats >> (16 * kt + qlocal)) & 1ull) << kt;
+            }
+            if (!q16_valid) bits = 0;
+            const float ks0 = __half2float(__ushort_as_half(static_cast<unsigned short>(slot.scales & 0xffffu)));
+            const float ks1 = __half2float(__ushort_as_half(static_cast<unsigned short>(slot.scales >> 16)));
+            if (!wait_bar(bar(kBarSFull + t), j & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
+            tc_fence_after();
+            const int key0 = j * kTileKeys;
+            const bool edge = key0 + kTileKeys > p.N || (p.causal && key0 + kTileKeys > q_row);
+            const int limit = p.causal ? min(p.N, q_row + 1) : p.N;
+            // ---- pass 1: row max in raw units. INT8 chunks take an integer
+            // max of the s32 dots (scales are >= 0 when score_scale > 0) and
+            // scale it once; blocks that touch the key mask, and score_scale
+            // <= 0, take the general per-element path.
+            const bool fast = pos_scale && !edge;
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+            auto pass1 = [&](const uint32_t (&x)[32], int c) {
+                const bool is_i8 = (bits >> c) & 1u;
+                const float ratio = is_i8 ? q_scale * (c < 2 ? ks0 : ks1) * a_f16 : a_f16;
+                if (kTrace && p.score_dots && row_valid && is_i8) {
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int key = key0 + c * 32 + i;
+                        if (key < p.N) {
+                            p.score_dots[(static_cast<std::size_t>(head) * p.M + q_row) * p.N + key] =
+                                static_cast<int32_t>(x[i]);
+                        }
+                    }
+                }
+                if (fast) {
+                    if (is_i8) {
+                        int i0 = static_cast<int>(x[0]), i1 = static_cast<int>(x[1]);
+                        #pragma unroll
+                        for (int i = 2; i < 32; i += 2) {
+                            i0 = max(i0, static_cast<int>(x[i]));
+                            i1 = max(i1, static_cast<int>(x[i + 1]));
+                        }
+                        mx0 = fmaxf(mx0, static_cast<float>(max(i0, i1)) * ratio);
+                    } else {
+                        #pragma unroll
+                        for (int i = 0; i < 32; i += 2) {
+                            mx0 = fmaxf(mx0, __uint_as_float(x[i]));
+                            mx1 = fmaxf(mx1, __uint_as_float(x[i + 1]));
+                        }
+                    }
+                } else {
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        float r = (is_i8 ? s32_to_f32(x[i]) : __uint_as_float(x[i])) * ratio;
+                        if (key0 + c * 32 + i >= limit) r = -INFINITY;
+                        if (i & 1) mx1 = fmaxf(mx1, r); else mx0 = fmaxf(mx0, r);
+                    }
+                }
+            };
+            tmem_ld32(s_addr, bufa);
+            #pragma unroll 1
+            for (int c = 0; c < 4; c += 2) {
+                tc_wait_ld();
+                tmem_ld32(s_addr + 32 * (c + 1), bufb);
+                pass1(bufa, c);
+                tc_wait_ld();
+                if (c + 2 < 4) tmem_ld32(s_addr + 32 * (c + 2), bufa);
+                pass1(bufb, c + 1);
             }
             if (kTrace && p.decoded_bits && row % 16 == 0 && q16_valid) {
                 #pragma unroll
@@ -552,89 +735,68 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     }
                 }
             }
-            if (!wait_bar(bar(kBarSFull + t), j & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
-            tc_fence_after();
-            uint32_t x[128];
-            tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
-            tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
-            tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&x[64]));
-            tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&x[96]));
-            tc_wait_ld();
-            const int key0 = j * kTileKeys;
-            if (kTrace && p.score_dots && row_valid) {
-                #pragma unroll
-                for (int kt = 0; kt < 4; ++kt) {
-                    if ((bits >> kt) & 1u) {
-                        #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const int key = key0 + kt * 32 + i;
-                            if (key < p.N) {
-                                p.score_dots[(static_cast<std::size_t>(head) * p.M + q_row) * p.N + key] =
-                                    static_cast<int32_t>(x[kt * 32 + i]);
-                            }
-                        }
-                    }
-                }
-            }
-            // Raw scores, in place (x[] reinterpreted as floats).
-            float* r = reinterpret_cast<float*>(x);
-            #pragma unroll
-            for (int kt = 0; kt < 4; ++kt) {
-                const bool is_i8 = (bits >> kt) & 1u;
-                const bool all_f16 = __all_sync(0xffffffffu, !is_i8);
-                const bool all_i8 = __all_sync(0xffffffffu, is_i8);
-                if (all_f16) {
-                    if (!pos_scale) {
-                        #pragma unroll
-                        for (int i = 0; i < 32; ++i) r[kt * 32 + i] *= a_f16;
-                    }
-                } else if (all_i8) {
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) r[kt * 32 + i] = s32_to_f32(x[kt * 32 + i]) * ratio[kt];
-                } else {
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float as_f16 = __uint_as_float(x[kt * 32 + i]);
-                        const float as_i8 = s32_to_f32(x[kt * 32 + i]);
-                        r[kt * 32 + i] = (is_i8 ? as_i8 : as_f16) * ratio[kt];
-                    }
-                }
-            }
-            if (key0 + kTileKeys > p.N || (p.causal && key0 + kTileKeys > q_row)) {
-                const int limit = p.causal ? min(p.N, q_row + 1) : p.N;
-                #pragma unroll
-                for (int i = 0; i < 128; ++i) {
-                    if (key0 + i >= limit) r[i] = -INFINITY;
-                }
-            }
-            float mx0 = r[0], mx1 = r[1], mx2 = r[2], mx3 = r[3];
-            #pragma unroll
-            for (int i = 4; i < 128; i += 4) {
-                mx0 = fmaxf(mx0, r[i]); mx1 = fmaxf(mx1, r[i + 1]);
-                mx2 = fmaxf(mx2, r[i + 2]); mx3 = fmaxf(mx3, r[i + 3]);
-            }
-            const float block_max = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+            const float block_max = fmaxf(mx0, mx1);
             float alpha = 1.0f;
             if (block_max > m_run + threshold) {             // also true on the first block
                 alpha = ex2((m_run - block_max) * c_exp);    // 0 on the first block
                 m_run = block_max;
             }
             const float neg_m = m_run == -INFINITY ? 0.0f : -m_run * c_exp;
-            // P = P_hi + P_lo, both fp16: P_hi keeps the top 11 significant bits
-            // of p (exact in fp16), P_lo = p - P_hi (exact) rounded to fp16. The
-            // two PV MMAs make the product accurate to ~2^-22 relative instead
-            // of fp16's 2^-11, which the parity tolerance needs once V has
-            // large-magnitude (outlier) channels. P_hi goes to columns [0,64)
-            // of the S buffer, P_lo to [64,128).
+            if (j > 0) {
+                // Rescale O before this block's PV. PV of the previous block was
+                // issued before this block's QK, so it has landed; the TMEM
+                // stores overlap pass 2 and are waited for before P is published.
+                if (!wait_bar(bar(kBarPvDone + t), (j - 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+                    tmem_ld32(o_addr, bufa);
+                    #pragma unroll 1
+                    for (int c = 0; c < p.pv_n; c += 64) {
+                        tc_wait_ld();
+                        if (c + 32 < p.pv_n) tmem_ld32(o_addr + c + 32, bufb);
+                        #pragma unroll
+                        for (int i = 0; i < 32; ++i) bufa[i] = __float_as_uint(__uint_as_float(bufa[i]) * alpha);
+                        tmem_st32(o_addr + c, bufa);
+                        if (c + 32 < p.pv_n) {
+                            tc_wait_ld();
+                            tc_wait_st();
+                            if (c + 64 < p.pv_n) tmem_ld32(o_addr + c + 64, bufa);
+                            #pragma unroll
+                            for (int i = 0; i < 32; ++i) bufb[i] = __float_as_uint(__uint_as_float(bufb[i]) * alpha);
+                            tmem_st32(o_addr + c + 32, bufb);
+                        }
+                    }
+                }
+            }
+            // ---- pass 2: P = P_hi + P_lo, both fp16. P_hi keeps the top 11
+            // significant bits of p (exact in fp16), P_lo = p - P_hi (exact)
+            // rounded to fp16; the two PV MMAs make the product accurate to
+            // ~2^-22 relative instead of fp16's 2^-11, which the parity
+            // tolerance needs once V has large-magnitude (outlier) channels.
+            // Chunk c's P_hi goes to its columns [32c, 32c+16), P_lo to [32c+16, 32c+32).
             float sum0 = 0.0f, sum1 = 0.0f;
-            #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            auto pass2 = [&](const uint32_t (&x)[32], int c) {
+                const bool is_i8 = (bits >> c) & 1u;
+                const float mul = (is_i8 ? q_scale * (c < 2 ? ks0 : ks1) * a_f16 : a_f16) * c_exp;
+                float arg[32];
+                if (is_i8) {
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(s32_to_f32(x[i]), mul, neg_m);
+                } else {
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(x[i]), mul, neg_m);
+                }
+                if (!fast) {
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        if (key0 + c * 32 + i >= limit) arg[i] = -INFINITY;
+                    }
+                }
                 uint32_t hi[16], lo[16];
                 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int e = c * 32 + 2 * i;
-                    const float p0 = ex2(fmaf(r[e], c_exp, neg_m));
-                    const float p1 = ex2(fmaf(r[e + 1], c_exp, neg_m));
+                    const float p0 = ex2(arg[2 * i]);
+                    const float p1 = ex2(arg[2 * i + 1]);
                     sum0 += p0;
                     sum1 += p1;
                     const float h0 = __uint_as_float(__float_as_uint(p0) & 0xFFFFE000u);
@@ -642,26 +804,20 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     hi[i] = pack_half2(h0, h1);
                     lo[i] = pack_half2(p0 - h0, p1 - h1);
                 }
-                tmem_st16(s_addr + 16 * c, hi);
-                tmem_st16(s_addr + 64 + 16 * c, lo);
+                tmem_st16(s_addr + 32 * c, hi);
+                tmem_st16(s_addr + 32 * c + 16, lo);
+            };
+            tmem_ld32(s_addr, bufa);
+            #pragma unroll 1
+            for (int c = 0; c < 4; c += 2) {
+                tc_wait_ld();
+                tmem_ld32(s_addr + 32 * (c + 1), bufb);
+                pass2(bufa, c);
+                tc_wait_ld();
+                if (c + 2 < 4) tmem_ld32(s_addr + 32 * (c + 2), bufa);
+                pass2(bufb, c + 1);
             }
             l_run = l_run * alpha + (sum0 + sum1);
-            if (j > 0) {
-                // O may only be rescaled once PV of the previous block landed
-                // (it was issued before this block's QK, so it has).
-                if (!wait_bar(bar(kBarPvDone + t), (j - 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-                    for (int c = 0; c < p.pv_n; c += 32) {
-                        uint32_t ov[32];
-                        tmem_ld32(o_addr + c, ov);
-                        tc_wait_ld();
-                        #pragma unroll
-                        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                        tmem_st32(o_addr + c, ov);
-                    }
-                }
-            }
             tc_wait_st();
             tc_fence_before();
             mbar_arrive(bar(kBarPFull + t));
@@ -670,9 +826,9 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             tc_fence_after();
             const float inv_l = 1.0f / l_run;
             float* out = p.o + (static_cast<std::size_t>(head) * p.M + q_row) * p.d;
+            #pragma unroll 1
             for (int c = 0; c < p.pv_n; c += 32) {
-                uint32_t ov[32];
-                tmem_ld32(o_addr + c, ov);
+                tmem_ld32(o_addr + c, bufa);
                 tc_wait_ld();
                 if (row_valid) {
                     if (p.o_vec) {
@@ -680,14 +836,14 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                         for (int i = 0; i < 32; i += 4) {
                             if (c + i < p.d) {
                                 reinterpret_cast<float4*>(out + c + i)[0] = make_float4(
-                                    __uint_as_float(ov[i]) * inv_l, __uint_as_float(ov[i + 1]) * inv_l,
-                                    __uint_as_float(ov[i + 2]) * inv_l, __uint_as_float(ov[i + 3]) * inv_l);
+                                    __uint_as_float(bufa[i]) * inv_l, __uint_as_float(bufa[i + 1]) * inv_l,
+                                    __uint_as_float(bufa[i + 2]) * inv_l, __uint_as_float(bufa[i + 3]) * inv_l);
                             }
                         }
                     } else {
                         #pragma unroll
                         for (int i = 0; i < 32; ++i) {
-                            if (c + i < p.d) out[c + i] = __uint_as_float(ov[i]) * inv_l;
+                            if (c + i < p.d) out[c + i] = __uint_as_float(bufa[i]) * inv_l;
                         }
                     }
                 }
@@ -750,12 +906,6 @@ cudaError_t launch_variant(const CUtensorMap* maps, const Params& p, unsigned gr
     if (status != cudaSuccess) return status;
     if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
     if (!configured[device]) {
-        // The in-kernel register split must fit in what the launch provides;
-        // otherwise the softmax warpgroups' setmaxnreg.inc could never complete.
-        cudaFuncAttributes attr{};
-        status = cudaFuncGetAttributes(&attr, kernel);
-        if (status != cudaSuccess) return status;
-        if (attr.numRegs * kAttnThreads < kSplitRegs) return cudaErrorInvalidConfiguration;
         status = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (status != cudaSuccess) return status;
         configured[device] = 1;

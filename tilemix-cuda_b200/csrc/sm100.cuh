@@ -60,6 +60,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
+// As mbar_try_wait, but a thread whose phase is not complete is suspended
+// (it does not spin and steal issue slots) until the phase completes or about
+// `suspend_ns` nanoseconds pass.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity, uint32_t suspend_ns) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done) : "r"(bar), "r"(parity), "r"(suspend_ns) : "memory");
+    return done != 0;
+}
+
 // Generic-proxy smem writes -> visible to the async proxy (TMA / tensor core).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
