@@ -13,8 +13,8 @@
 // Differences that stay inside the parity tolerance: exp2 with log2(e) folded
 // into the score scale, P carried as two fp16 terms (hi + lo) through two PV
 // tensor-core MMAs (~2^-22 relative, vs the reference's fp32 P), and the
-// running max only moved when it grows by more than 2^8 (the final result is
-// unchanged mathematically; P stays <= 256, well inside fp16).
+// running max only moved when it grows by more than 2^15 (the final result is
+// unchanged mathematically; P stays <= 32768, inside fp16's range).
 //
 // CTA = two 128-row query tiles (256 rows) of one head, 320 threads:
 //   warps 0-3  softmax of query tile 0   (thread t = query row t = TMEM lane t)
@@ -80,7 +80,7 @@ constexpr uint32_t kAtomBytes = 128 * 128;   // 128 rows x 128 bytes
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr uint32_t kSuspendNs = 200000;        // per try_wait suspension (wakes early on completion)
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescaleLog2 = 8.0f;         // rescale only when the max grows by > 2^8
+constexpr float kRescaleLog2 = 15.0f;        // rescale only when the max grows by > 2^15 (P <= 32768)
 
 __device__ __forceinline__ uint32_t col_s(int t) { return static_cast<uint32_t>(t) * 128u; }
 __device__ __forceinline__ uint32_t col_o(int t) { return 256u + static_cast<uint32_t>(t) * 128u; }
@@ -120,11 +120,47 @@ enum Bar : int {
 //   pats   bits [16 kt, 16 kt + 16): INT8 bit of the CTA's 16 query tiles for key tile kt
 //   valid  bits [0,16) query tiles that exist and process the block, [16,24) key tiles
 //   scales the block's two 64-key K scales (fp16, 0 when unrouted)
+//   plan[t] the QK MMA plan of 128-row tile t (see make_plan)
 struct RouteSlot {
     std::uint64_t pats;
     uint32_t valid;
     uint32_t scales;
+    std::uint64_t plan[2];
 };
+
+// QK plan of one 128-row tile for one key block, packed in 64 bits:
+//   bit 0 base precision (1 = INT8), bits [1,4) base key tiles (0 = no QK),
+//   bits [4,7) overlay count, overlay i at bit 8 + 13 i: key tile (2 bits),
+//   key-tile count (3 bits), row-tile set (8 bits). Overlays are of the other
+//   precision and run after the base on the listed 16-row tiles only.
+__device__ __forceinline__ std::uint64_t make_plan(uint32_t i8set, uint32_t f16set, int ktiles) {
+    if (ktiles <= 0 || (i8set | f16set) == 0) return 0;
+    auto runs_of = [&](uint32_t sets, std::uint64_t& packed) -> int {
+        int runs = 0, kt = 0;
+        packed = 0;
+        while (kt < ktiles) {
+            const uint32_t set = (sets >> (8 * kt)) & 0xffu;
+            int end = kt + 1;
+            while (end < ktiles && ((sets >> (8 * end)) & 0xffu) == set) ++end;
+            if (set) {
+                packed |= (static_cast<std::uint64_t>(kt) | (static_cast<std::uint64_t>(end - kt) << 2) |
+                           (static_cast<std::uint64_t>(set) << 5)) << (8 + 13 * runs);
+                ++runs;
+            }
+            kt = end;
+        }
+        return runs;
+    };
+    std::uint64_t plan = static_cast<std::uint64_t>(ktiles) << 1;
+    if (!i8set || !f16set) return plan | (i8set ? 1ull : 0ull);
+    std::uint64_t f16_runs_packed, i8_runs_packed;
+    const int f16_runs = runs_of(f16set, f16_runs_packed);
+    const int i8_runs = runs_of(i8set, i8_runs_packed);
+    // INT8 MMAs cost half as much per key as FP16 ones: prefer an INT8 base
+    // unless that leaves more FP16 overlay runs than the FP16 base leaves INT8 runs.
+    if (f16_runs <= i8_runs) return plan | 1ull | (static_cast<std::uint64_t>(f16_runs) << 4) | f16_runs_packed;
+    return plan | (static_cast<std::uint64_t>(i8_runs) << 4) | i8_runs_packed;
+}
 
 struct Params {
     const __half* q;
@@ -196,23 +232,6 @@ struct BlockRoute {
     bool need_f16;
     bool need_i8;
 };
-
-__device__ __forceinline__ BlockRoute unpack_route(const RouteSlot& slot) {
-    BlockRoute r;
-    r.valid = slot.valid & 0xffffu;
-    r.ktiles = static_cast<int>((slot.valid >> 16) & 0xffu);
-    r.need_f16 = false;
-    r.need_i8 = false;
-    #pragma unroll
-    for (int kt = 0; kt < 4; ++kt) {
-        r.pat[kt] = static_cast<uint32_t>(slot.pats >> (16 * kt)) & 0xffffu;
-        if (kt < r.ktiles) {
-            r.need_i8 |= r.pat[kt] != 0;
-            r.need_f16 |= (~r.pat[kt] & r.valid) != 0;
-        }
-    }
-    return r;
-}
 
 // Lane l < 16 reads the words of query tile l for the four key tiles of a block.
 struct RoutePrefetch {
@@ -433,6 +452,19 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 for (int kt = 0; kt < 4; ++kt) slot.pats |= static_cast<std::uint64_t>(r.pat[kt] & 0xffffu) << (16 * kt);
                 slot.valid = (r.valid & 0xffffu) | (static_cast<uint32_t>(r.ktiles) << 16);
                 slot.scales = scales;
+                #pragma unroll
+                for (int t = 0; t < kTilesPerCta; ++t) {
+                    const uint32_t valid = (r.valid >> (8 * t)) & 0xffu;
+                    uint32_t i8set = 0, f16set = 0;
+                    #pragma unroll
+                    for (int kt = 0; kt < 4; ++kt) {
+                        if (kt < r.ktiles) {
+                            i8set |= ((r.pat[kt] >> (8 * t)) & valid) << (8 * kt);
+                            f16set |= (~(r.pat[kt] >> (8 * t)) & valid) << (8 * kt);
+                        }
+                    }
+                    slot.plan[t] = j < nblk[t] ? make_plan(i8set, f16set, r.ktiles) : 0ull;
+                }
                 ring[j % kRouteSlots] = slot;
                 mbar_arrive(bar(kBarRoute + j % kRouteSlots));   // release: slot visible to its waiters
             }
@@ -495,13 +527,14 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             if (!wait_bar(bar(kBarVFull + vs), (i / kVStages) & 1, abort_flag, kStatusMma)) return false;
             tc_fence_after();
             if (lane == 0) {
-                const uint32_t v_addr = sbase + L::kV + vs * L::kTileF16;
+                // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
+                // 8-key groups 1024 B apart; each K step covers 16 keys (2048 B).
+                // P_hi and P_lo of a 16-key step share the V operand.
+                const uint64_t v_desc = smem_desc_sw128(sbase + L::kV + vs * L::kTileF16, kAtomBytes, 1024);
                 const uint32_t p_tmem = tmem + col_s(t);
                 #pragma unroll
                 for (int s = 0; s < kTileKeys / 16; ++s) {
-                    // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
-                    // 8-key groups 1024 B apart; each K step covers 16 keys.
-                    const uint64_t b_desc = smem_desc_sw128(v_addr + s * 2048, kAtomBytes, 1024);
+                    const uint64_t b_desc = v_desc + static_cast<uint64_t>(s * 128);
                     const uint32_t a_hi = p_tmem + 32 * (s >> 1) + 8 * (s & 1);
                     mma_f16_ts(tmem + col_o(t), a_hi, b_desc, pv_idesc, (i > 0 || s > 0) ? 1u : 0u);
                     mma_f16_ts(tmem + col_o(t), a_hi + 16, b_desc, pv_idesc, 1u);
@@ -512,70 +545,42 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             return true;
         };
         // QK^T of tile t for block j into S_t.
-        auto issue_qk = [&](int t, const BlockRoute& r) {
-            const uint32_t s_tmem = tmem + col_s(t);
-            const uint64_t qf = smem_desc_sw128(sbase + L::kQ + t * L::kTileF16, 16, 1024);
-            const uint64_t qi = smem_desc_sw128(sbase + L::kQ8 + t * kAtomBytes, 16, 1024);
-            const uint64_t kf = smem_desc_sw128(sbase + L::kK, 16, 1024);
-            const uint64_t ki = smem_desc_sw128(sbase + L::kK8, 16, 1024);
-            const uint32_t valid = (r.valid >> (8 * t)) & 0xffu;
-            // Row sets per key tile packed one byte per key tile.
-            uint32_t i8set = 0, f16set = 0;
-            #pragma unroll
-            for (int kt = 0; kt < 4; ++kt) {
-                if (kt < r.ktiles) {
-                    i8set |= ((r.pat[kt] >> (8 * t)) & valid) << (8 * kt);
-                    f16set |= (~(r.pat[kt] >> (8 * t)) & valid) << (8 * kt);
+        // Descriptor bases (constant for the CTA: single K stage, fixed Q tiles).
+        const uint64_t kf = smem_desc_sw128(sbase + L::kK, 16, 1024);
+        const uint64_t ki = smem_desc_sw128(sbase + L::kK8, 16, 1024);
+        const uint32_t none[4] = {0u, 0u, 0u, 0u};
+        // One precision over key tiles [kt0, kt0 + nkt) of tile t; `off` masks
+        // the TMEM lanes (16-row tiles) that keep their previous result.
+        auto mma_run = [&](int t, bool int8, int kt0, int nkt, const uint32_t (&off)[4]) {
+            const uint32_t d_tmem = tmem + col_s(t) + 32 * kt0;
+            const uint64_t kofs = static_cast<uint64_t>(kt0 * 256);       // 4096 B per key tile, >> 4
+            if (int8) {
+                const uint64_t qi = smem_desc_sw128(sbase + L::kQ8 + t * kAtomBytes, 16, 1024);
+                const uint32_t idesc = idesc_s8_s32(kTileRows, 32 * nkt);
+                #pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    if (ks < p.i8_ksteps) mma_i8_ss(d_tmem, qi + 2 * ks, ki + kofs + 2 * ks, idesc, off, ks > 0 ? 1u : 0u);
+                }
+            } else {
+                const uint64_t qf = smem_desc_sw128(sbase + L::kQ + t * L::kTileF16, 16, 1024);
+                const uint32_t idesc = idesc_f16_f32(kTileRows, 32 * nkt, false);
+                #pragma unroll
+                for (int ks = 0; ks < 4 * kAtoms; ++ks) {
+                    const uint64_t ko = static_cast<uint64_t>((ks >> 2) * (kAtomBytes >> 4) + (ks & 3) * 2);
+                    if (ks < p.f16_ksteps) mma_f16_ss(d_tmem, qf + ko, kf + kofs + ko, idesc, off, ks > 0 ? 1u : 0u);
                 }
             }
-            // One precision over key tiles [kt0, kt0 + nkt), TMEM lanes of the
-            // 16-row tiles outside `rows` left untouched (descriptor start
-            // addresses advance by byte offset >> 4).
-            auto mma_run = [&](bool int8, uint32_t rows, int kt0, int nkt) {
+        };
+        // QK^T of tile t for a block, following the producer's plan.
+        auto issue_qk = [&](int t, std::uint64_t plan) {
+            const bool base_i8 = plan & 1ull;
+            mma_run(t, base_i8, 0, static_cast<int>((plan >> 1) & 7u), none);
+            const int overlays = static_cast<int>((plan >> 4) & 7u);
+            for (int i = 0; i < overlays; ++i) {
+                const uint32_t ov = static_cast<uint32_t>(plan >> (8 + 13 * i)) & 0x1fffu;
                 uint32_t off[4];
-                lane_mask(~rows & 0xffu, off);
-                const uint32_t d_tmem = s_tmem + 32 * kt0;
-                const uint64_t kofs = static_cast<uint64_t>(kt0 * 4096) >> 4;
-                if (int8) {
-                    const uint32_t idesc = idesc_s8_s32(kTileRows, 32 * nkt);
-                    for (int ks = 0; ks < p.i8_ksteps; ++ks) {
-                        mma_i8_ss(d_tmem, qi + 2 * ks, ki + kofs + 2 * ks, idesc, off, ks > 0 ? 1u : 0u);
-                    }
-                } else {
-                    const uint32_t idesc = idesc_f16_f32(kTileRows, 32 * nkt, false);
-                    for (int ks = 0; ks < p.f16_ksteps; ++ks) {
-                        const uint64_t ko = static_cast<uint64_t>((ks >> 2) * kAtomBytes + (ks & 3) * 32) >> 4;
-                        mma_f16_ss(d_tmem, qf + ko, kf + kofs + ko, idesc, off, ks > 0 ? 1u : 0u);
-                    }
-                }
-            };
-            // Overlay runs: maximal runs of key tiles whose row sets are equal and non-empty.
-            auto overlay_runs = [&](uint32_t sets, bool issue, bool int8) -> int {
-                int runs = 0, kt = 0;
-                while (kt < r.ktiles) {
-                    const uint32_t set = (sets >> (8 * kt)) & 0xffu;
-                    int end = kt + 1;
-                    while (end < r.ktiles && ((sets >> (8 * end)) & 0xffu) == set) ++end;
-                    if (set) {
-                        ++runs;
-                        if (issue) mma_run(int8, set, kt, end - kt);
-                    }
-                    kt = end;
-                }
-                return runs;
-            };
-            if (!i8set || !f16set) {
-                mma_run(i8set != 0, 0xffu, 0, r.ktiles);
-            } else {
-                const int f16_runs = overlay_runs(f16set, false, false);
-                const int i8_runs = overlay_runs(i8set, false, true);
-                if (f16_runs <= i8_runs) {        // INT8 base, FP16 overlays
-                    mma_run(true, 0xffu, 0, r.ktiles);
-                    overlay_runs(f16set, true, false);
-                } else {                          // FP16 base, INT8 overlays
-                    mma_run(false, 0xffu, 0, r.ktiles);
-                    overlay_runs(i8set, true, true);
-                }
+                lane_mask(~(ov >> 5) & 0xffu, off);
+                mma_run(t, !base_i8, static_cast<int>(ov & 3u), static_cast<int>((ov >> 2) & 7u), off);
             }
             tc_commit(bar(kBarSFull + t));
         };
@@ -585,7 +590,8 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 ok = false;
                 break;
             }
-            const BlockRoute r = unpack_route(ring[j % kRouteSlots]);
+            const std::uint64_t plan0 = ring[j % kRouteSlots].plan[0];
+            const std::uint64_t plan1 = ring[j % kRouteSlots].plan[1];
             bool k_ready = false;
             for (int t = 0; t < kTilesPerCta && ok; ++t) {
                 // PV of the previous block first: it only needs P and V, so the
@@ -597,7 +603,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                         tc_fence_after();
                         k_ready = true;
                     }
-                    if (lane == 0) issue_qk(t, r);
+                    if (lane == 0) issue_qk(t, t == 0 ? plan0 : plan1);
                     __syncwarp();
                 }
             }
