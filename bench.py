@@ -49,6 +49,8 @@ def parse_args():
     ap.add_argument("--p", type=float, default=None, help="override the INT8 routing fraction")
     ap.add_argument("--cpu-seconds", type=float, default=6.0,
                     help="target CPU time of one reference-arm sample")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: every rank runs a full batch; strong: the batch's heads are split over ranks")
     return ap.parse_args()
 
 
@@ -142,13 +144,8 @@ def dist_setup(args):
 
 
 def reduce_max(value: float, world: int) -> float:
-    if world == 1:
-        return value
-    import torch
-    import torch.distributed as dist
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from tilemix_b200 import sharding
+    return sharding.max_over_ranks(value, world, device="cuda")
 
 
 def barrier(world: int):
@@ -222,9 +219,19 @@ def run_tilemix(args, rank, world, local):
     import tilemix_b200 as tm
     from tilemix_b200 import workloads
 
+    from tilemix_b200 import sharding
     cfg0 = workloads.config(args.config, p=args.p)
-    w = workloads.make_inputs(args.config, p=args.p, seed=cfg0["seed"] + 1000 * rank, device="cuda")
+    total_heads = cfg0["B"] * cfg0["H"]
+    if args.scaling == "strong":
+        _, my_heads = sharding.shard_heads(total_heads, world, rank)
+        w = workloads.make_inputs(args.config, p=args.p, batch=1, heads=my_heads,
+                                  seed=sharding.rank_seed(cfg0["seed"], rank), device="cuda")
+    else:
+        w = workloads.make_inputs(args.config, p=args.p, seed=sharding.rank_seed(cfg0["seed"], rank),
+                                  device="cuda")
     cfg, H, S, D = w["cfg"], w["heads"], w["S"], w["D"]
+    job_flops = (world * workloads.effective_flops(cfg0) if args.scaling == "weak"
+                 else workloads.effective_flops(cfg0))
     q, k, v = w["q"], w["k"], w["v"]
     words = w["words"].cuda()
     q8 = torch.empty_like(q, dtype=torch.int8)
@@ -235,7 +242,7 @@ def run_tilemix(args, rank, world, local):
     routing = tm.TileMixRouting(words, words.numel(), 2)
     quantized = tm.TileMixQuantized(q8, k8, qs, ks)
     stream = torch.cuda.current_stream()
-    f_eff = workloads.effective_flops(cfg)
+    f_eff = workloads.effective_flops(cfg, H)       # this rank's work per step
     f_real = workloads.realised_int8_fraction(w["mask"], cfg["causal"])
 
     def quantize():
@@ -318,20 +325,20 @@ def run_tilemix(args, rank, world, local):
     achieved = f_eff / (attn_avg * 1e-3) / 1e12
     peak = peaks["bf16_tflops"]
     traffic_per_head = profiled_traffic().get(args.config)
-    value = world * f_eff / (step_ms * 1e-3) / 1e12
+    value = job_flops / (step_ms * 1e-3) / 1e12
     p_mix = workloads.mix_peak(f_eff, f_real) / 1e12
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": n, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16+i8 (f32 accumulate)", "data": "synthetic",
-        "config": {"workload": f"{args.config}: B{cfg['B']} H{cfg['H']} S{S} D{D}"
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f16+i8 (f32 accumulate)", "data": "synthetic",
+        "config": {"workload": f"{args.config}: B{cfg0['B']} H{cfg0['H']} S{S} D{D}"
                                f"{' causal' if cfg['causal'] else ''}, INT8 routing p={cfg['p']}"
                                f"{', x20 outlier channels' if cfg['outliers'] else ''}",
-                   "B": cfg["B"], "H": cfg["H"], "S": S, "D": D, "causal": cfg["causal"],
+                   "B": cfg0["B"], "H": cfg0["H"], "S": S, "D": D, "causal": cfg["causal"],
                    "int8_fraction_requested": cfg["p"], "int8_fraction_realised": round(f_real, 4),
-                   "per_gpu_heads": H, "parallelism": f"batch x head shards, {world} rank(s), no collective",
+                   "per_gpu_heads": H, "parallelism": f"batch x head shards ({args.scaling}), {world} rank(s), no collective",
                    "l2": f"inputs {3 * q.numel() * 2 / 2**20:.0f} MiB > L2 {L2_BYTES / 2**20:.0f} MiB; no flush"},
-        "pct_of_mix_peak": round(100 * value / world / p_mix, 2),
+        "pct_of_mix_peak": round(100 * (f_eff / (step_ms * 1e-3) / 1e12) / p_mix, 2),
         "mix_peak_tflops": round(p_mix, 1),
         "attention_ms": round(attn_avg, 4), "quantize_ms": round(quant_avg, 4),
         "quantize_gbs": round(3 * 2 * H * S * D / (quant_avg * 1e-3) / 1e9, 1),
@@ -341,7 +348,7 @@ def run_tilemix(args, rank, world, local):
                      "traffic": None if traffic_per_head is None else traffic_per_head * H,
                      "kernel": "tilemix_attention_kernel",
                      "work": "F_eff = 4*B*H*S^2*D/2 (causal) algorithmic FLOPs per launch"},
-        "e2e": {"value": round(world * f_eff / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+        "e2e": {"value": round(job_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
         "clocks": clk,
         "gpu_launches": 2 * n,
