@@ -16,31 +16,32 @@
 // running max only moved when it grows by more than 2^15 (the final result is
 // unchanged mathematically; P stays <= 32768, inside fp16's range).
 //
-// CTA = two 128-row query tiles (256 rows) of one head, 320 threads:
-//   warps 0-3  softmax of query tile 0   (thread t = query row t = TMEM lane t)
-//   warps 4-7  softmax of query tile 1
-//   warp 8     MMA issuer (one lane) + TMEM owner: S0 | S1 | O0 | O1
-//              (4 x 128 columns); QK^T of tile t into S_t, PV into O_t
+// CTA = one 128-row query tile of one head, 320 threads:
+//   warps 0-7  softmax: warp w serves TMEM lanes 32*(w%4).. (query rows) and
+//              the 64-key half (w/4) of every 128-key block, so each SM
+//              sub-partition runs two softmax warps on the same block; the
+//              halves exchange row maxima through shared memory
+//   warp 8     MMA issuer (one lane) + TMEM owner: S_a | S_b | O (384 of 512
+//              columns); S is double-buffered so QK of block j+2 runs while
+//              the softmax works on block j+1
 //   warp 9     producer: TMA (or, for head dims TMA cannot address, plain
-//              loads) of Q/Q8 for both tiles once, then per 128-key block
-//              K/K8 (one stage) and V (two stages), 128-byte swizzled
-// The MMA warp issues, per key block j:  PV(0, j-1), QK(0, j), PV(1, j-1),
-// QK(1, j).  Each tile's chain is QK -> softmax -> PV -> next QK, and the two
-// tiles' chains interleave on the tensor pipe, so one tile's softmax runs while
-// the other tile's MMAs execute ("ping-pong"). P overwrites S in TMEM (per
-// 32-key chunk: fp16 hi in the chunk's first 16 columns, lo in the last 16) and
-// is consumed by TMEM-A MMAs; the in-order tensor pipe guarantees PV(t, j-1)
-// reads P before QK(t, j) rewrites S.
+//              loads) of Q/Q8 once, then per 128-key block K/K8 and V (two
+//              stages each), 128-byte swizzled; publishes each block's
+//              routing summary, MMA plan and K scales in a shared-memory ring
+// MMA order: QK(0), QK(1), then per block j: PV(j) as soon as P(j) is
+// published, then QK(j+2) into the S buffer PV(j) just read (the in-order
+// tensor pipe guarantees PV(j) reads P before QK(j+2) overwrites it). P
+// overwrites S in TMEM (per 32-key chunk: fp16 hi in the chunk's first 16
+// columns, lo in the last 16) and is the TMEM A operand of the PV MMAs.
 //
-// Routing inside a 128-row tile: for each 32-key tile the 8 routing bits of
+// Routing inside the 128-row tile: for each 32-key tile the 8 routing bits of
 // the tile's 16-row query tiles select INT8 or FP16 per 16 rows. A uniform
 // block is one full-width MMA (N = 128) of its precision. A mixed block is one
 // full-width "base" MMA of one precision for all rows, then "overlay" MMAs of
 // the other precision over the key-tile runs that need it, with the TMEM lanes
 // of rows that keep the base result disabled (tcgen05.mma disable-output-lane);
 // the in-order tensor pipe makes the overlay overwrite the base exactly where
-// routed. The base precision is the one that leaves the fewer overlay runs
-// (narrow MMAs are shared-memory bound, so they cost nearly a full one).
+// routed.
 //
 // Every mbarrier wait is bounded (1 s of %globaltimer). A wait that runs out
 // records a code in g_tilemix_status, raises a CTA-wide abort flag and every
@@ -66,24 +67,25 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kTileRows = 128;               // rows per query tile (tcgen05 M)
-constexpr int kTilesPerCta = 2;
-constexpr int kCtaRows = kTileRows * kTilesPerCta;
+constexpr int kTileRows = 128;               // query rows per CTA (tcgen05 M)
 constexpr int kTileKeys = 128;               // keys per block
+constexpr int kKStages = 2;
 constexpr int kVStages = 2;
-constexpr int kRouteSlots = 8;               // producer runs at most ~2 blocks ahead
+constexpr int kRouteSlots = 8;               // the producer runs at most ~3 blocks ahead
+constexpr int kSoftmaxWarps = 8;
+constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
 constexpr int kMmaWarp = 8;
 constexpr int kProducerWarp = 9;
 constexpr int kAttnThreads = 320;
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 256;              // S_a at 0, S_b at 128, O at 256
 constexpr uint32_t kAtomBytes = 128 * 128;   // 128 rows x 128 bytes
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
-constexpr uint32_t kSuspendNs = 200000;        // per try_wait suspension (wakes early on completion)
+constexpr uint32_t kSuspendNs = 200000;      // per try_wait suspension (wakes early on completion)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 15.0f;        // rescale only when the max grows by > 2^15 (P <= 32768)
 
-__device__ __forceinline__ uint32_t col_s(int t) { return static_cast<uint32_t>(t) * 128u; }
-__device__ __forceinline__ uint32_t col_o(int t) { return 256u + static_cast<uint32_t>(t) * 128u; }
+__device__ __forceinline__ uint32_t col_s(int b) { return static_cast<uint32_t>(b) * 128u; }
 
 // Watchdog codes (bit positions say which wait gave up).
 enum : unsigned int {
@@ -93,16 +95,29 @@ enum : unsigned int {
     kStatusDrain = 1u << 3,
 };
 
+// Per-block routing summary published by the producer in a shared-memory ring
+// (global loads issued from the softmax loop proved far costlier than their
+// latency; only the producer touches the routing words and K scales):
+//   pats   bits [8 kt, 8 kt + 8): INT8 bit of the tile's 8 query tiles for key tile kt
+//   scales the block's two 64-key K scales (fp16, 0 when unrouted)
+//   plan   the block's QK MMA plan (see make_plan)
+struct RouteSlot {
+    uint32_t pats;
+    uint32_t scales;
+    std::uint64_t plan;
+};
+
 template <int kAtoms>
 struct SmemLayout {
     static constexpr uint32_t kTileF16 = kAtoms * kAtomBytes;
-    static constexpr uint32_t kQ = 0;                                   // [2 tiles] fp16
-    static constexpr uint32_t kQ8 = kQ + kTilesPerCta * kTileF16;       // [2 tiles] int8
-    static constexpr uint32_t kK = kQ8 + kTilesPerCta * kAtomBytes;     // one stage
-    static constexpr uint32_t kK8 = kK + kTileF16;
-    static constexpr uint32_t kV = kK8 + kAtomBytes;                    // [2 stages]
-    static constexpr uint32_t kRoute = kV + kVStages * kTileF16;      // [kRouteSlots] x 16 B
-    static constexpr uint32_t kBars = kRoute + kRouteSlots * 16;
+    static constexpr uint32_t kQ = 0;
+    static constexpr uint32_t kQ8 = kQ + kTileF16;
+    static constexpr uint32_t kK = kQ8 + kAtomBytes;                    // [2 stages] fp16
+    static constexpr uint32_t kK8 = kK + kKStages * kTileF16;          // [2 stages] int8
+    static constexpr uint32_t kV = kK8 + kKStages * kAtomBytes;        // [2 stages]
+    static constexpr uint32_t kRoute = kV + kVStages * kTileF16;       // [kRouteSlots]
+    static constexpr uint32_t kXchg = kRoute + kRouteSlots * sizeof(RouteSlot);  // [2][256] u64 pair handshake words
+    static constexpr uint32_t kBars = kXchg + 2 * kSoftmaxThreads * 8;
     static constexpr uint32_t kNumBars = 16 + kRouteSlots;
     static constexpr uint32_t kMisc = kBars + kNumBars * 8;            // tmem base, abort flag
     static constexpr uint32_t kEnd = kMisc + 16;
@@ -110,30 +125,16 @@ struct SmemLayout {
 };
 
 enum Bar : int {
-    kBarQFull = 0, kBarKFull = 1, kBarKEmpty = 2, kBarVFull = 3, kBarVEmpty = 5,
-    kBarSFull = 7, kBarPFull = 9, kBarPvDone = 11, kBarDrain = 13, kBarRoute = 16,
+    kBarQFull = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7,
+    kBarSFull = 9, kBarPFull = 11, kBarPvDone = 13, kBarDrain = 15, kBarRoute = 16,
 };
 
-// Per-block routing summary published by the producer in a shared-memory ring
-// (global loads issued from the softmax loop proved far costlier than their
-// latency; only the producer touches the routing words and K scales):
-//   pats   bits [16 kt, 16 kt + 16): INT8 bit of the CTA's 16 query tiles for key tile kt
-//   valid  bits [0,16) query tiles that exist and process the block, [16,24) key tiles
-//   scales the block's two 64-key K scales (fp16, 0 when unrouted)
-//   plan[t] the QK MMA plan of 128-row tile t (see make_plan)
-struct RouteSlot {
-    std::uint64_t pats;
-    uint32_t valid;
-    uint32_t scales;
-    std::uint64_t plan[2];
-};
-
-// QK plan of one 128-row tile for one key block, packed in 64 bits:
+// QK plan of the tile for one key block, packed in 64 bits:
 //   bit 0 base precision (1 = INT8), bits [1,4) base key tiles (0 = no QK),
 //   bits [4,7) overlay count, overlay i at bit 8 + 13 i: key tile (2 bits),
 //   key-tile count (3 bits), row-tile set (8 bits). Overlays are of the other
 //   precision and run after the base on the listed 16-row tiles only.
-__device__ __forceinline__ std::uint64_t make_plan(uint32_t i8set, uint32_t f16set, int ktiles) {
+__device__ __noinline__ std::uint64_t make_plan(uint32_t i8set, uint32_t f16set, int ktiles) {
     if (ktiles <= 0 || (i8set | f16set) == 0) return 0;
     auto runs_of = [&](uint32_t sets, std::uint64_t& packed) -> int {
         int runs = 0, kt = 0;
@@ -175,7 +176,7 @@ struct Params {
     std::uint8_t* decoded_bits;
     std::int32_t* score_dots;
     int heads, M, N, d;
-    int cta_tiles, kv_blocks, q16_tiles, k32_tiles;
+    int q_tiles, kv_blocks, q16_tiles, k32_tiles;
     int group;
     int words_per_row;
     long long words_per_head;
@@ -190,83 +191,99 @@ struct Params {
 
 // Bounded wait, called by all 32 lanes of a warp; returns a warp-uniform
 // verdict. On timeout it records `code` and raises the CTA abort flag.
+// Slow path of a bounded wait. Kept inline: an out-of-line call from the
+// divergent slow path broke the warp convergence that the warp-wide
+// (.sync.aligned) tcgen05 instructions after the wait rely on.
+__device__ __forceinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                           unsigned int code) {
+    const uint64_t start = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
+        if (*abort_flag) return false;
+        if (global_timer_ns() - start > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicOr(&g_tilemix_status, code);
+            return false;
+        }
+    }
+}
+
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                          unsigned int code) {
     bool ok = mbar_try_wait(bar, parity);
-    if (!ok) {
-        const uint64_t start = global_timer_ns();
-        while (true) {
-            if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) { ok = true; break; }
-            if (*abort_flag) break;
-            if (global_timer_ns() - start > kWaitLimitNs) {
-                *abort_flag = 1;
-                atomicOr(&g_tilemix_status, code);
-                break;
-            }
-        }
-    }
+    if (!ok) ok = wait_bar_slow(bar, parity, abort_flag, code);
     return __all_sync(0xffffffffu, ok);
 }
 
-// Routing words are read one key block ahead and decoded in the next
-// iteration: decoding right after the load would stall the in-order warp on
-// global-load latency every block.
-__device__ __forceinline__ std::uint64_t route_word(const Params& p, int head, int q16, int gkt) {
-    const long long group = gkt / p.group;
-    return __ldg(p.words + head * p.words_per_head + static_cast<long long>(q16) * p.words_per_row + group / 64);
-}
-
-__device__ __forceinline__ bool route_word_bit(const Params& p, std::uint64_t word, int gkt) {
-    const long long group = gkt / p.group;
-    return ((word >> (group % 64)) & 1ull) != 0;
-}
-
-// Routing summary of key block j for the CTA's 16 query tiles (8 per
-// 128-row tile), computed by a whole warp. pat[kt] bit l = INT8 for query
-// tile l and key tile kt; valid bit l = query tile l exists and its 128-row
-// tile processes block j. need_f16/need_i8 say which K operands block j needs.
-struct BlockRoute {
-    uint32_t pat[4];
-    uint32_t valid;
-    int ktiles;
-    bool need_f16;
-    bool need_i8;
-};
-
-// Lane l < 16 reads the words of query tile l for the four key tiles of a block.
-struct RoutePrefetch {
-    std::uint64_t w[4];
-
-    __device__ __forceinline__ void fetch(const Params& p, int head, int cta_tile, int j,
-                                          const int (&nblk)[2], uint32_t lane) {
-        const int q16 = cta_tile * (kCtaRows / 16) + static_cast<int>(lane);
-        const bool q_valid = lane < 16 && q16 < p.q16_tiles && j < nblk[(lane >> 3) & 1];
-        #pragma unroll
-        for (int kt = 0; kt < 4; ++kt) {
-            const int gkt = 4 * j + kt;
-            w[kt] = p.routed && q_valid && gkt < p.k32_tiles ? route_word(p, head, q16, gkt) : 0ull;
+// Handshake between the two softmax threads of a query row (threads t and
+// t ^ 128: same TMEM lane, other 64-key half). Each publishes (tag, value) as
+// one 64-bit shared-memory word, so value and tag are seen together, then
+// waits (bounded) for the partner's word with the same tag. Two slot sets
+// alternate by tag parity: a thread can only reuse a slot after it has read
+// the partner's next word, which the partner writes after reading this one.
+__device__ __forceinline__ bool pair_wait_slow(volatile std::uint64_t* slot, uint32_t tag, std::uint64_t& v,
+                                            volatile int* abort_flag) {
+    const uint64_t start = global_timer_ns();
+    while (true) {
+        v = *slot;
+        if (static_cast<uint32_t>(v >> 32) == tag) return true;
+        if (*abort_flag) return false;
+        if (global_timer_ns() - start > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicOr(&g_tilemix_status, kStatusSoftmax);
+            return false;
         }
     }
+}
 
-    __device__ __forceinline__ BlockRoute decode(const Params& p, int cta_tile, int j,
-                                                 const int (&nblk)[2], uint32_t lane) const {
-        BlockRoute r;
-        const int q16 = cta_tile * (kCtaRows / 16) + static_cast<int>(lane);
-        const bool q_valid = lane < 16 && q16 < p.q16_tiles && j < nblk[(lane >> 3) & 1];
-        r.valid = __ballot_sync(0xffffffffu, q_valid);
-        r.ktiles = min(4, p.k32_tiles - 4 * j);
-        r.need_f16 = false;
-        r.need_i8 = false;
-        #pragma unroll
-        for (int kt = 0; kt < 4; ++kt) {
-            const bool bit = q_valid && kt < r.ktiles && route_word_bit(p, w[kt], 4 * j + kt);
-            r.pat[kt] = __ballot_sync(0xffffffffu, bit);
-            if (kt < r.ktiles) {
-                r.need_i8 |= r.pat[kt] != 0;
-                r.need_f16 |= (~r.pat[kt] & r.valid) != 0;
-            }
-        }
-        return r;
+__device__ __forceinline__ bool pair_exchange(volatile std::uint64_t* slots, int me, uint32_t tag, float mine,
+                                              float& theirs, volatile int* abort_flag) {
+    slots[me] = (static_cast<std::uint64_t>(tag) << 32) | __float_as_uint(mine);
+    std::uint64_t v = slots[me ^ 128];
+    bool ok = static_cast<uint32_t>(v >> 32) == tag;
+    if (!ok) ok = pair_wait_slow(slots + (me ^ 128), tag, v, abort_flag);
+    theirs = __uint_as_float(static_cast<uint32_t>(v));
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Routing of one key block for the tile's 8 query tiles, one routing bit per
+// lane: lane = 8 * kt + l reads the word of query tile l for key tile kt of the
+// block, so a ballot yields the block's whole pattern (bit 8 kt + l = INT8 for
+// query tile l, key tile kt). Words and the block's two K scales are loaded
+// one block ahead and decoded in the next iteration: decoding right after the
+// load would stall the producer on global-load latency every block.
+struct RouteFetch {
+    const std::uint64_t* row;   // this lane's query tile's routing words
+    uint32_t kt;                // this lane's key tile within a block
+    bool q_ok;                  // this lane's query tile exists
+    std::uint64_t word;         // prefetched word
+    uint32_t bit;               // bit of the prefetched word
+    uint32_t scale;             // lanes 0, 1: prefetched K scale (fp16 bits) of the block's 64-key halves
+
+    __device__ __forceinline__ void init(const Params& p, int head, int qt, uint32_t lane) {
+        const int q16 = qt * (kTileRows / 16) + static_cast<int>(lane & 7u);
+        kt = lane >> 3;
+        q_ok = q16 < p.q16_tiles;
+        row = p.routed ? p.words + head * p.words_per_head + static_cast<long long>(q16) * p.words_per_row : nullptr;
+    }
+
+    __device__ __forceinline__ void fetch(const Params& p, int head, int j, int nblk, uint32_t lane) {
+        const uint32_t gkt = 4u * static_cast<uint32_t>(j) + kt;
+        const uint32_t group = p.routed ? gkt / static_cast<uint32_t>(p.group) : 0u;
+        bit = group & 63u;
+        word = p.routed && q_ok && j < nblk && gkt < static_cast<uint32_t>(p.k32_tiles) ? __ldg(row + (group >> 6)) : 0ull;
+        const int sb = 2 * j + static_cast<int>(lane);
+        scale = p.routed && lane < 2 && j < nblk && sb < p.k_scale_blocks
+                    ? __half_as_ushort(p.k_scales[static_cast<std::size_t>(head) * p.k_scale_blocks + sb]) : 0u;
+    }
+
+    // pats: INT8 bits; valid: bits of existing (query tile, key tile) pairs.
+    __device__ __forceinline__ void decode(const Params& p, int j, uint32_t& pats, uint32_t& valid,
+                                           uint32_t& scales) const {
+        const bool ok = q_ok && 4 * j + static_cast<int>(kt) < p.k32_tiles;
+        valid = __ballot_sync(0xffffffffu, ok);
+        pats = __ballot_sync(0xffffffffu, ok && ((word >> bit) & 1ull) != 0);
+        scales = __shfl_sync(0xffffffffu, scale, 0) | (__shfl_sync(0xffffffffu, scale, 1) << 16);
     }
 };
 
@@ -324,12 +341,6 @@ __device__ void manual_tile_i8(uint8_t* dst, const std::int8_t* src, int row0, i
     }
 }
 
-// Exact s32 -> f32 for |x| < 2^22 (|dot| <= 127^2 * 128 < 2^22): add the
-// 1.5 * 2^23 bias in the integer domain, subtract it in fp32.
-__device__ __forceinline__ float s32_to_f32(uint32_t x) {
-    return __uint_as_float(x + 0x4B400000u) - 12582912.0f;
-}
-
 template <int kAtoms, bool kUseTma, bool kTrace>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -352,39 +363,34 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     const uint32_t lane = threadIdx.x & 31u;
 
     // Work item: heads are scheduled in groups (their K/V stay in L2 while the
-    // group runs); inside a group the heaviest (last) 256-row tiles go first.
+    // group runs); inside a group the heaviest (last) query tiles go first.
     const int bid = static_cast<int>(blockIdx.x);
-    const int per_group = p.head_group * p.cta_tiles;
+    const int per_group = p.head_group * p.q_tiles;
     const int group0 = (bid / per_group) * p.head_group;
     const int group_heads = min(p.head_group, p.heads - group0);
     const int in_group = bid - (bid / per_group) * per_group;
-    const int cta_tile = p.cta_tiles - 1 - in_group / group_heads;
+    const int qt = p.q_tiles - 1 - in_group / group_heads;
     const int head = group0 + in_group % group_heads;
-    int nblk[2];
-    #pragma unroll
-    for (int t = 0; t < kTilesPerCta; ++t) {
-        const int qt = cta_tile * kTilesPerCta + t;             // 128-row tile index
-        const bool exists = qt * kTileRows < p.M;
-        nblk[t] = !exists ? 0 : (p.causal ? min(p.kv_blocks, qt + 1) : p.kv_blocks);
-    }
-    const int nblk_max = max(nblk[0], nblk[1]);
+    const int nblk = p.causal ? min(p.kv_blocks, qt + 1) : p.kv_blocks;
     const int load_i8 = p.routed;
 
     if (threadIdx.x == 0) {
         mbar_init(bar(kBarQFull), 1);
-        mbar_init(bar(kBarKFull), 1);
-        mbar_init(bar(kBarKEmpty), 1);
+        for (int s = 0; s < kKStages; ++s) { mbar_init(bar(kBarKFull + s), 1); mbar_init(bar(kBarKEmpty + s), 1); }
         for (int s = 0; s < kVStages; ++s) { mbar_init(bar(kBarVFull + s), 1); mbar_init(bar(kBarVEmpty + s), 1); }
-        for (int t = 0; t < kTilesPerCta; ++t) {
-            mbar_init(bar(kBarSFull + t), 1);
-            mbar_init(bar(kBarPFull + t), 128);
-            mbar_init(bar(kBarPvDone + t), 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bar(kBarSFull + b), 1);
+            mbar_init(bar(kBarPFull + b), kSoftmaxThreads);
+            mbar_init(bar(kBarPvDone + b), 1);
         }
         mbar_init(bar(kBarDrain), 1);
         for (int r = 0; r < kRouteSlots; ++r) mbar_init(bar(kBarRoute + r), 1);
         *abort_flag = 0;
         mbar_init_fence();
         fence_proxy_async_smem();
+    }
+    for (int i = threadIdx.x; i < 2 * kSoftmaxThreads; i += kAttnThreads) {
+        reinterpret_cast<std::uint64_t*>(smem + L::kXchg)[i] = ~0ull;    // no tag matches
     }
     if (warp == kMmaWarp) {
         tmem_alloc(sbase + L::kMisc, kTmemCols);
@@ -405,98 +411,71 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         const std::size_t kv_off = static_cast<std::size_t>(head) * p.N * p.d;
         if (kUseTma) {
             if (lane == 0) {
-                uint32_t bytes = 0;
-                for (int t = 0; t < kTilesPerCta; ++t) {
-                    if (nblk[t] > 0) bytes += L::kTileF16 + (load_i8 ? kAtomBytes : 0u);
+                mbar_arrive_expect_tx(bar(kBarQFull), L::kTileF16 + (load_i8 ? kAtomBytes : 0u));
+                for (int a = 0; a < kAtoms; ++a) {
+                    tma_load_3d(sbase + L::kQ + a * kAtomBytes, &tm_q, bar(kBarQFull), a * 64, qt * kTileRows, head);
                 }
-                mbar_arrive_expect_tx(bar(kBarQFull), bytes);
-                for (int t = 0; t < kTilesPerCta; ++t) {
-                    if (nblk[t] == 0) continue;
-                    const int row0 = (cta_tile * kTilesPerCta + t) * kTileRows;
-                    for (int a = 0; a < kAtoms; ++a) {
-                        tma_load_3d(sbase + L::kQ + t * L::kTileF16 + a * kAtomBytes, &tm_q, bar(kBarQFull),
-                                    a * 64, row0, head);
-                    }
-                    if (load_i8) tma_load_3d(sbase + L::kQ8 + t * kAtomBytes, &tm_q8, bar(kBarQFull), 0, row0, head);
-                }
+                if (load_i8) tma_load_3d(sbase + L::kQ8, &tm_q8, bar(kBarQFull), 0, qt * kTileRows, head);
             }
         } else {
-            for (int t = 0; t < kTilesPerCta; ++t) {
-                if (nblk[t] == 0) continue;
-                const int row0 = (cta_tile * kTilesPerCta + t) * kTileRows;
-                manual_tile_f16(smem + L::kQ + t * L::kTileF16, p.q + q_off, row0, p.M, p.d, kAtoms, lane);
-                if (load_i8) manual_tile_i8(smem + L::kQ8 + t * kAtomBytes, p.q8 + q_off, row0, p.M, p.d, lane);
-            }
+            manual_tile_f16(smem + L::kQ, p.q + q_off, qt * kTileRows, p.M, p.d, kAtoms, lane);
+            if (load_i8) manual_tile_i8(smem + L::kQ8, p.q8 + q_off, qt * kTileRows, p.M, p.d, lane);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarQFull));
         }
-        int k_issued = 0, v_issued = 0;
-        RoutePrefetch pre;
-        pre.fetch(p, head, cta_tile, 0, nblk, lane);
-        const __half* k_scales = p.routed ? p.k_scales + static_cast<std::size_t>(head) * p.k_scale_blocks : nullptr;
+        RouteFetch route;
+        route.init(p, head, qt, lane);
+        route.fetch(p, head, 0, nblk, lane);
         RouteSlot* ring = reinterpret_cast<RouteSlot*>(smem + L::kRoute);
-        for (int j = 0; j < nblk_max; ++j) {
-            const BlockRoute r = pre.decode(p, cta_tile, j, nblk, lane);
-            pre.fetch(p, head, cta_tile, j + 1, nblk, lane);
+        int k_issued = 0, v_issued = 0;
+        for (int j = 0; j < nblk; ++j) {
+            uint32_t pats, valid, scales;
+            route.decode(p, j, pats, valid, scales);
+            route.fetch(p, head, j + 1, nblk, lane);
+            const bool need_i8 = pats != 0;
+            const bool need_f16 = (valid & ~pats) != 0;
             if (lane == 0) {
-                uint32_t scales = 0;
-                if (p.routed) {
-                    const uint32_t s0 = 2 * j < p.k_scale_blocks ? __half_as_ushort(k_scales[2 * j]) : 0u;
-                    const uint32_t s1 = 2 * j + 1 < p.k_scale_blocks ? __half_as_ushort(k_scales[2 * j + 1]) : 0u;
-                    scales = s0 | (s1 << 16);
-                }
                 RouteSlot slot;
-                slot.pats = 0;
-                #pragma unroll
-                for (int kt = 0; kt < 4; ++kt) slot.pats |= static_cast<std::uint64_t>(r.pat[kt] & 0xffffu) << (16 * kt);
-                slot.valid = (r.valid & 0xffffu) | (static_cast<uint32_t>(r.ktiles) << 16);
+                slot.pats = pats;
                 slot.scales = scales;
-                #pragma unroll
-                for (int t = 0; t < kTilesPerCta; ++t) {
-                    const uint32_t valid = (r.valid >> (8 * t)) & 0xffu;
-                    uint32_t i8set = 0, f16set = 0;
-                    #pragma unroll
-                    for (int kt = 0; kt < 4; ++kt) {
-                        if (kt < r.ktiles) {
-                            i8set |= ((r.pat[kt] >> (8 * t)) & valid) << (8 * kt);
-                            f16set |= (~(r.pat[kt] >> (8 * t)) & valid) << (8 * kt);
-                        }
-                    }
-                    slot.plan[t] = j < nblk[t] ? make_plan(i8set, f16set, r.ktiles) : 0ull;
-                }
+                slot.plan = make_plan(pats, valid & ~pats, min(4, p.k32_tiles - 4 * j));
                 ring[j % kRouteSlots] = slot;
                 mbar_arrive(bar(kBarRoute + j % kRouteSlots));   // release: slot visible to its waiters
             }
             __syncwarp();
-            if (!wait_bar(bar(kBarKEmpty), (j & 1) ^ 1, abort_flag, kStatusProducer)) break;
+            const int ks = j % kKStages;
+            if (!wait_bar(bar(kBarKEmpty + ks), ((j / kKStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
             if (kUseTma) {
                 if (lane == 0) {
-                    const uint32_t bytes = (r.need_f16 ? L::kTileF16 : 0u) + (r.need_i8 ? kAtomBytes : 0u);
-                    mbar_arrive_expect_tx(bar(kBarKFull), bytes);
-                    if (r.need_f16) {
+                    const uint32_t bytes = (need_f16 ? L::kTileF16 : 0u) + (need_i8 ? kAtomBytes : 0u);
+                    mbar_arrive_expect_tx(bar(kBarKFull + ks), bytes);
+                    if (need_f16) {
                         for (int a = 0; a < kAtoms; ++a) {
-                            tma_load_3d(sbase + L::kK + a * kAtomBytes, &tm_k, bar(kBarKFull), a * 64, j * kTileKeys, head);
+                            tma_load_3d(sbase + L::kK + ks * L::kTileF16 + a * kAtomBytes, &tm_k, bar(kBarKFull + ks),
+                                        a * 64, j * kTileKeys, head);
                         }
                     }
-                    if (r.need_i8) tma_load_3d(sbase + L::kK8, &tm_k8, bar(kBarKFull), 0, j * kTileKeys, head);
+                    if (need_i8) {
+                        tma_load_3d(sbase + L::kK8 + ks * kAtomBytes, &tm_k8, bar(kBarKFull + ks), 0, j * kTileKeys, head);
+                    }
                 }
             } else {
-                if (r.need_f16) manual_tile_f16(smem + L::kK, p.k + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
-                if (r.need_i8) manual_tile_i8(smem + L::kK8, p.k8 + kv_off, j * kTileKeys, p.N, p.d, lane);
+                if (need_f16) manual_tile_f16(smem + L::kK + ks * L::kTileF16, p.k + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
+                if (need_i8) manual_tile_i8(smem + L::kK8 + ks * kAtomBytes, p.k8 + kv_off, j * kTileKeys, p.N, p.d, lane);
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar(kBarKFull));
+                if (lane == 0) mbar_arrive(bar(kBarKFull + ks));
             }
             k_issued = j + 1;
             const int vs = j % kVStages;
             if (!wait_bar(bar(kBarVEmpty + vs), ((j / kVStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
-            const uint32_t v_dst = sbase + L::kV + vs * L::kTileF16;
             if (kUseTma) {
                 if (lane == 0) {
                     mbar_arrive_expect_tx(bar(kBarVFull + vs), L::kTileF16);
                     for (int a = 0; a < kAtoms; ++a) {
-                        tma_load_3d(v_dst + a * kAtomBytes, &tm_v, bar(kBarVFull + vs), a * 64, j * kTileKeys, head);
+                        tma_load_3d(sbase + L::kV + vs * L::kTileF16 + a * kAtomBytes, &tm_v, bar(kBarVFull + vs),
+                                    a * 64, j * kTileKeys, head);
                     }
                 }
             } else {
@@ -511,7 +490,9 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         // CTA may exit (normally long complete; matters only after an abort).
         if (kUseTma) {
             wait_bar(bar(kBarQFull), 0, abort_flag, kStatusDrain);
-            if (k_issued > 0) wait_bar(bar(kBarKFull), (k_issued - 1) & 1, abort_flag, kStatusDrain);
+            for (int j = max(0, k_issued - kKStages); j < k_issued; ++j) {
+                wait_bar(bar(kBarKFull + j % kKStages), (j / kKStages) & 1, abort_flag, kStatusDrain);
+            }
             for (int j = max(0, v_issued - kVStages); j < v_issued; ++j) {
                 wait_bar(bar(kBarVFull + j % kVStages), (j / kVStages) & 1, abort_flag, kStatusDrain);
             }
@@ -519,128 +500,117 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     } else if (warp == kMmaWarp) {
         // ----------------------------------------------------------------- MMA
         const uint32_t pv_idesc = idesc_f16_f32(kTileRows, p.pv_n, true);
+        const RouteSlot* ring = reinterpret_cast<const RouteSlot*>(smem + L::kRoute);
+        const uint64_t qf = smem_desc_sw128(sbase + L::kQ, 16, 1024);
+        const uint64_t qi = smem_desc_sw128(sbase + L::kQ8, 16, 1024);
         bool ok = wait_bar(bar(kBarQFull), 0, abort_flag, kStatusMma);
-        // PV of tile t for block i: O_t (+)= (P_hi + P_lo) V_i.
-        auto issue_pv = [&](int t, int i) -> bool {
-            if (!wait_bar(bar(kBarPFull + t), i & 1, abort_flag, kStatusMma)) return false;
-            const int vs = i % kVStages;
-            if (!wait_bar(bar(kBarVFull + vs), (i / kVStages) & 1, abort_flag, kStatusMma)) return false;
+        // One precision over key tiles [kt0, kt0 + nkt) of block j; `off` masks
+        // the TMEM lanes (16-row tiles) that keep their previous result.
+        // Descriptor start addresses advance by byte offset >> 4.
+        auto mma_run = [&](uint32_t d_tmem, int ks_stage, bool int8, int kt0, int nkt, const uint32_t (&off)[4]) {
+            const uint32_t d = d_tmem + 32 * kt0;
+            const uint64_t kofs = static_cast<uint64_t>(kt0 * 256);       // 4096 B per key tile
+            if (int8) {
+                const uint64_t ki = smem_desc_sw128(sbase + L::kK8 + ks_stage * kAtomBytes, 16, 1024);
+                const uint32_t idesc = idesc_s8_s32(kTileRows, 32 * nkt);
+                #pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    if (ks < p.i8_ksteps) mma_i8_ss(d, qi + 2 * ks, ki + kofs + 2 * ks, idesc, off, ks > 0 ? 1u : 0u);
+                }
+            } else {
+                const uint64_t kf = smem_desc_sw128(sbase + L::kK + ks_stage * L::kTileF16, 16, 1024);
+                const uint32_t idesc = idesc_f16_f32(kTileRows, 32 * nkt, false);
+                #pragma unroll
+                for (int ks = 0; ks < 4 * kAtoms; ++ks) {
+                    const uint64_t ko = static_cast<uint64_t>((ks >> 2) * (kAtomBytes >> 4) + (ks & 3) * 2);
+                    if (ks < p.f16_ksteps) mma_f16_ss(d, qf + ko, kf + kofs + ko, idesc, off, ks > 0 ? 1u : 0u);
+                }
+            }
+        };
+        // QK^T of block j into S[j % 2], following the producer's plan.
+        auto issue_qk = [&](int j) -> bool {
+            if (!wait_bar(bar(kBarRoute + j % kRouteSlots), (j / kRouteSlots) & 1, abort_flag, kStatusMma)) return false;
+            const std::uint64_t plan = ring[j % kRouteSlots].plan;
+            const int ks = j % kKStages;
+            if (!wait_bar(bar(kBarKFull + ks), (j / kKStages) & 1, abort_flag, kStatusMma)) return false;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t s_tmem = tmem + col_s(j & 1);
+                const bool base_i8 = plan & 1ull;
+                const int runs = 1 + static_cast<int>((plan >> 4) & 7u);
+                #pragma unroll 1
+                for (int r = 0; r < runs; ++r) {
+                    bool int8 = base_i8;
+                    int kt0 = 0, nkt = static_cast<int>((plan >> 1) & 7u);
+                    uint32_t off[4] = {0u, 0u, 0u, 0u};
+                    if (r > 0) {
+                        const uint32_t ov = static_cast<uint32_t>(plan >> (8 + 13 * (r - 1))) & 0x1fffu;
+                        int8 = !base_i8;
+                        kt0 = static_cast<int>(ov & 3u);
+                        nkt = static_cast<int>((ov >> 2) & 7u);
+                        lane_mask(~(ov >> 5) & 0xffu, off);
+                    }
+                    mma_run(s_tmem, ks, int8, kt0, nkt, off);
+                }
+                tc_commit(bar(kBarKEmpty + ks));
+                tc_commit(bar(kBarSFull + (j & 1)));
+            }
+            __syncwarp();
+            return true;
+        };
+        // PV of block j: O (+)= (P_hi + P_lo) V_j.
+        auto issue_pv = [&](int j) -> bool {
+            if (!wait_bar(bar(kBarPFull + (j & 1)), (j >> 1) & 1, abort_flag, kStatusMma)) return false;
+            const int vs = j % kVStages;
+            if (!wait_bar(bar(kBarVFull + vs), (j / kVStages) & 1, abort_flag, kStatusMma)) return false;
             tc_fence_after();
             if (lane == 0) {
                 // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
                 // 8-key groups 1024 B apart; each K step covers 16 keys (2048 B).
                 // P_hi and P_lo of a 16-key step share the V operand.
                 const uint64_t v_desc = smem_desc_sw128(sbase + L::kV + vs * L::kTileF16, kAtomBytes, 1024);
-                const uint32_t p_tmem = tmem + col_s(t);
+                const uint32_t p_tmem = tmem + col_s(j & 1);
                 #pragma unroll
                 for (int s = 0; s < kTileKeys / 16; ++s) {
                     const uint64_t b_desc = v_desc + static_cast<uint64_t>(s * 128);
                     const uint32_t a_hi = p_tmem + 32 * (s >> 1) + 8 * (s & 1);
-                    mma_f16_ts(tmem + col_o(t), a_hi, b_desc, pv_idesc, (i > 0 || s > 0) ? 1u : 0u);
-                    mma_f16_ts(tmem + col_o(t), a_hi + 16, b_desc, pv_idesc, 1u);
+                    mma_f16_ts(tmem + kColO, a_hi, b_desc, pv_idesc, (j > 0 || s > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem + kColO, a_hi + 16, b_desc, pv_idesc, 1u);
                 }
-                tc_commit(bar(kBarPvDone + t));
+                tc_commit(bar(kBarVEmpty + vs));
+                tc_commit(bar(kBarPvDone + (j & 1)));
             }
             __syncwarp();
             return true;
         };
-        // QK^T of tile t for block j into S_t.
-        // Descriptor bases (constant for the CTA: single K stage, fixed Q tiles).
-        const uint64_t kf = smem_desc_sw128(sbase + L::kK, 16, 1024);
-        const uint64_t ki = smem_desc_sw128(sbase + L::kK8, 16, 1024);
-        const uint32_t none[4] = {0u, 0u, 0u, 0u};
-        // One precision over key tiles [kt0, kt0 + nkt) of tile t; `off` masks
-        // the TMEM lanes (16-row tiles) that keep their previous result.
-        auto mma_run = [&](int t, bool int8, int kt0, int nkt, const uint32_t (&off)[4]) {
-            const uint32_t d_tmem = tmem + col_s(t) + 32 * kt0;
-            const uint64_t kofs = static_cast<uint64_t>(kt0 * 256);       // 4096 B per key tile, >> 4
-            if (int8) {
-                const uint64_t qi = smem_desc_sw128(sbase + L::kQ8 + t * kAtomBytes, 16, 1024);
-                const uint32_t idesc = idesc_s8_s32(kTileRows, 32 * nkt);
-                #pragma unroll
-                for (int ks = 0; ks < 4; ++ks) {
-                    if (ks < p.i8_ksteps) mma_i8_ss(d_tmem, qi + 2 * ks, ki + kofs + 2 * ks, idesc, off, ks > 0 ? 1u : 0u);
-                }
-            } else {
-                const uint64_t qf = smem_desc_sw128(sbase + L::kQ + t * L::kTileF16, 16, 1024);
-                const uint32_t idesc = idesc_f16_f32(kTileRows, 32 * nkt, false);
-                #pragma unroll
-                for (int ks = 0; ks < 4 * kAtoms; ++ks) {
-                    const uint64_t ko = static_cast<uint64_t>((ks >> 2) * (kAtomBytes >> 4) + (ks & 3) * 2);
-                    if (ks < p.f16_ksteps) mma_f16_ss(d_tmem, qf + ko, kf + kofs + ko, idesc, off, ks > 0 ? 1u : 0u);
-                }
-            }
-        };
-        // QK^T of tile t for a block, following the producer's plan.
-        auto issue_qk = [&](int t, std::uint64_t plan) {
-            const bool base_i8 = plan & 1ull;
-            mma_run(t, base_i8, 0, static_cast<int>((plan >> 1) & 7u), none);
-            const int overlays = static_cast<int>((plan >> 4) & 7u);
-            for (int i = 0; i < overlays; ++i) {
-                const uint32_t ov = static_cast<uint32_t>(plan >> (8 + 13 * i)) & 0x1fffu;
-                uint32_t off[4];
-                lane_mask(~(ov >> 5) & 0xffu, off);
-                mma_run(t, !base_i8, static_cast<int>(ov & 3u), static_cast<int>((ov >> 2) & 7u), off);
-            }
-            tc_commit(bar(kBarSFull + t));
-        };
-        const RouteSlot* ring = reinterpret_cast<const RouteSlot*>(smem + L::kRoute);
-        for (int j = 0; ok && j < nblk_max; ++j) {
-            if (!wait_bar(bar(kBarRoute + j % kRouteSlots), (j / kRouteSlots) & 1, abort_flag, kStatusMma)) {
-                ok = false;
-                break;
-            }
-            const std::uint64_t plan0 = ring[j % kRouteSlots].plan[0];
-            const std::uint64_t plan1 = ring[j % kRouteSlots].plan[1];
-            bool k_ready = false;
-            for (int t = 0; t < kTilesPerCta && ok; ++t) {
-                // PV of the previous block first: it only needs P and V, so the
-                // load of this block's K is off the tensor pipe's critical path.
-                if (j > 0 && j - 1 < nblk[t] && !issue_pv(t, j - 1)) { ok = false; break; }
-                if (j < nblk[t]) {
-                    if (!k_ready) {
-                        if (!wait_bar(bar(kBarKFull), j & 1, abort_flag, kStatusMma)) { ok = false; break; }
-                        tc_fence_after();
-                        k_ready = true;
-                    }
-                    if (lane == 0) issue_qk(t, t == 0 ? plan0 : plan1);
-                    __syncwarp();
-                }
-            }
-            if (!ok) break;
-            if (lane == 0) {
-                tc_commit(bar(kBarKEmpty));
-                if (j > 0) tc_commit(bar(kBarVEmpty + (j - 1) % kVStages));
-            }
-            __syncwarp();
-        }
-        if (ok && nblk_max > 0) {
-            for (int t = 0; t < kTilesPerCta && ok; ++t) {
-                if (nblk_max - 1 < nblk[t]) ok = issue_pv(t, nblk_max - 1);
-            }
-            if (ok && lane == 0) tc_commit(bar(kBarVEmpty + (nblk_max - 1) % kVStages));
-            __syncwarp();
+        // QK(0), QK(1), then PV(j), QK(j + 2) for each block j (one call site
+        // per lambda keeps this warp's code small).
+        for (int j = -2; ok && j < nblk; ++j) {
+            if (j >= 0 && !issue_pv(j)) { ok = false; break; }
+            if (j + 2 < nblk && !issue_qk(j + 2)) { ok = false; break; }
         }
         // Drain every MMA this thread issued before TMEM can be released.
         if (lane == 0) tc_commit(bar(kBarDrain));
         __syncwarp();
         wait_bar(bar(kBarDrain), 0, abort_flag, kStatusDrain);
-    } else if (warp < 8) {
+    } else if (warp < kSoftmaxWarps) {
         // ------------------------------------------------------------- softmax
-        // Two passes over the 128-column S row in 32-column TMEM chunks (the
-        // next chunk's load overlaps the current chunk's math): pass 1
-        // dequantises INT8 chunks into raw fp32 units, applies the key mask on
-        // edge blocks, writes modified chunks back and takes the row max;
-        // pass 2 exponentiates and writes P (hi, lo) over the chunk.
-        const int t = warp >> 2;                                     // query tile
-        const int row = static_cast<int>(threadIdx.x) - 128 * t;     // TMEM lane
+        // Thread = (query row, 64-key half). Each thread reads its row's whole
+        // 128-key block from TMEM (four 32-column chunks) and takes the row
+        // max itself (integer max of the s32 dots on INT8 chunks, scaled once),
+        // so the two halves of a row agree on the max without exchanging it;
+        // it then exponentiates only its own two chunks and writes P (hi, lo)
+        // over them. Precision choices are per 16-row query tile, so a warp
+        // (32 rows) can mix INT8 and FP16 chunks: the code paths branch on
+        // warp votes, never per lane.
+        const int half = warp >> 2;                                  // key half of every block
+        const int row = (warp & 3) * 32 + static_cast<int>(lane);    // TMEM lane = query row
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-        const int qt = cta_tile * kTilesPerCta + t;
         const int q_row = qt * kTileRows + row;
         const bool row_valid = q_row < p.M;
         const int q16 = qt * (kTileRows / 16) + row / 16;
         const bool q16_valid = q16 < p.q16_tiles;
-        const float q_scale = p.routed && nblk[t] > 0 ? __half2float(p.q_scales[head * p.q_scale_blocks + qt]) : 0.0f;
+        const float q_scale = p.routed ? __half2float(p.q_scales[head * p.q_scale_blocks + qt]) : 0.0f;
         // Scores are kept in "raw" units r with score_log2 = r * c_exp: FP16
         // tiles give r = q.k directly when score_scale > 0 (no multiply); INT8
         // tiles give r = dot * q_scale * k_scale.
@@ -648,208 +618,228 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         const float c_exp = pos_scale ? p.scale_log2 : 1.0f;
         const float a_f16 = pos_scale ? 1.0f : p.scale_log2;
         const float threshold = kRescaleLog2 / c_exp;
-        float m_run = -INFINITY;    // running max (raw units), possibly stale by < 2^8 in p
-        float l_run = 0.0f;
-        bool ok = true;
-        const uint32_t s_addr = tmem + lane_base + col_s(t);
-        const uint32_t o_addr = tmem + lane_base + col_o(t);
         const RouteSlot* ring = reinterpret_cast<const RouteSlot*>(smem + L::kRoute);
-        const int qlocal = 8 * t + row / 16;                          // query tile within the CTA
-        uint32_t bufa[32], bufb[32];
-        for (int j = 0; j < nblk[t]; ++j) {
-            // The route slot of block j was published before its K load, so it
-            // is complete by the time S is; the wait only orders the read.
+        const int qlocal = row / 16;
+        float m_run = -INFINITY;    // running max (raw units), possibly stale by < 2^15 in p
+        float l_run = 0.0f;         // this half's share of the row sum
+        bool ok = true;
+        const uint32_t o_addr = tmem + lane_base + kColO + 64u * half;
+        volatile std::uint64_t* xchg = reinterpret_cast<volatile std::uint64_t*>(smem + L::kXchg);
+        const int me = static_cast<int>(threadIdx.x);
+        uint32_t xa[32], xb[32];
+        for (int j = 0; j < nblk; ++j) {
+            const int b = j & 1;
+            const uint32_t s_row = tmem + lane_base + col_s(b);
+            const uint32_t s_own = s_row + 64u * half;
             if (!wait_bar(bar(kBarRoute + j % kRouteSlots), (j / kRouteSlots) & 1, abort_flag, kStatusSoftmax)) {
                 ok = false;
                 break;
             }
             const RouteSlot slot = ring[j % kRouteSlots];
-            uint32_t bits = 0;
-            #pragma unroll
-            for (int kt = 0; kt < 4; ++kt) {
-                bits |= static_cast<uint32_t>((slot.pats >> (16 * kt + qlocal)) & 1ull) << kt;
-            }
-            if (!q16_valid) bits = 0;
-            const float ks0 = __half2float(__ushort_as_half(static_cast<unsigned short>(slot.scales & 0xffffu)));
-            const float ks1 = __half2float(__ushort_as_half(static_cast<unsigned short>(slot.scales >> 16)));
-            if (!wait_bar(bar(kBarSFull + t), j & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
-            tc_fence_after();
-            const int key0 = j * kTileKeys;
-            const bool edge = key0 + kTileKeys > p.N || (p.causal && key0 + kTileKeys > q_row);
-            const int limit = p.causal ? min(p.N, q_row + 1) : p.N;
-            // ---- pass 1: row max in raw units. INT8 chunks take an integer
-            // max of the s32 dots (scales are >= 0 when score_scale > 0) and
-            // scale it once; blocks that touch the key mask, and score_scale
-            // <= 0, take the general per-element path.
-            const bool fast = pos_scale && !edge;
-            float mx0 = -INFINITY, mx1 = -INFINITY;
-            auto pass1 = [&](const uint32_t (&x)[32], int c) {
-                const bool is_i8 = (bits >> c) & 1u;
-                const float ratio = is_i8 ? q_scale * (c < 2 ? ks0 : ks1) * a_f16 : a_f16;
-                if (kTrace && p.score_dots && row_valid && is_i8) {
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int key = key0 + c * 32 + i;
-                        if (key < p.N) {
-                            p.score_dots[(static_cast<std::size_t>(head) * p.M + q_row) * p.N + key] =
-                                static_cast<int32_t>(x[i]);
-                        }
-                    }
-                }
-                if (fast) {
-                    if (is_i8) {
-                        int i0 = static_cast<int>(x[0]), i1 = static_cast<int>(x[1]);
-                        #pragma unroll
-                        for (int i = 2; i < 32; i += 2) {
-                            i0 = max(i0, static_cast<int>(x[i]));
-                            i1 = max(i1, static_cast<int>(x[i + 1]));
-                        }
-                        mx0 = fmaxf(mx0, static_cast<float>(max(i0, i1)) * ratio);
-                    } else {
-                        #pragma unroll
-                        for (int i = 0; i < 32; i += 2) {
-                            mx0 = fmaxf(mx0, __uint_as_float(x[i]));
-                            mx1 = fmaxf(mx1, __uint_as_float(x[i + 1]));
-                        }
-                    }
-                } else {
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        float r = (is_i8 ? s32_to_f32(x[i]) : __uint_as_float(x[i])) * ratio;
-                        if (key0 + c * 32 + i >= limit) r = -INFINITY;
-                        if (i & 1) mx1 = fmaxf(mx1, r); else mx0 = fmaxf(mx0, r);
-                    }
-                }
-            };
-            tmem_ld32(s_addr, bufa);
-            #pragma unroll 1
-            for (int c = 0; c < 4; c += 2) {
-                tc_wait_ld();
-                tmem_ld32(s_addr + 32 * (c + 1), bufb);
-                pass1(bufa, c);
-                tc_wait_ld();
-                if (c + 2 < 4) tmem_ld32(s_addr + 32 * (c + 2), bufa);
-                pass1(bufb, c + 1);
-            }
-            if (kTrace && p.decoded_bits && row % 16 == 0 && q16_valid) {
+            uint32_t bits4 = 0;     // bit kt = this row's key tile kt is INT8
+            if (q16_valid) {
                 #pragma unroll
-                for (int kt = 0; kt < 4; ++kt) {
-                    const int gkt = 4 * j + kt;
-                    if (gkt < p.k32_tiles) {
-                        p.decoded_bits[(static_cast<std::size_t>(head) * p.q16_tiles + q16) * p.k32_tiles + gkt] =
-                            static_cast<uint8_t>((bits >> kt) & 1u);
+                for (int kt = 0; kt < 4; ++kt) bits4 |= ((slot.pats >> (8 * kt + qlocal)) & 1u) << kt;
+            }
+            const float ratio_lo = q_scale * __half2float(__ushort_as_half(static_cast<unsigned short>(slot.scales & 0xffffu))) * a_f16;
+            const float ratio_hi = q_scale * __half2float(__ushort_as_half(static_cast<unsigned short>(slot.scales >> 16))) * a_f16;
+            const int key0 = j * kTileKeys;
+            const int limit = p.causal ? min(p.N, q_row + 1) : p.N;
+            // fast: no key of the block is masked for any row of the warp and
+            // score_scale > 0, so FP16 raw units are the accumulator values.
+            const bool fast = __all_sync(0xffffffffu, pos_scale && key0 + kTileKeys <= limit);
+            if (!wait_bar(bar(kBarSFull + b), (j >> 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
+            tc_fence_after();
+            // ---- pass 1: this half's max in raw units; the row max combines
+            // both halves through the pair handshake
+            tmem_ld32(s_own, xa);
+            tmem_ld32(s_own + 32, xb);
+            tc_wait_ld();
+            const float ratio = half ? ratio_hi : ratio_lo;
+            uint32_t types = (bits4 >> (2 * half)) & 3u;      // bit c: chunk c is INT8
+            if (!fast) {
+                // Rare: edge blocks or score_scale <= 0. Rewrite both chunks as
+                // raw-unit floats with masked keys at -inf, then take the FP16
+                // (float) max below.
+                #pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t (&x)[32] = c ? xb : xa;
+                    const bool is_i8 = (types >> c) & 1u;
+                    const uint32_t addi = is_i8 ? 0x4B400000u : 0u;
+                    const float subf = is_i8 ? 12582912.0f : 0.0f;
+                    const float mul = is_i8 ? ratio : a_f16;
+                    const int k0 = key0 + 64 * half + 32 * c;
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float r = (__uint_as_float(x[i] + addi) - subf) * mul;
+                        x[i] = __float_as_uint(k0 + i >= limit ? -INFINITY : r);
                     }
                 }
+                types = 0;
             }
-            const float block_max = fmaxf(mx0, mx1);
+            float half_max = -INFINITY;
+            #pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const uint32_t (&x)[32] = c ? xb : xa;
+                const bool is_i8 = (types >> c) & 1u;
+                const uint32_t vote = __ballot_sync(0xffffffffu, is_i8);
+                float mi = -INFINITY, mf = -INFINITY;
+                if (vote != 0u) {
+                    int i0 = static_cast<int>(x[0]), i1 = static_cast<int>(x[1]);
+                    #pragma unroll
+                    for (int i = 2; i < 32; i += 2) {
+                        i0 = max(i0, static_cast<int>(x[i]));
+                        i1 = max(i1, static_cast<int>(x[i + 1]));
+                    }
+                    mi = static_cast<float>(max(i0, i1)) * ratio;
+                }
+                if (vote != 0xffffffffu) {
+                    float f0 = __uint_as_float(x[0]), f1 = __uint_as_float(x[1]);
+                    #pragma unroll
+                    for (int i = 2; i < 32; i += 2) {
+                        f0 = fmaxf(f0, __uint_as_float(x[i]));
+                        f1 = fmaxf(f1, __uint_as_float(x[i + 1]));
+                    }
+                    mf = fmaxf(f0, f1);
+                }
+                half_max = fmaxf(half_max, is_i8 ? mi : mf);
+            }
+            float other_max;
+            if (!pair_exchange(xchg + (j & 1) * kSoftmaxThreads, me, static_cast<uint32_t>(j), half_max, other_max,
+                               abort_flag)) {
+                ok = false;
+                break;
+            }
+            const float block_max = fmaxf(half_max, other_max);
             float alpha = 1.0f;
             if (block_max > m_run + threshold) {             // also true on the first block
                 alpha = ex2((m_run - block_max) * c_exp);    // 0 on the first block
                 m_run = block_max;
             }
             const float neg_m = m_run == -INFINITY ? 0.0f : -m_run * c_exp;
-            if (j > 0) {
-                // Rescale O before this block's PV. PV of the previous block was
-                // issued before this block's QK, so it has landed; the TMEM
-                // stores overlap pass 2 and are waited for before P is published.
-                if (!wait_bar(bar(kBarPvDone + t), (j - 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+                // Rescale this half's O columns before this block's PV; PV of
+                // the previous block must have landed first.
+                if (!wait_bar(bar(kBarPvDone + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort_flag, kStatusSoftmax)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-                    tmem_ld32(o_addr, bufa);
-                    #pragma unroll 1
-                    for (int c = 0; c < p.pv_n; c += 64) {
+                #pragma unroll 1
+                for (int c = 0; c < 64; c += 32) {
+                    if (64 * half + c < p.pv_n) {
+                        tmem_ld32(o_addr + c, xa);
                         tc_wait_ld();
-                        if (c + 32 < p.pv_n) tmem_ld32(o_addr + c + 32, bufb);
                         #pragma unroll
-                        for (int i = 0; i < 32; ++i) bufa[i] = __float_as_uint(__uint_as_float(bufa[i]) * alpha);
-                        tmem_st32(o_addr + c, bufa);
-                        if (c + 32 < p.pv_n) {
-                            tc_wait_ld();
-                            tc_wait_st();
-                            if (c + 64 < p.pv_n) tmem_ld32(o_addr + c + 64, bufa);
-                            #pragma unroll
-                            for (int i = 0; i < 32; ++i) bufb[i] = __float_as_uint(__uint_as_float(bufb[i]) * alpha);
-                            tmem_st32(o_addr + c + 32, bufb);
-                        }
+                        for (int i = 0; i < 32; ++i) xa[i] = __float_as_uint(__uint_as_float(xa[i]) * alpha);
+                        tmem_st32(o_addr + c, xa);
                     }
                 }
             }
-            // ---- pass 2: P = P_hi + P_lo, both fp16. P_hi keeps the top 11
-            // significant bits of p (exact in fp16), P_lo = p - P_hi (exact)
-            // rounded to fp16; the two PV MMAs make the product accurate to
-            // ~2^-22 relative instead of fp16's 2^-11, which the parity
-            // tolerance needs once V has large-magnitude (outlier) channels.
-            // Chunk c's P_hi goes to its columns [32c, 32c+16), P_lo to [32c+16, 32c+32).
-            float sum0 = 0.0f, sum1 = 0.0f;
-            auto pass2 = [&](const uint32_t (&x)[32], int c) {
-                const bool is_i8 = (bits >> c) & 1u;
-                const float mul = (is_i8 ? q_scale * (c < 2 ? ks0 : ks1) * a_f16 : a_f16) * c_exp;
+            // ---- pass 2: P = P_hi + P_lo over this thread's two chunks, both
+            // fp16. P_hi keeps the top 11 significant bits of p (exact in
+            // fp16), P_lo = p - P_hi (exact) rounded to fp16; the two PV MMAs
+            // make the product accurate to ~2^-22 relative instead of fp16's
+            // 2^-11, which the parity tolerance needs once V has
+            // large-magnitude (outlier) channels. Chunk c's P_hi goes to its
+            // columns [32c, 32c+16), P_lo to [32c+16, 32c+32).
+            float sum0 = 0.0f, sum1 = 0.0f, sum2 = 0.0f, sum3 = 0.0f;
+            #pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+                const int kt = 2 * half + c;
+                tmem_ld32(s_own + 32 * c, xa);
+                const bool is_i8 = (bits4 >> kt) & 1u;
+                const uint32_t vote = __ballot_sync(0xffffffffu, is_i8);
+                const float mul = (is_i8 ? (half ? ratio_hi : ratio_lo) : a_f16) * c_exp;
+                const int k0 = key0 + 32 * kt;
+                tc_wait_ld();
+                if (kTrace && row_valid) {
+                    if (p.score_dots && is_i8) {
+                        for (int i = 0; i < 32; ++i) {
+                            if (k0 + i < p.N) {
+                                p.score_dots[(static_cast<std::size_t>(head) * p.M + q_row) * p.N + k0 + i] =
+                                    static_cast<int32_t>(xa[i]);
+                            }
+                        }
+                    }
+                    if (p.decoded_bits && row % 16 == 0 && q16_valid && 4 * j + kt < p.k32_tiles) {
+                        p.decoded_bits[(static_cast<std::size_t>(head) * p.q16_tiles + q16) * p.k32_tiles + 4 * j + kt] =
+                            static_cast<uint8_t>(is_i8);
+                    }
+                }
                 float arg[32];
-                if (is_i8) {
+                if (vote == 0u) {
                     #pragma unroll
-                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(s32_to_f32(x[i]), mul, neg_m);
+                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(xa[i]), mul, neg_m);
                 } else {
+                    // INT8 lanes: exact s32 -> f32 through the 1.5 * 2^23 bias;
+                    // FP16 lanes of a mixed warp pass through unchanged.
+                    const uint32_t addi = is_i8 ? 0x4B400000u : 0u;
+                    const float subf = is_i8 ? 12582912.0f : 0.0f;
                     #pragma unroll
-                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(x[i]), mul, neg_m);
+                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(xa[i] + addi) - subf, mul, neg_m);
                 }
                 if (!fast) {
                     #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        if (key0 + c * 32 + i >= limit) arg[i] = -INFINITY;
+                        if (k0 + i >= limit) arg[i] = -INFINITY;
                     }
                 }
                 uint32_t hi[16], lo[16];
                 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
+                for (int i = 0; i < 16; i += 2) {
                     const float p0 = ex2(arg[2 * i]);
                     const float p1 = ex2(arg[2 * i + 1]);
-                    sum0 += p0;
-                    sum1 += p1;
+                    const float p2 = ex2(arg[2 * i + 2]);
+                    const float p3 = ex2(arg[2 * i + 3]);
+                    sum0 += p0; sum1 += p1; sum2 += p2; sum3 += p3;
                     const float h0 = __uint_as_float(__float_as_uint(p0) & 0xFFFFE000u);
                     const float h1 = __uint_as_float(__float_as_uint(p1) & 0xFFFFE000u);
+                    const float h2 = __uint_as_float(__float_as_uint(p2) & 0xFFFFE000u);
+                    const float h3 = __uint_as_float(__float_as_uint(p3) & 0xFFFFE000u);
                     hi[i] = pack_half2(h0, h1);
+                    hi[i + 1] = pack_half2(h2, h3);
                     lo[i] = pack_half2(p0 - h0, p1 - h1);
+                    lo[i + 1] = pack_half2(p2 - h2, p3 - h3);
                 }
-                tmem_st16(s_addr + 32 * c, hi);
-                tmem_st16(s_addr + 32 * c + 16, lo);
-            };
-            tmem_ld32(s_addr, bufa);
-            #pragma unroll 1
-            for (int c = 0; c < 4; c += 2) {
-                tc_wait_ld();
-                tmem_ld32(s_addr + 32 * (c + 1), bufb);
-                pass2(bufa, c);
-                tc_wait_ld();
-                if (c + 2 < 4) tmem_ld32(s_addr + 32 * (c + 2), bufa);
-                pass2(bufb, c + 1);
+                tmem_st16(s_own + 32 * c, hi);
+                tmem_st16(s_own + 32 * c + 16, lo);
             }
-            l_run = l_run * alpha + (sum0 + sum1);
+            l_run = l_run * alpha + ((sum0 + sum1) + (sum2 + sum3));
             tc_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(kBarPFull + t));
+            mbar_arrive(bar(kBarPFull + b));
         }
-        if (ok && nblk[t] > 0 && wait_bar(bar(kBarPvDone + t), (nblk[t] - 1) & 1, abort_flag, kStatusSoftmax)) {
-            tc_fence_after();
-            const float inv_l = 1.0f / l_run;
-            float* out = p.o + (static_cast<std::size_t>(head) * p.M + q_row) * p.d;
-            #pragma unroll 1
-            for (int c = 0; c < p.pv_n; c += 32) {
-                tmem_ld32(o_addr + c, bufa);
-                tc_wait_ld();
-                if (row_valid) {
-                    if (p.o_vec) {
-                        #pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            if (c + i < p.d) {
-                                reinterpret_cast<float4*>(out + c + i)[0] = make_float4(
-                                    __uint_as_float(bufa[i]) * inv_l, __uint_as_float(bufa[i + 1]) * inv_l,
-                                    __uint_as_float(bufa[i + 2]) * inv_l, __uint_as_float(bufa[i + 3]) * inv_l);
+        // ---- epilogue: full row sum = this half + partner half; write this half's O columns
+        if (ok && nblk > 0) {
+            float l_other = 0.0f;
+            ok = pair_exchange(xchg + (nblk & 1) * kSoftmaxThreads, me, static_cast<uint32_t>(nblk), l_run, l_other,
+                               abort_flag);
+            const float l_total = l_run + l_other;
+            if (ok && wait_bar(bar(kBarPvDone + ((nblk - 1) & 1)), ((nblk - 1) >> 1) & 1, abort_flag, kStatusSoftmax)) {
+                tc_fence_after();
+                const float inv_l = 1.0f / l_total;
+                float* out = p.o + (static_cast<std::size_t>(head) * p.M + q_row) * p.d + 64 * half;
+                #pragma unroll 1
+                for (int c = 0; c < 64; c += 32) {
+                    if (64 * half + c >= p.pv_n) break;
+                    tmem_ld32(o_addr + c, xa);
+                    tc_wait_ld();
+                    if (row_valid) {
+                        if (p.o_vec) {
+                            #pragma unroll
+                            for (int i = 0; i < 32; i += 4) {
+                                if (64 * half + c + i < p.d) {
+                                    reinterpret_cast<float4*>(out + c + i)[0] = make_float4(
+                                        __uint_as_float(xa[i]) * inv_l, __uint_as_float(xa[i + 1]) * inv_l,
+                                        __uint_as_float(xa[i + 2]) * inv_l, __uint_as_float(xa[i + 3]) * inv_l);
+                                }
                             }
-                        }
-                    } else {
-                        #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            if (c + i < p.d) out[c + i] = __uint_as_float(bufa[i]) * inv_l;
+                        } else {
+                            #pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                if (64 * half + c + i < p.d) out[c + i] = __uint_as_float(xa[i]) * inv_l;
+                            }
                         }
                     }
                 }
@@ -941,7 +931,7 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     p.decoded_bits = prob.decoded_bits;
     p.score_dots = prob.score_dots;
     p.heads = prob.heads; p.M = prob.M; p.N = prob.N; p.d = prob.d;
-    p.cta_tiles = (prob.M - 1) / kCtaRows + 1;
+    p.q_tiles = (prob.M - 1) / kTileRows + 1;
     p.kv_blocks = (prob.N - 1) / kTileKeys + 1;
     p.q16_tiles = (prob.M - 1) / 16 + 1;
     p.k32_tiles = (prob.N - 1) / 32 + 1;
@@ -961,7 +951,7 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     p.o_vec = (prob.d % 4 == 0 && aligned16(prob.o)) ? 1 : 0;
     p.head_group = std::min(prob.heads, 8);
 
-    const long long grid = static_cast<long long>(p.cta_tiles) * p.heads;
+    const long long grid = static_cast<long long>(p.q_tiles) * p.heads;
     if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     const int atoms = prob.d <= 64 ? 1 : 2;
     const bool trace = prob.decoded_bits != nullptr || prob.score_dots != nullptr;
