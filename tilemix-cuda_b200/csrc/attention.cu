@@ -657,6 +657,28 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             tc_wait_ld();
             const float ratio = half ? ratio_hi : ratio_lo;
             uint32_t types = (bits4 >> (2 * half)) & 3u;      // bit c: chunk c is INT8
+            if (kTrace && row_valid) {
+                // Debug outputs (routing bits, INT32 dots) from the raw accumulators.
+                #pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const uint32_t (&x)[32] = c ? xb : xa;
+                    const bool is_i8 = (types >> c) & 1u;
+                    const int k0 = key0 + 64 * half + 32 * c;
+                    if (p.score_dots && is_i8) {
+                        for (int i = 0; i < 32; ++i) {
+                            if (k0 + i < p.N) {
+                                p.score_dots[(static_cast<std::size_t>(head) * p.M + q_row) * p.N + k0 + i] =
+                                    static_cast<int32_t>(x[i]);
+                            }
+                        }
+                    }
+                    const int gkt = 4 * j + 2 * half + c;
+                    if (p.decoded_bits && row % 16 == 0 && q16_valid && gkt < p.k32_tiles) {
+                        p.decoded_bits[(static_cast<std::size_t>(head) * p.q16_tiles + q16) * p.k32_tiles + gkt] =
+                            static_cast<uint8_t>(is_i8);
+                    }
+                }
+            }
             if (!fast) {
                 // Rare: edge blocks or score_scale <= 0. Rewrite both chunks as
                 // raw-unit floats with masked keys at -inf, then take the FP16
@@ -726,64 +748,44 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 }
                 tc_fence_after();
                 #pragma unroll 1
-                for (int c = 0; c < 64; c += 32) {
+                for (int c = 0; c < 64; c += 16) {
                     if (64 * half + c < p.pv_n) {
-                        tmem_ld32(o_addr + c, xa);
+                        uint32_t t[16];
+                        tmem_ld16(o_addr + c, t);
                         tc_wait_ld();
                         #pragma unroll
-                        for (int i = 0; i < 32; ++i) xa[i] = __float_as_uint(__uint_as_float(xa[i]) * alpha);
-                        tmem_st32(o_addr + c, xa);
+                        for (int i = 0; i < 16; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
+                        tmem_st16(o_addr + c, t);
                     }
                 }
             }
-            // ---- pass 2: P = P_hi + P_lo over this thread's two chunks, both
-            // fp16. P_hi keeps the top 11 significant bits of p (exact in
-            // fp16), P_lo = p - P_hi (exact) rounded to fp16; the two PV MMAs
-            // make the product accurate to ~2^-22 relative instead of fp16's
-            // 2^-11, which the parity tolerance needs once V has
-            // large-magnitude (outlier) channels. Chunk c's P_hi goes to its
-            // columns [32c, 32c+16), P_lo to [32c+16, 32c+32).
+            // ---- pass 2: P = P_hi + P_lo over this thread's two chunks (still in
+            // registers from pass 1), both fp16. P_hi keeps the top 11
+            // significant bits of p (exact in fp16), P_lo = p - P_hi (exact)
+            // rounded to fp16; the two PV MMAs make the product accurate to
+            // ~2^-22 relative instead of fp16's 2^-11, which the parity
+            // tolerance needs once V has large-magnitude (outlier) channels.
+            // Chunk c's P_hi goes to its columns [32c, 32c+16), P_lo to
+            // [32c+16, 32c+32). Chunks rewritten by the rare path of pass 1
+            // already hold raw units (masked keys at -inf), like FP16 chunks.
             float sum0 = 0.0f, sum1 = 0.0f, sum2 = 0.0f, sum3 = 0.0f;
-            #pragma unroll 1
+            #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                const int kt = 2 * half + c;
-                tmem_ld32(s_own + 32 * c, xa);
-                const bool is_i8 = (bits4 >> kt) & 1u;
+                const uint32_t (&x)[32] = c ? xb : xa;
+                const bool is_i8 = (types >> c) & 1u;
                 const uint32_t vote = __ballot_sync(0xffffffffu, is_i8);
-                const float mul = (is_i8 ? (half ? ratio_hi : ratio_lo) : a_f16) * c_exp;
-                const int k0 = key0 + 32 * kt;
-                tc_wait_ld();
-                if (kTrace && row_valid) {
-                    if (p.score_dots && is_i8) {
-                        for (int i = 0; i < 32; ++i) {
-                            if (k0 + i < p.N) {
-                                p.score_dots[(static_cast<std::size_t>(head) * p.M + q_row) * p.N + k0 + i] =
-                                    static_cast<int32_t>(xa[i]);
-                            }
-                        }
-                    }
-                    if (p.decoded_bits && row % 16 == 0 && q16_valid && 4 * j + kt < p.k32_tiles) {
-                        p.decoded_bits[(static_cast<std::size_t>(head) * p.q16_tiles + q16) * p.k32_tiles + 4 * j + kt] =
-                            static_cast<uint8_t>(is_i8);
-                    }
-                }
+                const float mul = (is_i8 ? ratio : 1.0f) * c_exp;
                 float arg[32];
                 if (vote == 0u) {
                     #pragma unroll
-                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(xa[i]), mul, neg_m);
+                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(x[i]), mul, neg_m);
                 } else {
                     // INT8 lanes: exact s32 -> f32 through the 1.5 * 2^23 bias;
                     // FP16 lanes of a mixed warp pass through unchanged.
                     const uint32_t addi = is_i8 ? 0x4B400000u : 0u;
                     const float subf = is_i8 ? 12582912.0f : 0.0f;
                     #pragma unroll
-                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(xa[i] + addi) - subf, mul, neg_m);
-                }
-                if (!fast) {
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        if (k0 + i >= limit) arg[i] = -INFINITY;
-                    }
+                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(x[i] + addi) - subf, mul, neg_m);
                 }
                 uint32_t hi[16], lo[16];
                 #pragma unroll
