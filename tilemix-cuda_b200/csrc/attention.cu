@@ -501,29 +501,56 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         // ----------------------------------------------------------------- MMA
         const uint32_t pv_idesc = idesc_f16_f32(kTileRows, p.pv_n, true);
         const RouteSlot* ring = reinterpret_cast<const RouteSlot*>(smem + L::kRoute);
-        const uint64_t qf = smem_desc_sw128(sbase + L::kQ, 16, 1024);
-        const uint64_t qi = smem_desc_sw128(sbase + L::kQ8, 16, 1024);
+        // Descriptor words: every operand here is 128-byte swizzled with
+        // 1024-byte 8-row groups, so the high word is shared; the low word
+        // carries the start address (16-byte units) and the leading offset.
+        const uint32_t dhi = smem_desc_sw128_hi(1024);
+        const uint32_t qf_lo = smem_desc_sw128_lo(sbase + L::kQ, 16);
+        const uint32_t qi_lo = smem_desc_sw128_lo(sbase + L::kQ8, 16);
+        const uint32_t kf_lo0 = smem_desc_sw128_lo(sbase + L::kK, 16);
+        const uint32_t ki_lo0 = smem_desc_sw128_lo(sbase + L::kK8, 16);
+        const uint32_t v_lo0 = smem_desc_sw128_lo(sbase + L::kV, kAtomBytes);
+        const bool f16_full = p.f16_ksteps == 4 * kAtoms;
+        const bool i8_full = p.i8_ksteps == 4;
+        const uint32_t none[4] = {0u, 0u, 0u, 0u};
         bool ok = wait_bar(bar(kBarQFull), 0, abort_flag, kStatusMma);
         // One precision over key tiles [kt0, kt0 + nkt) of block j; `off` masks
         // the TMEM lanes (16-row tiles) that keep their previous result.
-        // Descriptor start addresses advance by byte offset >> 4.
-        auto mma_run = [&](uint32_t d_tmem, int ks_stage, bool int8, int kt0, int nkt, const uint32_t (&off)[4]) {
+        // Start addresses advance by byte offset >> 4: 32 B per K step inside
+        // a 64-wide (fp16) atom, one atom (kAtomBytes) per 64 of d, 4096 B
+        // (32 rows) per key tile.
+        auto mma_run = [&](uint32_t d_tmem, int stage, bool int8, int kt0, int nkt, const uint32_t (&off)[4]) {
             const uint32_t d = d_tmem + 32 * kt0;
-            const uint64_t kofs = static_cast<uint64_t>(kt0 * 256);       // 4096 B per key tile
+            const uint32_t kofs = static_cast<uint32_t>(kt0) * 256u;
             if (int8) {
-                const uint64_t ki = smem_desc_sw128(sbase + L::kK8 + ks_stage * kAtomBytes, 16, 1024);
+                const uint32_t k_lo = ki_lo0 + static_cast<uint32_t>(stage) * (kAtomBytes >> 4) + kofs;
                 const uint32_t idesc = idesc_s8_s32(kTileRows, 32 * nkt);
-                #pragma unroll
-                for (int ks = 0; ks < 4; ++ks) {
-                    if (ks < p.i8_ksteps) mma_i8_ss(d, qi + 2 * ks, ki + kofs + 2 * ks, idesc, off, ks > 0 ? 1u : 0u);
+                if (i8_full) {
+                    mma_i8_ss_w<0>(d, qi_lo, k_lo, dhi, idesc, off);
+                    #pragma unroll
+                    for (int ks = 1; ks < 4; ++ks) mma_i8_ss_w<1>(d, qi_lo + 2 * ks, k_lo + 2 * ks, dhi, idesc, off);
+                } else {
+                    mma_i8_ss_w<0>(d, qi_lo, k_lo, dhi, idesc, off);
+                    #pragma unroll 1
+                    for (int ks = 1; ks < p.i8_ksteps; ++ks) mma_i8_ss_w<1>(d, qi_lo + 2 * ks, k_lo + 2 * ks, dhi, idesc, off);
                 }
             } else {
-                const uint64_t kf = smem_desc_sw128(sbase + L::kK + ks_stage * L::kTileF16, 16, 1024);
+                const uint32_t k_lo = kf_lo0 + static_cast<uint32_t>(stage) * (L::kTileF16 >> 4) + kofs;
                 const uint32_t idesc = idesc_f16_f32(kTileRows, 32 * nkt, false);
-                #pragma unroll
-                for (int ks = 0; ks < 4 * kAtoms; ++ks) {
-                    const uint64_t ko = static_cast<uint64_t>((ks >> 2) * (kAtomBytes >> 4) + (ks & 3) * 2);
-                    if (ks < p.f16_ksteps) mma_f16_ss(d, qf + ko, kf + kofs + ko, idesc, off, ks > 0 ? 1u : 0u);
+                if (f16_full) {
+                    mma_f16_ss_w<0>(d, qf_lo, k_lo, dhi, idesc, off);
+                    #pragma unroll
+                    for (int ks = 1; ks < 4 * kAtoms; ++ks) {
+                        const uint32_t ko = static_cast<uint32_t>((ks >> 2) * (kAtomBytes >> 4) + (ks & 3) * 2);
+                        mma_f16_ss_w<1>(d, qf_lo + ko, k_lo + ko, dhi, idesc, off);
+                    }
+                } else {
+                    mma_f16_ss_w<0>(d, qf_lo, k_lo, dhi, idesc, off);
+                    #pragma unroll 1
+                    for (int ks = 1; ks < p.f16_ksteps; ++ks) {
+                        const uint32_t ko = static_cast<uint32_t>((ks >> 2) * (kAtomBytes >> 4) + (ks & 3) * 2);
+                        mma_f16_ss_w<1>(d, qf_lo + ko, k_lo + ko, dhi, idesc, off);
+                    }
                 }
             }
         };
@@ -537,20 +564,14 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             if (lane == 0) {
                 const uint32_t s_tmem = tmem + col_s(j & 1);
                 const bool base_i8 = plan & 1ull;
-                const int runs = 1 + static_cast<int>((plan >> 4) & 7u);
+                mma_run(s_tmem, ks, base_i8, 0, static_cast<int>((plan >> 1) & 7u), none);
+                const int overlays = static_cast<int>((plan >> 4) & 7u);
                 #pragma unroll 1
-                for (int r = 0; r < runs; ++r) {
-                    bool int8 = base_i8;
-                    int kt0 = 0, nkt = static_cast<int>((plan >> 1) & 7u);
-                    uint32_t off[4] = {0u, 0u, 0u, 0u};
-                    if (r > 0) {
-                        const uint32_t ov = static_cast<uint32_t>(plan >> (8 + 13 * (r - 1))) & 0x1fffu;
-                        int8 = !base_i8;
-                        kt0 = static_cast<int>(ov & 3u);
-                        nkt = static_cast<int>((ov >> 2) & 7u);
-                        lane_mask(~(ov >> 5) & 0xffu, off);
-                    }
-                    mma_run(s_tmem, ks, int8, kt0, nkt, off);
+                for (int r = 0; r < overlays; ++r) {
+                    const uint32_t ov = static_cast<uint32_t>(plan >> (8 + 13 * r)) & 0x1fffu;
+                    uint32_t off[4];
+                    lane_mask(~(ov >> 5) & 0xffu, off);
+                    mma_run(s_tmem, ks, !base_i8, static_cast<int>(ov & 3u), static_cast<int>((ov >> 2) & 7u), off);
                 }
                 tc_commit(bar(kBarKEmpty + ks));
                 tc_commit(bar(kBarSFull + (j & 1)));
@@ -568,14 +589,15 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
                 // 8-key groups 1024 B apart; each K step covers 16 keys (2048 B).
                 // P_hi and P_lo of a 16-key step share the V operand.
-                const uint64_t v_desc = smem_desc_sw128(sbase + L::kV + vs * L::kTileF16, kAtomBytes, 1024);
+                const uint32_t v_lo = v_lo0 + static_cast<uint32_t>(vs) * (L::kTileF16 >> 4);
                 const uint32_t p_tmem = tmem + col_s(j & 1);
+                mma_f16_ts_w(tmem + kColO, p_tmem, v_lo, dhi, pv_idesc, j > 0 ? 1u : 0u);
+                mma_f16_ts_w(tmem + kColO, p_tmem + 16, v_lo, dhi, pv_idesc, 1u);
                 #pragma unroll
-                for (int s = 0; s < kTileKeys / 16; ++s) {
-                    const uint64_t b_desc = v_desc + static_cast<uint64_t>(s * 128);
+                for (int s = 1; s < kTileKeys / 16; ++s) {
                     const uint32_t a_hi = p_tmem + 32 * (s >> 1) + 8 * (s & 1);
-                    mma_f16_ts(tmem + kColO, a_hi, b_desc, pv_idesc, (j > 0 || s > 0) ? 1u : 0u);
-                    mma_f16_ts(tmem + kColO, a_hi + 16, b_desc, pv_idesc, 1u);
+                    mma_f16_ts_w(tmem + kColO, a_hi, v_lo + 128 * s, dhi, pv_idesc, 1u);
+                    mma_f16_ts_w(tmem + kColO, a_hi + 16, v_lo + 128 * s, dhi, pv_idesc, 1u);
                 }
                 tc_commit(bar(kBarVEmpty + vs));
                 tc_commit(bar(kBarPvDone + (j & 1)));

@@ -147,6 +147,46 @@ __device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint
                  : "memory");
 }
 
+// Lean issue forms for hot loops: the 64-bit shared-memory descriptors are
+// passed as their two 32-bit words (the low word holds the start address and
+// the leading byte offset, so stepping through a tile is one 32-bit add), and
+// the accumulate flag is a compile-time constant where the caller knows it.
+template <int kAccumulate>
+__device__ __forceinline__ void mma_f16_ss_w(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t desc_hi,
+                                             uint32_t idesc, const uint32_t (&disabled)[4]) {
+    asm volatile("{\n\t.reg .pred p;\n\t.reg .b64 a, b;\n\t"
+                 "setp.ne.b32 p, %5, 0;\n\t"
+                 "mov.b64 a, {%1, %3};\n\t"
+                 "mov.b64 b, {%2, %3};\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %4, {%6, %7, %8, %9}, p;\n\t}"
+                 :: "r"(d_tmem), "r"(a_lo), "r"(b_lo), "r"(desc_hi), "r"(idesc), "n"(kAccumulate),
+                    "r"(disabled[0]), "r"(disabled[1]), "r"(disabled[2]), "r"(disabled[3])
+                 : "memory");
+}
+
+template <int kAccumulate>
+__device__ __forceinline__ void mma_i8_ss_w(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t desc_hi,
+                                            uint32_t idesc, const uint32_t (&disabled)[4]) {
+    asm volatile("{\n\t.reg .pred p;\n\t.reg .b64 a, b;\n\t"
+                 "setp.ne.b32 p, %5, 0;\n\t"
+                 "mov.b64 a, {%1, %3};\n\t"
+                 "mov.b64 b, {%2, %3};\n\t"
+                 "tcgen05.mma.cta_group::1.kind::i8 [%0], a, b, %4, {%6, %7, %8, %9}, p;\n\t}"
+                 :: "r"(d_tmem), "r"(a_lo), "r"(b_lo), "r"(desc_hi), "r"(idesc), "n"(kAccumulate),
+                    "r"(disabled[0]), "r"(disabled[1]), "r"(disabled[2]), "r"(disabled[3])
+                 : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t desc_hi,
+                                             uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\t.reg .b64 b;\n\t"
+                 "setp.ne.b32 p, %5, 0;\n\t"
+                 "mov.b64 b, {%2, %3};\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], b, %4, p;\n\t}"
+                 :: "r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(desc_hi), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem desc]  (A is 128 lanes x K fp16, 2 per column).
 __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                            uint32_t idesc, uint32_t accumulate) {
@@ -178,6 +218,14 @@ __host__ __device__ constexpr uint32_t idesc_s8_s32(int m, int n) {
 // [61,64)), descriptor version 1 (bits [46,48)), base offset 0: the operand
 // tile must start on a 1024-byte boundary (modulo the K-step byte offset added
 // to the start address).
+// Its two 32-bit words, for the lean issue forms above.
+__host__ __device__ constexpr uint32_t smem_desc_sw128_lo(uint32_t addr, uint32_t lbo_bytes) {
+    return ((addr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t smem_desc_sw128_hi(uint32_t sbo_bytes) {
+    return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+}
+
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes,
                                                     uint32_t sbo_bytes) {
     return static_cast<uint64_t>((addr >> 4) & 0x3FFFu)
