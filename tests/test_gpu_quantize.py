@@ -83,3 +83,38 @@ def test_baseline_batch_bit_exact(name):
     assert np.array_equal(q8, eq8) and np.array_equal(k8, ek8)
     assert np.array_equal(qs.view(np.uint16), eqs.view(np.uint16).reshape(qs.shape))
     assert np.array_equal(ks.view(np.uint16), eks.view(np.uint16).reshape(ks.shape))
+
+
+def _all_fp16_up_to(absmax: float) -> np.ndarray:
+    """Every finite fp16 value v with |v| <= absmax (both signs, with zero)."""
+    bits = np.arange(0, 0x7C00, dtype=np.uint16)
+    pos = bits.view(np.float16)
+    pos = pos[pos.astype(np.float32) <= np.float32(absmax)]
+    return np.concatenate([pos, -pos[1:]])
+
+
+@pytest.mark.parametrize("absmax", [1.0, 127.0, 3.140625, 100.0, 65504.0, 2.0 ** -10, 6.0e-8])
+def test_exhaustive_fp16_values_bit_exact(absmax):
+    """Every fp16 value within one block's absmax, so every tie (x / scale exactly
+    k + 1/2) and near-tie of the half-away-from-zero rounding is exercised on the
+    quantizer's vector path, for Q (128-row) and K (64-row) blocks."""
+    vals = _all_fp16_up_to(absmax)
+    d = 128
+    per_block = 64 * d - 1                      # one slot per block holds the absmax
+    nblocks = -(-vals.size // per_block)
+    rows = []
+    for b in range(nblocks):
+        chunk = vals[b * per_block:(b + 1) * per_block]
+        block = np.zeros(64 * d, np.float16)
+        block[0] = np.float16(absmax)
+        block[1:1 + chunk.size] = chunk
+        rows.append(block.reshape(64, d))
+    x = np.concatenate(rows)                     # 64-row K blocks; Q blocks pair them
+    if x.shape[0] % 128:
+        x = np.concatenate([x, np.zeros((64, d), np.float16)])
+    q8, k8, qs, ks = quantize_gpu(x, x)
+    eq8, eqs = oracle.quantize(x, 128)
+    ek8, eks = oracle.quantize(x, 64)
+    assert np.array_equal(q8, eq8) and np.array_equal(k8, ek8)
+    assert np.array_equal(qs.view(np.uint16), eqs.view(np.uint16))
+    assert np.array_equal(ks.view(np.uint16), eks.view(np.uint16))

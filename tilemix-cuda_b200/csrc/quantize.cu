@@ -12,8 +12,9 @@
 // B200 design: the block is read from HBM once. Each CTA owns one block
 // (<= 128 x 128 fp16 = 32 KB), its 256 threads hold the block in registers
 // (up to 8 x 16-byte loads each), reduce the absmax with warp shuffles, then
-// quantize from registers and write 8-byte stores: 3 bytes of HBM traffic per
-// element, the algorithmic minimum. Unaligned pointers or d % 8 != 0 take a
+// quantize from registers (a reciprocal multiply, with the exact division kept
+// for near-ties) and write 8-byte stores: 3 bytes of HBM traffic per element,
+// the algorithmic minimum. Unaligned pointers or d % 8 != 0 take a
 // scalar two-pass path (the second pass hits L2).
 #include "kernels.cuh"
 
@@ -25,10 +26,30 @@ namespace {
 constexpr int kQuantThreads = 256;
 constexpr int kMaxChunksPerThread = 8;   // 128 rows x 128 d / 8 halves / 256 threads
 
-__device__ __forceinline__ std::int8_t quantize_one(float x, float scale) {
+// Reference rounding: fl(x / scale) by a correctly rounded division, then
+// round half away from zero. Exact shortcut: the answer depends on the
+// quotient only through trunc(fl(|q| + 0.5)), which changes only where |q| + 0.5
+// crosses an integer. With y = fl(|x| * fl(1/scale)), |y - fl(|x| / scale)| <
+// 2^-15 for |q| <= 128 (two roundings of 2^-24 relative each, plus the
+// quotient's own), and fl(v + 0.5) moves v by at most 2^-17 there; so when
+// y + 0.5 is more than 2^-14 away from an integer both give the same integer.
+// Anything closer (ties, near-ties), and NaN / inf / zero scales, takes the
+// exact division.
+__device__ __forceinline__ std::int8_t quantize_exact(float x, float scale) {
     const float normalized = scale > 0.0f ? __fdiv_rn(x, scale) : 0.0f;
     const int rounded = __float2int_rz(__fadd_rn(normalized, copysignf(0.5f, normalized)));
     return static_cast<std::int8_t>(max(-127, min(127, rounded)));
+}
+
+__device__ __forceinline__ std::int8_t quantize_one(float x, float scale, float recip) {
+    const float t = __fadd_rn(__fmul_rn(fabsf(x), recip), 0.5f);
+    const float whole = truncf(t);
+    const float frac = t - whole;                         // exact: t and whole share the exponent range
+    if (frac > 0x1p-14f && frac < 1.0f - 0x1p-14f) {      // false for NaN
+        const int mag = min(127, __float2int_rz(whole));
+        return static_cast<std::int8_t>(x < 0.0f ? -mag : mag);
+    }
+    return quantize_exact(x, scale);
 }
 
 __device__ __forceinline__ float block_max(float value, float* scratch) {
@@ -85,6 +106,7 @@ quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
             }
         }
         const float scale = __fdiv_rn(block_max(local, scratch), 127.0f);
+        const float recip = scale > 0.0f ? __frcp_rn(scale) : 0.0f;
         if (threadIdx.x == 0) t.scales[static_cast<std::size_t>(head) * t.blocks + block] = __float2half_rn(scale);
         #pragma unroll
         for (int i = 0; i < kMaxChunksPerThread; ++i) {
@@ -94,7 +116,7 @@ quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
                 uint32_t packed[2] = {0u, 0u};
                 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const uint32_t byte = static_cast<uint8_t>(quantize_one(__half2float(h[e]), scale));
+                    const uint32_t byte = static_cast<uint8_t>(quantize_one(__half2float(h[e]), scale, recip));
                     packed[e >> 2] |= byte << ((e & 3) * 8);
                 }
                 reinterpret_cast<uint2*>(dst)[c] = make_uint2(packed[0], packed[1]);
@@ -108,7 +130,7 @@ quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
         const float scale = __fdiv_rn(block_max(local, scratch), 127.0f);
         if (threadIdx.x == 0) t.scales[static_cast<std::size_t>(head) * t.blocks + block] = __float2half_rn(scale);
         for (int i = threadIdx.x; i < count; i += kQuantThreads) {
-            dst[i] = quantize_one(__half2float(src[i]), scale);
+            dst[i] = quantize_exact(__half2float(src[i]), scale);
         }
     }
 }

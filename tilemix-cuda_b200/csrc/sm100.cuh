@@ -60,6 +60,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
+// Non-blocking probe: true if the phase with this parity has completed
+// (acquire semantics, like a successful wait).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+    return done != 0;
+}
+
 // As mbar_try_wait, but a thread whose phase is not complete is suspended
 // (it does not spin and steal issue slots) until the phase completes or about
 // `suspend_ns` nanoseconds pass.
