@@ -27,7 +27,7 @@ import subprocess
 import sys
 import tempfile
 import time
-from datetime import timedelta
+from datetime import datetime, timedelta
 from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
@@ -42,7 +42,7 @@ L2_BYTES = 126 * 2**20
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="tilemix", choices=["tilemix", "reference"])
     ap.add_argument("--config", default="c3")
@@ -77,7 +77,7 @@ def profiled_traffic() -> dict:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -85,12 +85,16 @@ class ClockSampler:
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.proc = None
         self.gpu = gpu_index
+        self.window = None       # (start, end) host wall-clock of the timed region
+
+    def mark(self, start: float, end: float):
+        self.window = (start, end)
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -108,8 +112,15 @@ class ClockSampler:
         with open(self.file.name) as f:
             for line in f:
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
+                if len(parts) < 10:
+                    continue
+                try:
+                    stamp = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                # keep the samples taken while the timed region ran
+                if self.window is None or self.window[0] <= stamp <= self.window[1]:
+                    rows.append(parts[1:])
         os.unlink(self.file.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
@@ -263,6 +274,7 @@ def run_tilemix(args, rank, world, local):
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * n + 2)]
     barrier(world)
     torch.cuda.synchronize()
+    t_start = time.time()
     ev[0].record(stream)
     for i in range(n):
         quantize()
@@ -271,6 +283,7 @@ def run_tilemix(args, rank, world, local):
         ev[2 + 2 * i].record(stream)
     ev[-1].record(stream)
     torch.cuda.synchronize()
+    clocks.mark(t_start, time.time())
     barrier(world)
     clk = clocks.stop()
     total_ms = ev[0].elapsed_time(ev[-1])
