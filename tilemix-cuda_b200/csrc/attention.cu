@@ -78,7 +78,7 @@ constexpr int kMmaWarp = 8;
 constexpr int kProducerWarp = 9;
 constexpr int kAttnThreads = 320;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;              // S_a at 0, S_b at 128, O at 256
+constexpr uint32_t kColO = 256;              // S_a at 0, S_b at 128, O_0 at 256, O_1 at 384
 constexpr uint32_t kAtomBytes = 128 * 128;   // 128 rows x 128 bytes
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 constexpr uint32_t kSuspendNs = 200000;      // per try_wait suspension (wakes early on completion)
@@ -118,7 +118,7 @@ struct SmemLayout {
     static constexpr uint32_t kRoute = kV + kVStages * kTileF16;       // [kRouteSlots]
     static constexpr uint32_t kXchg = kRoute + kRouteSlots * sizeof(RouteSlot);  // [2][256] u64 pair handshake words
     static constexpr uint32_t kBars = kXchg + 2 * kSoftmaxThreads * 8;
-    static constexpr uint32_t kNumBars = 16 + kRouteSlots;
+    static constexpr uint32_t kNumBars = 18 + kRouteSlots;
     static constexpr uint32_t kMisc = kBars + kNumBars * 8;            // tmem base, abort flag
     static constexpr uint32_t kEnd = kMisc + 16;
     static constexpr uint32_t kBytes = kEnd + 1024;                     // + alignment slack
@@ -126,7 +126,7 @@ struct SmemLayout {
 
 enum Bar : int {
     kBarQFull = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7,
-    kBarSFull = 9, kBarPFull = 11, kBarPvDone = 13, kBarDrain = 15, kBarRoute = 16,
+    kBarSFull = 9, kBarPFull = 11, kBarPvDone = 15, kBarDrain = 17, kBarRoute = 18,
 };
 
 // QK plan of the tile for one key block, packed in 64 bits:
@@ -134,33 +134,50 @@ enum Bar : int {
 //   bits [4,7) overlay count, overlay i at bit 8 + 13 i: key tile (2 bits),
 //   key-tile count (3 bits), row-tile set (8 bits). Overlays are of the other
 //   precision and run after the base on the listed 16-row tiles only.
-__device__ __noinline__ std::uint64_t make_plan(uint32_t i8set, uint32_t f16set, int ktiles) {
-    if (ktiles <= 0 || (i8set | f16set) == 0) return 0;
-    auto runs_of = [&](uint32_t sets, std::uint64_t& packed) -> int {
-        int runs = 0, kt = 0;
-        packed = 0;
-        while (kt < ktiles) {
-            const uint32_t set = (sets >> (8 * kt)) & 0xffu;
-            int end = kt + 1;
-            while (end < ktiles && ((sets >> (8 * end)) & 0xffu) == set) ++end;
-            if (set) {
-                packed |= (static_cast<std::uint64_t>(kt) | (static_cast<std::uint64_t>(end - kt) << 2) |
-                           (static_cast<std::uint64_t>(set) << 5)) << (8 + 13 * runs);
+// Runs of equal, non-empty row sets over the block's key tiles (byte kt of
+// `sets`), packed as the plan's overlay entries; straight-line code for the
+// four key tiles of a block.
+__device__ __forceinline__ int plan_runs(uint32_t sets, int ktiles, std::uint64_t& packed, int& tiles) {
+    int runs = 0, start = 0, len = 0;
+    uint32_t cur = 0;
+    packed = 0;
+    tiles = 0;
+    #pragma unroll
+    for (int kt = 0; kt <= 4; ++kt) {
+        const uint32_t set = kt < ktiles ? (sets >> (8 * kt)) & 0xffu : 0u;
+        if (set != cur) {
+            if (cur) {
+                packed |= static_cast<std::uint64_t>(static_cast<uint32_t>(start) | (static_cast<uint32_t>(len) << 2) |
+                                                     (cur << 5)) << (8 + 13 * runs);
                 ++runs;
+                tiles += len;
             }
-            kt = end;
+            cur = set;
+            start = kt;
+            len = 0;
         }
-        return runs;
-    };
-    std::uint64_t plan = static_cast<std::uint64_t>(ktiles) << 1;
+        ++len;
+    }
+    return runs;
+}
+
+// A mixed block is one full-width base MMA of one precision, then overlays of
+// the other precision. Base chosen by tensor-time estimate per d = 128 (K steps
+// x cycles per step; one step of N keys costs about max(N / 2, 32 + N / 4)
+// cycles, shared-memory bound below N = 128): INT8 base 256, FP16 base 512,
+// FP16 overlay run of L key tiles 256 + 64 L, INT8 overlay run 128 + 32 L.
+__device__ __forceinline__ std::uint64_t make_plan(uint32_t i8set, uint32_t f16set, int ktiles) {
+    if (ktiles <= 0 || (i8set | f16set) == 0) return 0;
+    const std::uint64_t plan = static_cast<std::uint64_t>(ktiles) << 1;
     if (!i8set || !f16set) return plan | (i8set ? 1ull : 0ull);
-    std::uint64_t f16_runs_packed, i8_runs_packed;
-    const int f16_runs = runs_of(f16set, f16_runs_packed);
-    const int i8_runs = runs_of(i8set, i8_runs_packed);
-    // INT8 MMAs cost half as much per key as FP16 ones: prefer an INT8 base
-    // unless that leaves more FP16 overlay runs than the FP16 base leaves INT8 runs.
-    if (f16_runs <= i8_runs) return plan | 1ull | (static_cast<std::uint64_t>(f16_runs) << 4) | f16_runs_packed;
-    return plan | (static_cast<std::uint64_t>(i8_runs) << 4) | i8_runs_packed;
+    std::uint64_t f16_packed, i8_packed;
+    int f16_tiles, i8_tiles;
+    const int f16_runs = plan_runs(f16set, ktiles, f16_packed, f16_tiles);
+    const int i8_runs = plan_runs(i8set, ktiles, i8_packed, i8_tiles);
+    const int cost_i8_base = 256 + 256 * f16_runs + 64 * f16_tiles;
+    const int cost_f16_base = 512 + 128 * i8_runs + 32 * i8_tiles;
+    if (cost_i8_base <= cost_f16_base) return plan | 1ull | (static_cast<std::uint64_t>(f16_runs) << 4) | f16_packed;
+    return plan | (static_cast<std::uint64_t>(i8_runs) << 4) | i8_packed;
 }
 
 struct Params {
@@ -380,7 +397,8 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int s = 0; s < kVStages; ++s) { mbar_init(bar(kBarVFull + s), 1); mbar_init(bar(kBarVEmpty + s), 1); }
         for (int b = 0; b < 2; ++b) {
             mbar_init(bar(kBarSFull + b), 1);
-            mbar_init(bar(kBarPFull + b), kSoftmaxThreads);
+            mbar_init(bar(kBarPFull + 2 * b), kSoftmaxThreads / 2);
+            mbar_init(bar(kBarPFull + 2 * b + 1), kSoftmaxThreads / 2);
             mbar_init(bar(kBarPvDone + b), 1);
         }
         mbar_init(bar(kBarDrain), 1);
@@ -429,62 +447,72 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         route.fetch(p, head, 0, nblk, lane);
         RouteSlot* ring = reinterpret_cast<RouteSlot*>(smem + L::kRoute);
         int k_issued = 0, v_issued = 0;
-        for (int j = 0; j < nblk; ++j) {
-            uint32_t pats, valid, scales;
-            route.decode(p, j, pats, valid, scales);
-            route.fetch(p, head, j + 1, nblk, lane);
-            const bool need_i8 = pats != 0;
-            const bool need_f16 = (valid & ~pats) != 0;
-            if (lane == 0) {
-                RouteSlot slot;
-                slot.pats = pats;
-                slot.scales = scales;
-                slot.plan = make_plan(pats, valid & ~pats, min(4, p.k32_tiles - 4 * j));
-                ring[j % kRouteSlots] = slot;
-                mbar_arrive(bar(kBarRoute + j % kRouteSlots));   // release: slot visible to its waiters
-            }
-            __syncwarp();
-            const int ks = j % kKStages;
-            if (!wait_bar(bar(kBarKEmpty + ks), ((j / kKStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
-            if (kUseTma) {
+        // K (and the routing summary) of block i go out one block ahead of V
+        // of block i - 1: the K stage frees up when QK(i - 2) completes,
+        // earlier than the V stage (PV(i - 3)) on the in-order tensor pipe.
+        for (int i = 0; i <= nblk; ++i) {
+            if (i < nblk) {
+                const int j = i;
+                uint32_t pats, valid, scales;
+                route.decode(p, j, pats, valid, scales);
+                route.fetch(p, head, j + 1, nblk, lane);
+                const bool need_i8 = pats != 0;
+                const bool need_f16 = (valid & ~pats) != 0;
                 if (lane == 0) {
-                    const uint32_t bytes = (need_f16 ? L::kTileF16 : 0u) + (need_i8 ? kAtomBytes : 0u);
-                    mbar_arrive_expect_tx(bar(kBarKFull + ks), bytes);
-                    if (need_f16) {
+                    RouteSlot slot;
+                    slot.pats = pats;
+                    slot.scales = scales;
+                    slot.plan = make_plan(pats, valid & ~pats, min(4, p.k32_tiles - 4 * j));
+                    ring[j % kRouteSlots] = slot;
+                    mbar_arrive(bar(kBarRoute + j % kRouteSlots));   // release: slot visible to its waiters
+                }
+                __syncwarp();
+                const int ks = j % kKStages;
+                if (!wait_bar(bar(kBarKEmpty + ks), ((j / kKStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
+                if (kUseTma) {
+                    if (lane == 0) {
+                        const uint32_t bytes = (need_f16 ? L::kTileF16 : 0u) + (need_i8 ? kAtomBytes : 0u);
+                        mbar_arrive_expect_tx(bar(kBarKFull + ks), bytes);
+                        if (need_f16) {
+                            for (int a = 0; a < kAtoms; ++a) {
+                                tma_load_3d(sbase + L::kK + ks * L::kTileF16 + a * kAtomBytes, &tm_k,
+                                            bar(kBarKFull + ks), a * 64, j * kTileKeys, head);
+                            }
+                        }
+                        if (need_i8) {
+                            tma_load_3d(sbase + L::kK8 + ks * kAtomBytes, &tm_k8, bar(kBarKFull + ks), 0,
+                                        j * kTileKeys, head);
+                        }
+                    }
+                } else {
+                    if (need_f16) manual_tile_f16(smem + L::kK + ks * L::kTileF16, p.k + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
+                    if (need_i8) manual_tile_i8(smem + L::kK8 + ks * kAtomBytes, p.k8 + kv_off, j * kTileKeys, p.N, p.d, lane);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar(kBarKFull + ks));
+                }
+                k_issued = j + 1;
+            }
+            if (i >= 1) {
+                const int j = i - 1;
+                const int vs = j % kVStages;
+                if (!wait_bar(bar(kBarVEmpty + vs), ((j / kVStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
+                if (kUseTma) {
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(bar(kBarVFull + vs), L::kTileF16);
                         for (int a = 0; a < kAtoms; ++a) {
-                            tma_load_3d(sbase + L::kK + ks * L::kTileF16 + a * kAtomBytes, &tm_k, bar(kBarKFull + ks),
+                            tma_load_3d(sbase + L::kV + vs * L::kTileF16 + a * kAtomBytes, &tm_v, bar(kBarVFull + vs),
                                         a * 64, j * kTileKeys, head);
                         }
                     }
-                    if (need_i8) {
-                        tma_load_3d(sbase + L::kK8 + ks * kAtomBytes, &tm_k8, bar(kBarKFull + ks), 0, j * kTileKeys, head);
-                    }
+                } else {
+                    manual_tile_f16(smem + L::kV + vs * L::kTileF16, p.v + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar(kBarVFull + vs));
                 }
-            } else {
-                if (need_f16) manual_tile_f16(smem + L::kK + ks * L::kTileF16, p.k + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
-                if (need_i8) manual_tile_i8(smem + L::kK8 + ks * kAtomBytes, p.k8 + kv_off, j * kTileKeys, p.N, p.d, lane);
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(kBarKFull + ks));
+                v_issued = j + 1;
             }
-            k_issued = j + 1;
-            const int vs = j % kVStages;
-            if (!wait_bar(bar(kBarVEmpty + vs), ((j / kVStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
-            if (kUseTma) {
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(bar(kBarVFull + vs), L::kTileF16);
-                    for (int a = 0; a < kAtoms; ++a) {
-                        tma_load_3d(sbase + L::kV + vs * L::kTileF16 + a * kAtomBytes, &tm_v, bar(kBarVFull + vs),
-                                    a * 64, j * kTileKeys, head);
-                    }
-                }
-            } else {
-                manual_tile_f16(smem + L::kV + vs * L::kTileF16, p.v + kv_off, j * kTileKeys, p.N, p.d, kAtoms, lane);
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(kBarVFull + vs));
-            }
-            v_issued = j + 1;
         }
         // Drain: the newest load into each buffer must have landed before the
         // CTA may exit (normally long complete; matters only after an abort).
@@ -579,26 +607,37 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             __syncwarp();
             return true;
         };
-        // PV of block j: O (+)= (P_hi + P_lo) V_j.
+        // PV of block j, per 64-key half h: O_h (+)= (P_hi + P_lo) V_j[keys of h].
+        // Each half of the softmax publishes its own P, so half 0's MMAs can
+        // start while half 1 is still exponentiating.
         auto issue_pv = [&](int j) -> bool {
-            if (!wait_bar(bar(kBarPFull + (j & 1)), (j >> 1) & 1, abort_flag, kStatusMma)) return false;
             const int vs = j % kVStages;
             if (!wait_bar(bar(kBarVFull + vs), (j / kVStages) & 1, abort_flag, kStatusMma)) return false;
-            tc_fence_after();
-            if (lane == 0) {
-                // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
-                // 8-key groups 1024 B apart; each K step covers 16 keys (2048 B).
-                // P_hi and P_lo of a 16-key step share the V operand.
-                const uint32_t v_lo = v_lo0 + static_cast<uint32_t>(vs) * (L::kTileF16 >> 4);
-                const uint32_t p_tmem = tmem + col_s(j & 1);
-                mma_f16_ts_w(tmem + kColO, p_tmem, v_lo, dhi, pv_idesc, j > 0 ? 1u : 0u);
-                mma_f16_ts_w(tmem + kColO, p_tmem + 16, v_lo, dhi, pv_idesc, 1u);
-                #pragma unroll
-                for (int s = 1; s < kTileKeys / 16; ++s) {
-                    const uint32_t a_hi = p_tmem + 32 * (s >> 1) + 8 * (s & 1);
-                    mma_f16_ts_w(tmem + kColO, a_hi, v_lo + 128 * s, dhi, pv_idesc, 1u);
-                    mma_f16_ts_w(tmem + kColO, a_hi + 16, v_lo + 128 * s, dhi, pv_idesc, 1u);
+            // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
+            // 8-key groups 1024 B apart; each K step covers 16 keys (2048 B).
+            // P_hi and P_lo of a 16-key step share the V operand.
+            const uint32_t v_lo = v_lo0 + static_cast<uint32_t>(vs) * (L::kTileF16 >> 4);
+            const uint32_t p_tmem = tmem + col_s(j & 1);
+            #pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (!wait_bar(bar(kBarPFull + 2 * (j & 1) + h), (j >> 1) & 1, abort_flag, kStatusMma)) return false;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t o_tmem = tmem + kColO + 128u * h;
+                    const uint32_t a0 = p_tmem + 64u * h;
+                    const uint32_t b0 = v_lo + 512u * h;
+                    mma_f16_ts_w(o_tmem, a0, b0, dhi, pv_idesc, j > 0 ? 1u : 0u);
+                    mma_f16_ts_w(o_tmem, a0 + 16, b0, dhi, pv_idesc, 1u);
+                    #pragma unroll
+                    for (int t = 1; t < 4; ++t) {
+                        const uint32_t a_hi = a0 + 32 * (t >> 1) + 8 * (t & 1);
+                        mma_f16_ts_w(o_tmem, a_hi, b0 + 128 * t, dhi, pv_idesc, 1u);
+                        mma_f16_ts_w(o_tmem, a_hi + 16, b0 + 128 * t, dhi, pv_idesc, 1u);
+                    }
                 }
+                __syncwarp();
+            }
+            if (lane == 0) {
                 tc_commit(bar(kBarVEmpty + vs));
                 tc_commit(bar(kBarPvDone + (j & 1)));
             }
@@ -617,14 +656,14 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         wait_bar(bar(kBarDrain), 0, abort_flag, kStatusDrain);
     } else if (warp < kSoftmaxWarps) {
         // ------------------------------------------------------------- softmax
-        // Thread = (query row, 64-key half). Each thread reads its row's whole
-        // 128-key block from TMEM (four 32-column chunks) and takes the row
-        // max itself (integer max of the s32 dots on INT8 chunks, scaled once),
-        // so the two halves of a row agree on the max without exchanging it;
-        // it then exponentiates only its own two chunks and writes P (hi, lo)
-        // over them. Precision choices are per 16-row query tile, so a warp
-        // (32 rows) can mix INT8 and FP16 chunks: the code paths branch on
-        // warp votes, never per lane.
+        // Thread = (query row, 64-key half h). Per block it reads its half's
+        // two 32-key chunks from TMEM once, turns INT8 chunks into exact
+        // floats, takes the half's max and swaps it with the other half of
+        // the row (pair handshake), then exponentiates the two chunks from
+        // the same registers and writes P (hi, lo) over them. Precision is
+        // chosen per 16-row query tile, so a warp (32 rows) can mix INT8 and
+        // FP16 chunks: per-lane differences are selects, branches are on
+        // warp votes.
         const int half = warp >> 2;                                  // key half of every block
         const int row = (warp & 3) * 32 + static_cast<int>(lane);    // TMEM lane = query row
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
@@ -645,40 +684,47 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         float m_run = -INFINITY;    // running max (raw units), possibly stale by < 2^15 in p
         float l_run = 0.0f;         // this half's share of the row sum
         bool ok = true;
-        const uint32_t o_addr = tmem + lane_base + kColO + 64u * half;
+        const uint32_t o_addr = tmem + lane_base + kColO + 128u * half;     // O_h
         volatile std::uint64_t* xchg = reinterpret_cast<volatile std::uint64_t*>(smem + L::kXchg);
         const int me = static_cast<int>(threadIdx.x);
         uint32_t xa[32], xb[32];
-        for (int j = 0; j < nblk; ++j) {
+        // Routing of the next block (this half's two INT8 bits and its INT8
+        // score ratio) is read and decoded while the current block is being
+        // exponentiated, so the loop top only waits for S.
+        uint32_t n_types = 0;
+        float n_ratio = 0.0f;
+        auto decode = [&](int jb) {
+            const RouteSlot sl = ring[jb % kRouteSlots];
+            n_types = q16_valid ? (((sl.pats >> (16 * half + qlocal)) & 1u) |
+                                   (((sl.pats >> (16 * half + 8 + qlocal)) & 1u) << 1)) : 0u;
+            const uint32_t sc = half ? sl.scales >> 16 : sl.scales & 0xffffu;
+            n_ratio = q_scale * __half2float(__ushort_as_half(static_cast<unsigned short>(sc))) * a_f16;
+        };
+        if (nblk > 0) {
+            ok = wait_bar(bar(kBarRoute), 0, abort_flag, kStatusSoftmax);
+            if (ok) decode(0);
+        }
+        bool s_ready = false;
+        for (int j = 0; ok && j < nblk; ++j) {
             const int b = j & 1;
             const uint32_t s_row = tmem + lane_base + col_s(b);
             const uint32_t s_own = s_row + 64u * half;
-            if (!wait_bar(bar(kBarRoute + j % kRouteSlots), (j / kRouteSlots) & 1, abort_flag, kStatusSoftmax)) {
-                ok = false;
-                break;
-            }
-            const RouteSlot slot = ring[j % kRouteSlots];
-            uint32_t bits4 = 0;     // bit kt = this row's key tile kt is INT8
-            if (q16_valid) {
-                #pragma unroll
-                for (int kt = 0; kt < 4; ++kt) bits4 |= ((slot.pats >> (8 * kt + qlocal)) & 1u) << kt;
-            }
-            const float ratio_lo = q_scale * __half2float(__ushort_as_half(static_cast<unsigned short>(slot.scales & 0xffffu))) * a_f16;
-            const float ratio_hi = q_scale * __half2float(__ushort_as_half(static_cast<unsigned short>(slot.scales >> 16))) * a_f16;
+            uint32_t types = n_types;          // bit c: chunk c of this half is INT8
+            const float ratio = n_ratio;
             const int key0 = j * kTileKeys;
             const int limit = p.causal ? min(p.N, q_row + 1) : p.N;
             // fast: no key of the block is masked for any row of the warp and
             // score_scale > 0, so FP16 raw units are the accumulator values.
             const bool fast = __all_sync(0xffffffffu, pos_scale && key0 + kTileKeys <= limit);
-            if (!wait_bar(bar(kBarSFull + b), (j >> 1) & 1, abort_flag, kStatusSoftmax)) { ok = false; break; }
+            if (!s_ready && !wait_bar(bar(kBarSFull + b), (j >> 1) & 1, abort_flag, kStatusSoftmax)) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
-            // ---- pass 1: this half's max in raw units; the row max combines
-            // both halves through the pair handshake
+            // ---- this half's two 32-key chunks
             tmem_ld32(s_own, xa);
             tmem_ld32(s_own + 32, xb);
             tc_wait_ld();
-            const float ratio = half ? ratio_hi : ratio_lo;
-            uint32_t types = (bits4 >> (2 * half)) & 3u;      // bit c: chunk c is INT8
             if (kTrace && row_valid) {
                 // Debug outputs (routing bits, INT32 dots) from the raw accumulators.
                 #pragma unroll
@@ -703,8 +749,8 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             }
             if (!fast) {
                 // Rare: edge blocks or score_scale <= 0. Rewrite both chunks as
-                // raw-unit floats with masked keys at -inf, then take the FP16
-                // (float) max below.
+                // raw-unit floats with masked keys at -inf; they then go through
+                // the FP16 (float) path below.
                 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
                     uint32_t (&x)[32] = c ? xb : xa;
@@ -721,94 +767,70 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 }
                 types = 0;
             }
-            float half_max = -INFINITY;
+            // INT8 chunks become exact floats in place (s32 -> f32 through
+            // the 1.5 * 2^23 bias, |dot| <= 127^2 * 128 < 2^22), so the max
+            // and the exponent below are one code path for both precisions;
+            // FP16 lanes of a mixed warp pass through unchanged.
             #pragma unroll
             for (int c = 0; c < 2; ++c) {
-                const uint32_t (&x)[32] = c ? xb : xa;
+                uint32_t (&x)[32] = c ? xb : xa;
                 const bool is_i8 = (types >> c) & 1u;
-                const uint32_t vote = __ballot_sync(0xffffffffu, is_i8);
-                float mi = -INFINITY, mf = -INFINITY;
-                if (vote != 0u) {
-                    int i0 = static_cast<int>(x[0]), i1 = static_cast<int>(x[1]);
+                if (__any_sync(0xffffffffu, is_i8)) {
+                    const uint32_t addi = is_i8 ? 0x4B400000u : 0u;
+                    const float subf = is_i8 ? 12582912.0f : 0.0f;
                     #pragma unroll
-                    for (int i = 2; i < 32; i += 2) {
-                        i0 = max(i0, static_cast<int>(x[i]));
-                        i1 = max(i1, static_cast<int>(x[i + 1]));
-                    }
-                    mi = static_cast<float>(max(i0, i1)) * ratio;
+                    for (int i = 0; i < 32; ++i) x[i] = __float_as_uint(__uint_as_float(x[i] + addi) - subf);
                 }
-                if (vote != 0xffffffffu) {
-                    float f0 = __uint_as_float(x[0]), f1 = __uint_as_float(x[1]);
-                    #pragma unroll
-                    for (int i = 2; i < 32; i += 2) {
-                        f0 = fmaxf(f0, __uint_as_float(x[i]));
-                        f1 = fmaxf(f1, __uint_as_float(x[i + 1]));
-                    }
-                    mf = fmaxf(f0, f1);
+            }
+            const float mul0 = ((types & 1u) ? ratio : 1.0f) * c_exp;   // score_log2 = x * mul
+            const float mul1 = ((types & 2u) ? ratio : 1.0f) * c_exp;
+            // next block's routing: probe now, decode alongside the exponent
+            bool r_ready = true;
+            if (j + 1 < nblk) {
+                r_ready = mbar_test_wait(bar(kBarRoute + (j + 1) % kRouteSlots), ((j + 1) / kRouteSlots) & 1);
+                if (r_ready) decode(j + 1);
+            }
+            // ---- this half's max; the running max moves only when the block
+            // exceeds it by more than 2^15 in p. O_h is then rescaled, after
+            // P is written: by then the previous block's PV, which must land
+            // first, has mostly finished.
+            float rescale = 1.0f;
+            {
+                float m0 = max3f(__uint_as_float(xa[0]), __uint_as_float(xa[1]), __uint_as_float(xa[2]));
+                float m1 = max3f(__uint_as_float(xb[0]), __uint_as_float(xb[1]), __uint_as_float(xb[2]));
+                #pragma unroll
+                for (int i = 3; i < 31; i += 2) {
+                    m0 = max3f(m0, __uint_as_float(xa[i]), __uint_as_float(xa[i + 1]));
+                    m1 = max3f(m1, __uint_as_float(xb[i]), __uint_as_float(xb[i + 1]));
                 }
-                half_max = fmaxf(half_max, is_i8 ? mi : mf);
-            }
-            float other_max;
-            if (!pair_exchange(xchg + (j & 1) * kSoftmaxThreads, me, static_cast<uint32_t>(j), half_max, other_max,
-                               abort_flag)) {
-                ok = false;
-                break;
-            }
-            const float block_max = fmaxf(half_max, other_max);
-            float alpha = 1.0f;
-            if (block_max > m_run + threshold) {             // also true on the first block
-                alpha = ex2((m_run - block_max) * c_exp);    // 0 on the first block
-                m_run = block_max;
+                m0 = fmaxf(m0, __uint_as_float(xa[31]));
+                m1 = fmaxf(m1, __uint_as_float(xb[31]));
+                // raw units: INT8 chunks scale by their (non-negative) ratio
+                const float bm = fmaxf((types & 1u) ? m0 * ratio : m0, (types & 2u) ? m1 * ratio : m1);
+                float alpha = 1.0f;
+                if (bm > m_run + threshold) {            // also true when m_run is -inf
+                    alpha = ex2((m_run - bm) * c_exp);   // 0 when m_run is -inf
+                    m_run = bm;
+                }
+                l_run *= alpha;
+                rescale = alpha;
             }
             const float neg_m = m_run == -INFINITY ? 0.0f : -m_run * c_exp;
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-                // Rescale this half's O columns before this block's PV; PV of
-                // the previous block must have landed first.
-                if (!wait_bar(bar(kBarPvDone + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort_flag, kStatusSoftmax)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                #pragma unroll 1
-                for (int c = 0; c < 64; c += 16) {
-                    if (64 * half + c < p.pv_n) {
-                        uint32_t t[16];
-                        tmem_ld16(o_addr + c, t);
-                        tc_wait_ld();
-                        #pragma unroll
-                        for (int i = 0; i < 16; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * alpha);
-                        tmem_st16(o_addr + c, t);
-                    }
-                }
-            }
-            // ---- pass 2: P = P_hi + P_lo over this thread's two chunks (still in
-            // registers from pass 1), both fp16. P_hi keeps the top 11
-            // significant bits of p (exact in fp16), P_lo = p - P_hi (exact)
-            // rounded to fp16; the two PV MMAs make the product accurate to
-            // ~2^-22 relative instead of fp16's 2^-11, which the parity
-            // tolerance needs once V has large-magnitude (outlier) channels.
-            // Chunk c's P_hi goes to its columns [32c, 32c+16), P_lo to
-            // [32c+16, 32c+32). Chunks rewritten by the rare path of pass 1
-            // already hold raw units (masked keys at -inf), like FP16 chunks.
+            // ---- P = 2^(score_log2 - m) as P_hi + P_lo, both fp16. P_hi keeps
+            // the top 11 significant bits of p (exact in fp16), P_lo = p - P_hi
+            // (exact) rounded to fp16; the two PV MMAs make the product
+            // accurate to ~2^-22 relative instead of fp16's 2^-11, which the
+            // parity tolerance needs once V has large-magnitude (outlier)
+            // channels. Chunk c's P_hi goes to its columns [32c, 32c+16), P_lo
+            // to [32c+16, 32c+32).
             float sum0 = 0.0f, sum1 = 0.0f, sum2 = 0.0f, sum3 = 0.0f;
             #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const uint32_t (&x)[32] = c ? xb : xa;
-                const bool is_i8 = (types >> c) & 1u;
-                const uint32_t vote = __ballot_sync(0xffffffffu, is_i8);
-                const float mul = (is_i8 ? ratio : 1.0f) * c_exp;
+                const float mul = c ? mul1 : mul0;
                 float arg[32];
-                if (vote == 0u) {
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(x[i]), mul, neg_m);
-                } else {
-                    // INT8 lanes: exact s32 -> f32 through the 1.5 * 2^23 bias;
-                    // FP16 lanes of a mixed warp pass through unchanged.
-                    const uint32_t addi = is_i8 ? 0x4B400000u : 0u;
-                    const float subf = is_i8 ? 12582912.0f : 0.0f;
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(x[i] + addi) - subf, mul, neg_m);
-                }
+                #pragma unroll
+                for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(x[i]), mul, neg_m);
                 uint32_t hi[16], lo[16];
                 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
@@ -829,40 +851,75 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 tmem_st16(s_own + 32 * c, hi);
                 tmem_st16(s_own + 32 * c + 16, lo);
             }
-            l_run = l_run * alpha + ((sum0 + sum1) + (sum2 + sum3));
+            l_run += (sum0 + sum1) + (sum2 + sum3);
+            if (j > 0 && __any_sync(0xffffffffu, rescale != 1.0f)) {
+                if (!wait_bar(bar(kBarPvDone + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort_flag, kStatusSoftmax)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                #pragma unroll 1
+                for (int c = 0; c < p.pv_n; c += 16) {
+                    uint32_t t[16];
+                    tmem_ld16(o_addr + c, t);
+                    tc_wait_ld();
+                    #pragma unroll
+                    for (int i = 0; i < 16; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * rescale);
+                    tmem_st16(o_addr + c, t);
+                }
+            }
+            s_ready = j + 1 < nblk && mbar_test_wait(bar(kBarSFull + (b ^ 1)), ((j + 1) >> 1) & 1);
             tc_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(kBarPFull + b));
+            mbar_arrive(bar(kBarPFull + 2 * b + half));
+            if (!__all_sync(0xffffffffu, r_ready)) {
+                if (!wait_bar(bar(kBarRoute + (j + 1) % kRouteSlots), ((j + 1) / kRouteSlots) & 1, abort_flag,
+                              kStatusSoftmax)) {
+                    ok = false;
+                    break;
+                }
+                decode(j + 1);
+            }
+            s_ready = __all_sync(0xffffffffu, s_ready);
         }
-        // ---- epilogue: full row sum = this half + partner half; write this half's O columns
+        // ---- epilogue: combine the two halves of the row; this thread writes
+        // output columns [64h, 64h + 64)
         if (ok && nblk > 0) {
-            float l_other = 0.0f;
-            ok = pair_exchange(xchg + (nblk & 1) * kSoftmaxThreads, me, static_cast<uint32_t>(nblk), l_run, l_other,
-                               abort_flag);
-            const float l_total = l_run + l_other;
+            float m_oth = 0.0f, l_oth = 0.0f;
+            ok = pair_exchange(xchg + kSoftmaxThreads, me, 1u, m_run, m_oth, abort_flag) &&
+                 pair_exchange(xchg, me, 2u, l_run, l_oth, abort_flag);
             if (ok && wait_bar(bar(kBarPvDone + ((nblk - 1) & 1)), ((nblk - 1) >> 1) & 1, abort_flag, kStatusSoftmax)) {
                 tc_fence_after();
-                const float inv_l = 1.0f / l_total;
-                float* out = p.o + (static_cast<std::size_t>(head) * p.M + q_row) * p.d + 64 * half;
+                const float m = fmaxf(m_run, m_oth);
+                const float a_me = m_run == -INFINITY ? 0.0f : ex2((m_run - m) * c_exp);
+                const float a_oth = m_oth == -INFINITY ? 0.0f : ex2((m_oth - m) * c_exp);
+                const float inv_l = 1.0f / (l_run * a_me + l_oth * a_oth);
+                const float w_me = a_me * inv_l, w_oth = a_oth * inv_l;
+                const uint32_t o_oth = tmem + lane_base + kColO + 128u * (half ^ 1);
+                float* out = p.o + (static_cast<std::size_t>(head) * p.M + q_row) * p.d;
                 #pragma unroll 1
-                for (int c = 0; c < 64; c += 32) {
-                    if (64 * half + c >= p.pv_n) break;
+                for (int c = 64 * half; c < 64 * half + 64 && c < p.pv_n; c += 32) {
                     tmem_ld32(o_addr + c, xa);
+                    tmem_ld32(o_oth + c, xb);
                     tc_wait_ld();
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        xa[i] = __float_as_uint(__uint_as_float(xa[i]) * w_me + __uint_as_float(xb[i]) * w_oth);
+                    }
                     if (row_valid) {
                         if (p.o_vec) {
                             #pragma unroll
                             for (int i = 0; i < 32; i += 4) {
-                                if (64 * half + c + i < p.d) {
+                                if (c + i < p.d) {
                                     reinterpret_cast<float4*>(out + c + i)[0] = make_float4(
-                                        __uint_as_float(xa[i]) * inv_l, __uint_as_float(xa[i + 1]) * inv_l,
-                                        __uint_as_float(xa[i + 2]) * inv_l, __uint_as_float(xa[i + 3]) * inv_l);
+                                        __uint_as_float(xa[i]), __uint_as_float(xa[i + 1]),
+                                        __uint_as_float(xa[i + 2]), __uint_as_float(xa[i + 3]));
                                 }
                             }
                         } else {
                             #pragma unroll
                             for (int i = 0; i < 32; ++i) {
-                                if (64 * half + c + i < p.d) out[c + i] = __uint_as_float(xa[i]) * inv_l;
+                                if (c + i < p.d) out[c + i] = __uint_as_float(xa[i]);
                             }
                         }
                     }
