@@ -858,14 +858,19 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     break;
                 }
                 tc_fence_after();
+                // 64 columns per round trip (xa, xb are free again here)
                 #pragma unroll 1
-                for (int c = 0; c < p.pv_n; c += 16) {
-                    uint32_t t[16];
-                    tmem_ld16(o_addr + c, t);
+                for (int c = 0; c < p.pv_n; c += 64) {
+                    tmem_ld32(o_addr + c, xa);
+                    tmem_ld32(o_addr + c + 32, xb);
                     tc_wait_ld();
                     #pragma unroll
-                    for (int i = 0; i < 16; ++i) t[i] = __float_as_uint(__uint_as_float(t[i]) * rescale);
-                    tmem_st16(o_addr + c, t);
+                    for (int i = 0; i < 32; ++i) {
+                        xa[i] = __float_as_uint(__uint_as_float(xa[i]) * rescale);
+                        xb[i] = __float_as_uint(__uint_as_float(xb[i]) * rescale);
+                    }
+                    tmem_st32(o_addr + c, xa);
+                    tmem_st32(o_addr + c + 32, xb);
                 }
             }
             s_ready = j + 1 < nblk && mbar_test_wait(bar(kBarSFull + (b ^ 1)), ((j + 1) >> 1) & 1);
