@@ -386,8 +386,10 @@ def run_reference(args, rank, world):
     host = {"q": w["q"].numpy(), "k": w["k"].numpy(), "v": w["v"].numpy(), "words": w["words"].numpy()}
     values = []
     last = None
+    # each step is a bounded sample, so that the whole run ends within a few minutes
+    per_step = max(0.5, min(args.cpu_seconds, 150.0 / (args.warmup + args.steps)))
     for i in range(args.warmup + args.steps):
-        last = cpu_reference_sample(host, cfg, args.cpu_seconds)
+        last = cpu_reference_sample(host, cfg, per_step)
         if i >= args.warmup:
             values.append(last["step_seconds"])
     step_s = statistics.median(values)
@@ -405,7 +407,57 @@ def run_reference(args, rank, world):
             "cpu_baseline": cpu,
             "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    gpu = reference_gpu_sample(args, cfg)
+    if gpu is not None:
+        line["reference_gpu"] = gpu
     print(json.dumps(line), flush=True)
+
+
+def reference_gpu_sample(args, cfg, heads: int = 4, reps: int = 3):
+    """The reference's own GPU kernels (src/tilemix.cu built for sm_100a, called
+    per head through quantize_tilemix_qk + launch_fused_fp16_attention) on a few
+    whole heads of the workload. The reference kernel has no causal mask, so the
+    heads run non-causal and the value is 4*heads*S^2*D FLOP per second."""
+    import torch
+    import oracle
+    from tilemix_b200 import workloads
+    lib = oracle.ref_gpu_lib()
+    if lib is None or not torch.cuda.is_available():
+        return None
+    w = workloads.make_inputs(args.config, p=args.p, batch=1, heads=heads, device="cuda")
+    H, S, D = w["heads"], w["S"], w["D"]
+    q, k, v = w["q"], w["k"], w["v"]
+    words = w["words"].cuda()
+    q8, k8 = torch.empty_like(q, dtype=torch.int8), torch.empty_like(k, dtype=torch.int8)
+    qs = torch.empty((H, (S - 1) // 128 + 1), dtype=torch.float16, device="cuda")
+    ks = torch.empty((H, (S - 1) // 64 + 1), dtype=torch.float16, device="cuda")
+    out = torch.empty((H, S, D), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def run():
+        err = lib.ref_gpu_tilemix_heads(q.data_ptr(), k.data_ptr(), v.data_ptr(), q8.data_ptr(), k8.data_ptr(),
+                                        qs.data_ptr(), ks.data_ptr(), out.data_ptr(), H, S, S, D,
+                                        w["score_scale"], words.data_ptr(), words.numel() // H, 2,
+                                        stream.cuda_stream)
+        if err:
+            raise SystemExit(f"reference GPU kernels returned cudaError {err}")
+
+    run()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        run()
+        b.record(stream)
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    ms = statistics.median(times)
+    flops = 4.0 * H * S * S * D
+    return {"value": round(flops / (ms * 1e-3) / 1e12, 4), "unit": "TFLOP/s", "ms_per_head": round(ms / H, 3),
+            "sample": f"{H} whole heads of {args.config} shapes (S={S}, D={D}) through the reference's "
+                      f"quantize_tilemix_qk + launch_fused_fp16_attention built for sm_100a, one call per "
+                      f"head; non-causal (the reference kernel has no causal mask), median of {reps}"}
 
 
 def main():

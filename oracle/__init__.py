@@ -11,9 +11,13 @@ Python (ctypes + numpy) access to two CPU checkers:
   reference tree; the committed golden vectors under ``tests/golden/`` carry its
   outputs there).
 
+It also loads ``oracle/_ref/libtilemix_ref_gpu.so``, the reference's own GPU
+kernels (``src/tilemix.cu``) compiled in place for sm_100a, which only
+``bench.py --impl reference`` times (its "reference GPU" column).
+
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg
-may use this package, and only as the checker / the timed CPU baseline. The
-product library never imports it.
+and reference arm may use this package, and only as the checker / the timed
+reference. The product library never imports it.
 """
 from __future__ import annotations
 
@@ -27,6 +31,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "_build" / "libtilemix_oracle.so"
 REF_SO = HERE / "_ref" / "libtilemix_ref.so"
+REF_GPU_SO = HERE / "_ref" / "libtilemix_ref_gpu.so"
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -34,6 +39,7 @@ _F = ctypes.c_float
 
 _lib = None
 _ref = None
+_ref_gpu = None
 
 
 def build(reference_root: str | None = None) -> None:
@@ -90,6 +96,17 @@ def ref_lib():
                                              _I, _P, _I, _P, _I, _P]
         _ref.ref_max_threads.restype = _I
     return _ref
+
+
+def ref_gpu_lib():
+    """The reference's own GPU kernels (compiled in place for sm_100a), or None."""
+    global _ref_gpu
+    if _ref_gpu is None and REF_GPU_SO.exists():
+        _ref_gpu = ctypes.CDLL(str(REF_GPU_SO))
+        _ref_gpu.ref_gpu_tilemix_heads.restype = _I
+        _ref_gpu.ref_gpu_tilemix_heads.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F,
+                                                   _P, ctypes.c_size_t, _I, _P]
+    return _ref_gpu
 
 
 def _ptr(a: np.ndarray | None):

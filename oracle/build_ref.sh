@@ -4,6 +4,10 @@
 #   oracle/_ref/libtilemix_ref.so      : the reference's OWN CPU oracle headers
 #                                        (src/tests/reference_*.h), compiled where
 #                                        they lie, behind ref_shim.cpp
+#   oracle/_ref/libtilemix_ref_gpu.so  : the reference's OWN GPU kernels
+#                                        (src/tilemix.cu) for sm_100a, compiled
+#                                        where they lie, behind ref_gpu_shim.cu
+#                                        (bench.py's "reference GPU" column)
 # Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default /root/reference)
 # The reference build is skipped, not failed, when the reference tree is absent.
 set -euo pipefail
@@ -21,6 +25,12 @@ if [[ -f "$ref_root/src/tests/reference_tilemix.h" ]]; then
         -I"$cuda_inc" -I"$ref_root/src/tests" -I"$ref_root/include" \
         "$here/ref_shim.cpp" -o "$here/_ref/libtilemix_ref.so"
     echo "built $here/_ref/libtilemix_ref.so from $ref_root/src/tests"
+    if [[ -f "$ref_root/src/tilemix.cu" ]] && command -v nvcc > /dev/null; then
+        nvcc -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -Xcompiler -fPIC -shared \
+            -I"$ref_root/include" "$ref_root/src/tilemix.cu" "$here/ref_gpu_shim.cu" \
+            -o "$here/_ref/libtilemix_ref_gpu.so"
+        echo "built $here/_ref/libtilemix_ref_gpu.so from $ref_root/src/tilemix.cu"
+    fi
 else
     echo "reference tree not found at $ref_root; oracle/_ref not rebuilt"
 fi
