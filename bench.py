@@ -141,6 +141,8 @@ def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    # keep stdout to the one JSON line (NCCL would print its version banner there)
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     if world > 1:
         import torch.distributed as dist
         if args.impl == "tilemix":
