@@ -1,0 +1,63 @@
+"""The PyTorch operator layer (torch.ops.tilemix.*) over the C-ABI.
+
+CPU: the operators are registered and their fake kernels give the output
+shapes/dtypes (what torch.compile tracing and CUDA-graph capture rely on).
+GPU: the operators return exactly what the direct C-ABI calls return.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+from torch._subclasses.fake_tensor import FakeTensorMode
+
+from tilemix_b200 import ops  # noqa: F401  (registers torch.ops.tilemix.*)
+
+
+def test_ops_registered():
+    assert hasattr(torch.ops.tilemix, "quantize_qk")
+    assert hasattr(torch.ops.tilemix, "attention")
+
+
+def test_fake_shapes():
+    with FakeTensorMode():
+        q = torch.empty((3, 300, 128), dtype=torch.float16)
+        k = torch.empty((3, 257, 128), dtype=torch.float16)
+        v = torch.empty((3, 257, 128), dtype=torch.float16)
+        q8, k8, qs, ks = torch.ops.tilemix.quantize_qk(q, k)
+        assert q8.shape == q.shape and q8.dtype == torch.int8
+        assert k8.shape == k.shape and k8.dtype == torch.int8
+        assert qs.shape == (3, 3) and ks.shape == (3, 5) and qs.dtype == torch.float16
+        words = torch.empty((3 * 19,), dtype=torch.int64)
+        o = torch.ops.tilemix.attention(q, k, v, q8, k8, qs, ks, words, 2, 0.088, True)
+        assert o.shape == q.shape and o.dtype == torch.float32
+        o2 = torch.ops.tilemix.attention(q[0], k[0], v[0], None, None, None, None, None, 2, 0.088, False)
+        assert o2.shape == (300, 128) and o2.dtype == torch.float32
+
+
+@pytest.mark.gpu
+def test_ops_match_c_abi_bitwise():
+    import tilemix_b200 as tm
+    from tilemix_b200 import workloads
+    g = torch.Generator(device="cpu").manual_seed(5)
+    heads, m, d = 2, 384, 128
+    q = torch.randn((heads, m, d), generator=g).half().cuda()
+    k = torch.randn((heads, m, d), generator=g).half().cuda()
+    v = torch.randn((heads, m, d), generator=g).half().cuda()
+    bm = (torch.rand((heads, (m + 63) // 64, (m + 63) // 64), generator=g) < 0.5).to(torch.uint8).numpy()
+    words = torch.from_numpy(workloads.pack_block_mask64(bm, m, m).view(np.int64)).cuda()
+    q8, k8, qs, ks = torch.ops.tilemix.quantize_qk(q, k)
+    e8, f8, es, fs = tm.quantize(q, k)
+    torch.cuda.synchronize()
+    assert torch.equal(q8, e8) and torch.equal(k8, f8) and torch.equal(qs, es) and torch.equal(ks, fs)
+    scale = 1.0 / math.sqrt(d)
+    o = torch.ops.tilemix.attention(q, k, v, q8, k8, qs, ks, words, 2, scale, True)
+    e = tm.attention(q, k, v, q8=e8, k8=f8, q_scales=es, k_scales=fs, words=words, key_tiles_per_group=2,
+                     score_scale=scale, causal=True)
+    torch.cuda.synchronize()
+    assert torch.equal(o, e)
+    o2 = ops.tilemix_attention(q, k, v, words, causal=True)
+    torch.cuda.synchronize()
+    assert torch.equal(o2, e)
+    err, status = tm.read_and_clear_status()
+    assert err == 0 and status == 0

@@ -397,8 +397,8 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int s = 0; s < kVStages; ++s) { mbar_init(bar(kBarVFull + s), 1); mbar_init(bar(kBarVEmpty + s), 1); }
         for (int b = 0; b < 2; ++b) {
             mbar_init(bar(kBarSFull + b), 1);
-            mbar_init(bar(kBarPFull + 2 * b), kSoftmaxThreads / 2);
-            mbar_init(bar(kBarPFull + 2 * b + 1), kSoftmaxThreads / 2);
+            mbar_init(bar(kBarPFull + 2 * b), kSoftmaxWarps / 2);       // one arrival per warp of the half
+            mbar_init(bar(kBarPFull + 2 * b + 1), kSoftmaxWarps / 2);
             mbar_init(bar(kBarPvDone + b), 1);
         }
         mbar_init(bar(kBarDrain), 1);
@@ -584,10 +584,11 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         };
         // QK^T of block j into S[j % 2], following the producer's plan.
         auto issue_qk = [&](int j) -> bool {
-            if (!wait_bar(bar(kBarRoute + j % kRouteSlots), (j / kRouteSlots) & 1, abort_flag, kStatusMma)) return false;
-            const std::uint64_t plan = ring[j % kRouteSlots].plan;
+            // The producer publishes block j's routing slot before it arms
+            // K(j)'s barrier, so waiting for K(j) also makes the slot visible.
             const int ks = j % kKStages;
             if (!wait_bar(bar(kBarKFull + ks), (j / kKStages) & 1, abort_flag, kStatusMma)) return false;
+            const std::uint64_t plan = ring[j % kRouteSlots].plan;
             tc_fence_after();
             if (lane == 0) {
                 const uint32_t s_tmem = tmem + col_s(j & 1);
@@ -876,7 +877,8 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             s_ready = j + 1 < nblk && mbar_test_wait(bar(kBarSFull + (b ^ 1)), ((j + 1) >> 1) & 1);
             tc_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(kBarPFull + 2 * b + half));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarPFull + 2 * b + half));
             if (!__all_sync(0xffffffffu, r_ready)) {
                 if (!wait_bar(bar(kBarRoute + (j + 1) % kRouteSlots), ((j + 1) / kRouteSlots) & 1, abort_flag,
                               kStatusSoftmax)) {

@@ -1,0 +1,87 @@
+"""PyTorch operators over the C-ABI: ``torch.ops.tilemix.quantize_qk`` and
+``torch.ops.tilemix.attention``.
+
+They call the same extern "C" entry points as the ctypes functions in
+``tilemix_b200`` (``tilemix_quantize_qk_batched``, ``tilemix_attention_batched``)
+on the current CUDA stream, and register fake (meta) kernels so that shape
+propagation, ``torch.compile`` tracing and CUDA-graph capture see the outputs
+without running the GPU code. Layout: [heads, S, d] contiguous fp16 (a 2-D
+[S, d] tensor is one head), the reference's layout per head; the routing words
+are the reference's per-head mask words (``include/attention_fused.h:47-52``),
+``words_per_head`` apart.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import (TileMixQuantized, TileMixRouting, check, quantize_tilemix_qk_batched,
+               tilemix_attention_batched)
+
+_Q_ROWS, _K_ROWS = 128, 64   # quantization block rows (include/attention_fused.h:13-14)
+
+
+def _heads3(x: torch.Tensor) -> torch.Tensor:
+    return x if x.dim() == 3 else x.unsqueeze(0)
+
+
+@torch.library.custom_op("tilemix::quantize_qk", mutates_args=())
+def quantize_qk(q: torch.Tensor, k: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Per-block symmetric INT8 quantization of Q (128-row blocks) and K (64-row
+    blocks): returns (q8, k8, q_scales [heads, ceil(M/128)], k_scales [heads, ceil(N/64)])."""
+    q3, k3 = _heads3(q).contiguous(), _heads3(k).contiguous()
+    heads, m, d = q3.shape
+    n = k3.shape[1]
+    q8 = torch.empty(q.shape, dtype=torch.int8, device=q.device)
+    k8 = torch.empty(k.shape, dtype=torch.int8, device=k.device)
+    qs = torch.empty((heads, (m - 1) // _Q_ROWS + 1), dtype=torch.float16, device=q.device)
+    ks = torch.empty((heads, (n - 1) // _K_ROWS + 1), dtype=torch.float16, device=q.device)
+    check(quantize_tilemix_qk_batched(q3, k3, q8, k8, qs, ks, heads, m, n, d,
+                                      torch.cuda.current_stream(q.device)), "tilemix::quantize_qk")
+    return q8, k8, qs, ks
+
+
+@quantize_qk.register_fake
+def _(q, k):
+    heads = 1 if q.dim() == 2 else q.shape[0]
+    m, n = q.shape[-2], k.shape[-2]
+    return (q.new_empty(q.shape, dtype=torch.int8), k.new_empty(k.shape, dtype=torch.int8),
+            q.new_empty((heads, (m - 1) // _Q_ROWS + 1), dtype=torch.float16),
+            q.new_empty((heads, (n - 1) // _K_ROWS + 1), dtype=torch.float16))
+
+
+@torch.library.custom_op("tilemix::attention", mutates_args=())
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q8: torch.Tensor | None,
+              k8: torch.Tensor | None, q_scales: torch.Tensor | None, k_scales: torch.Tensor | None,
+              words: torch.Tensor | None, key_tiles_per_group: int, score_scale: float,
+              causal: bool) -> torch.Tensor:
+    """Routed mixed-precision attention, fp32 output of q's shape. With
+    ``words`` (uint64 mask words viewed as int64) the quantized operands are
+    required; without, every tile runs FP16 (the reference's unrouted path)."""
+    q3, k3, v3 = _heads3(q).contiguous(), _heads3(k).contiguous(), _heads3(v).contiguous()
+    heads, m, d = q3.shape
+    n = k3.shape[1]
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    routing = TileMixRouting(words, 0 if words is None else words.numel(), key_tiles_per_group)
+    quantized = TileMixQuantized(q8, k8, q_scales, k_scales) if q8 is not None else None
+    check(tilemix_attention_batched(q3, k3, v3, out, heads, m, n, d, score_scale, causal,
+                                    torch.cuda.current_stream(q.device), routing, quantized),
+          "tilemix::attention")
+    return out
+
+
+@attention.register_fake
+def _(q, k, v, q8, k8, q_scales, k_scales, words, key_tiles_per_group, score_scale, causal):
+    return q.new_empty(q.shape, dtype=torch.float32)
+
+
+def tilemix_attention(q, k, v, words=None, *, key_tiles_per_group: int = 2, score_scale: float | None = None,
+                      causal: bool = False) -> torch.Tensor:
+    """Quantize (when routed) and attend: the whole TileMix hot path as two operators."""
+    d = q.shape[-1]
+    scale = 1.0 / math.sqrt(d) if score_scale is None else float(score_scale)
+    if words is None:
+        return attention(q, k, v, None, None, None, None, None, key_tiles_per_group, scale, causal)
+    q8, k8, qs, ks = quantize_qk(q, k)
+    return attention(q, k, v, q8, k8, qs, ks, words, key_tiles_per_group, scale, causal)
