@@ -306,6 +306,14 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// Three-input maximum (PTX max.f32 with three sources, sm_100+); like fmaxf, a
+// NaN input is ignored when another input is a number.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float y;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);   // .x (low 16 bits) = lo
     return *reinterpret_cast<const uint32_t*>(&h);
