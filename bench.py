@@ -299,18 +299,19 @@ def run_tilemix(args, rank, world, local):
     attn_avg = reduce_max(sum(attn_ms) / n, world)
     quant_avg = reduce_max(sum(quant_ms) / n, world)
 
-    # end to end through the C-ABI with host buffers: H2D inputs + mask, both
-    # kernels, D2H of the fp32 output, every step.
+    # end to end through the C-ABI with host buffers: one
+    # tilemix_attention_from_host call per step (H2D of Q, K, V and the
+    # routing words, both kernels, D2H of the fp32 output, pipelined over
+    # chunks of heads inside the library).
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
     hwords = w["words"].pin_memory()
     hout = torch.empty((H, S, D), dtype=torch.float32).pin_memory()
+    bufs = tm.TileMixDeviceBuffers(q=q, k=k, v=v, q8=q8, k8=k8, q_scales=qs, k_scales=ks, words=words, o=out)
     e2e_steps = max(1, min(n, 5))
 
     def e2e_step():
-        q.copy_(hq, non_blocking=True); k.copy_(hk, non_blocking=True); v.copy_(hv, non_blocking=True)
-        words.copy_(hwords, non_blocking=True)
-        quantize(); attend()
-        hout.copy_(out, non_blocking=True)
+        tm.check(tm.tilemix_attention_from_host(hq, hk, hv, hwords, hout, bufs, H, S, S, D, w["score_scale"],
+                                                cfg["causal"], 2, 0, stream), "attention_from_host")
 
     e2e_step()
     torch.cuda.synchronize()
@@ -364,7 +365,8 @@ def run_tilemix(args, rank, world, local):
                      "kernel": "tilemix_attention_kernel",
                      "work": "F_eff = 4*B*H*S^2*D/2 (causal) algorithmic FLOPs per launch"},
         "e2e": {"value": round(job_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
+                "api": "tilemix_attention_from_host (C-ABI, pinned host buffers, pipelined over head chunks)"},
         "clocks": clk,
         "gpu_launches": 2 * n,
     }

@@ -61,6 +61,44 @@ int tilemix_attention_batched(const void* Q, const void* K, const void* V, float
                               void* stream, const tilemix_routing* routing,
                               const tilemix_quantized* quantized);
 
+/* Caller-owned device buffers of tilemix_attention_from_host, each sized for
+ * all `heads` heads: q, k, v fp16 [heads, M|N, d]; q8, k8 int8 of the same
+ * shapes; q_scales fp16 [heads, ceil(M/128)]; k_scales fp16 [heads, ceil(N/64)];
+ * words [heads * tilemix_routing_word_count_c(M, N, g)]; o fp32 [heads, M, d].
+ * q8, k8, q_scales, k_scales and words may be NULL when no routing is given. */
+typedef struct tilemix_device_buffers {
+    void* q;
+    void* k;
+    void* v;
+    int8_t* q8;
+    int8_t* k8;
+    void* q_scales;
+    void* k_scales;
+    uint64_t* words;
+    float* o;
+} tilemix_device_buffers;
+
+/* The whole path from host memory, as the reference's driver runs it
+ * (src/main.cu:44-60: H2D copies, quantize_tilemix_qk,
+ * launch_fused_fp16_attention, D2H of O), for [heads, M|N, d] batches and
+ * pipelined: heads are processed in chunks of `chunk_heads` (<= 0 picks a
+ * size), and the H2D copy of chunk c + 1, the kernels of chunk c and the D2H
+ * copy of chunk c - 1 overlap on two library-owned copy streams. hQ, hK, hV
+ * (fp16) and hO (fp32) are host buffers in the same layouts as their device
+ * counterparts; pinned memory is needed for the copies to overlap. h_words
+ * (heads * tilemix_routing_word_count_c(M, N, key_tiles_per_group) words, NULL
+ * = every tile FP16) selects the routed path: Q and K are quantized on the
+ * device and each tile is scored by its routing bit. Asynchronous: every step
+ * is ordered after the work already queued on `stream`, and once `stream`
+ * reaches the point of the call's return, hO holds the output. Same error
+ * contract as tilemix_attention_batched; nothing is queued when an argument is
+ * invalid. */
+int tilemix_attention_from_host(const void* hQ, const void* hK, const void* hV,
+                                const uint64_t* h_words, float* hO,
+                                const tilemix_device_buffers* dev, int heads, int M, int N,
+                                int d, float score_scale, int causal, int key_tiles_per_group,
+                                int chunk_heads, void* stream);
+
 /* Sizing helpers (reference include/attention_fused.h:34-45). */
 size_t tilemix_routing_word_count_c(int M, int N, int key_tiles_per_group);
 size_t tilemix_routing_words_per_row_c(int N, int key_tiles_per_group);

@@ -106,3 +106,23 @@ def test_batched_validation_without_cuda():
 
 def test_demo_driver_built():
     assert _build.DEMO_BIN.exists()
+
+
+def test_from_host_validation_without_cuda():
+    """The host-buffer pipeline rejects bad arguments before any CUDA call."""
+    x = ctypes.create_string_buffer(64)
+    X = ctypes.addressof(x)
+    full = tm.TileMixDeviceBuffers(X, X, X, X, X, X, X, X, X)
+    f = tm.tilemix_attention_from_host
+    assert f(None, X, X, X, X, full, 1, 4, 4, 16, 1.0) == INVALID
+    assert f(X, X, X, X, None, full, 1, 4, 4, 16, 1.0) == INVALID
+    assert f(X, X, X, X, X, None, 1, 4, 4, 16, 1.0) == INVALID
+    assert f(X, X, X, X, X, tm.TileMixDeviceBuffers(X, X, X, o=None), 1, 4, 4, 16, 1.0) == INVALID
+    for bad in (0, -1):
+        assert f(X, X, X, X, X, full, bad, 4, 4, 16, 1.0) == INVALID
+        assert f(X, X, X, X, X, full, 1, bad, 4, 16, 1.0) == INVALID
+        assert f(X, X, X, X, X, full, 1, 4, 4, 16, 1.0, key_tiles_per_group=bad) == INVALID
+    assert f(X, X, X, X, X, full, 1, 4, 4, 16, float("nan")) == INVALID
+    # routed (host words given) needs every quantized device buffer
+    assert f(X, X, X, X, X, tm.TileMixDeviceBuffers(X, X, X, o=X), 1, 4, 4, 16, 1.0) == INVALID
+    assert f(X, X, X, X, X, full, 1, 4, 4, 129, 1.0) == NOT_SUPPORTED

@@ -5,9 +5,12 @@
 #include "kernels.cuh"
 #include "tilemix_c_api.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
+#include <vector>
 
 namespace {
 
@@ -109,6 +112,119 @@ TileMixQuantized to_cpp(const tilemix_quantized* q) {
     return out;
 }
 
+// ------------------------------------------------- pipelined host-buffer path
+// Per device: two copy streams (host->device, device->host) and a pool of
+// events, created on first use and kept for the life of the process. The
+// mutex only serialises the enqueueing of calls that share a device.
+struct PipelineContext {
+    std::mutex mu;
+    cudaStream_t h2d = nullptr;
+    cudaStream_t d2h = nullptr;
+    std::vector<cudaEvent_t> events;
+};
+
+PipelineContext g_pipeline[kMaxDevices];
+
+cudaError_t pipeline_context(PipelineContext& ctx, std::size_t events) {
+    cudaError_t status = cudaSuccess;
+    if (!ctx.h2d) status = cudaStreamCreateWithFlags(&ctx.h2d, cudaStreamNonBlocking);
+    if (status == cudaSuccess && !ctx.d2h) status = cudaStreamCreateWithFlags(&ctx.d2h, cudaStreamNonBlocking);
+    while (status == cudaSuccess && ctx.events.size() < events) {
+        cudaEvent_t e = nullptr;
+        status = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+        if (status == cudaSuccess) ctx.events.push_back(e);
+    }
+    return status;
+}
+
+#define TM_TRY(expr)                                \
+    do {                                            \
+        const cudaError_t tm_status_ = (expr);      \
+        if (tm_status_ != cudaSuccess) return tm_status_; \
+    } while (0)
+
+// H2D of chunk c (copy stream 1) -> quantize + attention of chunk c (the
+// caller's stream) -> D2H of chunk c (copy stream 2), linked by events, so the
+// copies of neighbouring chunks overlap the kernels. A recorded event is only
+// re-recorded by a later call, after every wait on it has been enqueued
+// (cudaStreamWaitEvent binds to the record current at the time of the wait).
+cudaError_t from_host_impl(const __half* hQ, const __half* hK, const __half* hV, const std::uint64_t* h_words,
+                           float* hO, const tilemix_device_buffers* dev, int heads, int M, int N, int d,
+                           float score_scale, bool causal, int g, int chunk_heads, cudaStream_t stream) {
+    if (!hQ || !hK || !hV || !hO || !dev || !dev->q || !dev->k || !dev->v || !dev->o || heads <= 0 ||
+        M <= 0 || N <= 0 || d <= 0 || !std::isfinite(score_scale) || g <= 0) {
+        return cudaErrorInvalidValue;
+    }
+    const bool routed = h_words != nullptr;
+    if (routed && (!dev->words || !dev->q8 || !dev->k8 || !dev->q_scales || !dev->k_scales)) {
+        return cudaErrorInvalidValue;
+    }
+    if (d > kFusedMaxHeadDim) return cudaErrorNotSupported;
+    if (!fits(heads, M, d) || !fits(heads, N, d)) return cudaErrorInvalidValue;
+    TM_TRY(check_device());
+    int device = 0;
+    TM_TRY(cudaGetDevice(&device));
+
+    const int chunk = chunk_heads > 0 ? std::min(chunk_heads, heads) : std::max(1, (heads + 15) / 16);
+    const int chunks = (heads - 1) / chunk + 1;
+    const std::size_t q_elems = static_cast<std::size_t>(M) * d;     // per head
+    const std::size_t kv_elems = static_cast<std::size_t>(N) * d;
+    const std::size_t words_per_head = routed ? tilemix_routing_word_count(M, N, g) : 0;
+    const std::size_t q_scale_blocks = (static_cast<std::size_t>(M) - 1) / kTileMixQQuantRows + 1;
+    const std::size_t k_scale_blocks = (static_cast<std::size_t>(N) - 1) / kTileMixKQuantRows + 1;
+    auto* dq = static_cast<__half*>(dev->q);
+    auto* dk = static_cast<__half*>(dev->k);
+    auto* dv = static_cast<__half*>(dev->v);
+    auto* dqs = static_cast<__half*>(dev->q_scales);
+    auto* dks = static_cast<__half*>(dev->k_scales);
+
+    PipelineContext& ctx = g_pipeline[device];
+    std::lock_guard<std::mutex> lock(ctx.mu);
+    TM_TRY(pipeline_context(ctx, 2 * static_cast<std::size_t>(chunks) + 2));
+    cudaEvent_t start = ctx.events[0], done = ctx.events[1];
+    TM_TRY(cudaEventRecord(start, stream));
+    TM_TRY(cudaStreamWaitEvent(ctx.h2d, start, 0));
+    TM_TRY(cudaStreamWaitEvent(ctx.d2h, start, 0));
+    for (int c = 0; c < chunks; ++c) {
+        const int h0 = c * chunk;
+        const int hn = std::min(chunk, heads - h0);
+        const std::size_t qo = h0 * q_elems, kvo = h0 * kv_elems;
+        cudaEvent_t in = ctx.events[2 + 2 * c], out = ctx.events[3 + 2 * c];
+        TM_TRY(cudaMemcpyAsync(dq + qo, hQ + qo, hn * q_elems * sizeof(__half), cudaMemcpyHostToDevice, ctx.h2d));
+        TM_TRY(cudaMemcpyAsync(dk + kvo, hK + kvo, hn * kv_elems * sizeof(__half), cudaMemcpyHostToDevice, ctx.h2d));
+        TM_TRY(cudaMemcpyAsync(dv + kvo, hV + kvo, hn * kv_elems * sizeof(__half), cudaMemcpyHostToDevice, ctx.h2d));
+        TileMixRouting routing{};
+        routing.key_tiles_per_group = g;
+        TileMixQuantized quantized{};
+        if (routed) {
+            const std::size_t wo = h0 * words_per_head;
+            TM_TRY(cudaMemcpyAsync(dev->words + wo, h_words + wo, hn * words_per_head * sizeof(std::uint64_t),
+                                   cudaMemcpyHostToDevice, ctx.h2d));
+            routing.words = dev->words + wo;
+            routing.word_count = hn * words_per_head;
+            quantized.q = dev->q8 + qo;
+            quantized.k = dev->k8 + kvo;
+            quantized.q_scales = dqs + h0 * q_scale_blocks;
+            quantized.k_scales = dks + h0 * k_scale_blocks;
+        }
+        TM_TRY(cudaEventRecord(in, ctx.h2d));
+        TM_TRY(cudaStreamWaitEvent(stream, in, 0));
+        if (routed) {
+            TM_TRY(quantize_impl(dq + qo, dk + kvo, dev->q8 + qo, dev->k8 + kvo, dqs + h0 * q_scale_blocks,
+                                 dks + h0 * k_scale_blocks, hn, M, N, d, stream));
+        }
+        TM_TRY(attention_impl(dq + qo, dk + kvo, dv + kvo, dev->o + qo, hn, M, N, d, score_scale, causal, stream,
+                              routing, quantized));
+        TM_TRY(cudaEventRecord(out, stream));
+        TM_TRY(cudaStreamWaitEvent(ctx.d2h, out, 0));
+        TM_TRY(cudaMemcpyAsync(hO + qo, dev->o + qo, hn * q_elems * sizeof(float), cudaMemcpyDeviceToHost, ctx.d2h));
+    }
+    TM_TRY(cudaEventRecord(done, ctx.d2h));
+    return cudaStreamWaitEvent(stream, done, 0);
+}
+
+#undef TM_TRY
+
 }  // namespace
 
 // ------------------------------------------------------------- C++ drop-in API
@@ -179,6 +295,16 @@ int tilemix_attention_batched(const void* Q, const void* K, const void* V, float
                                            static_cast<const __half*>(V), O, heads, M, N, d,
                                            score_scale, causal != 0, static_cast<cudaStream_t>(stream),
                                            to_cpp(routing), to_cpp(quantized)));
+}
+
+int tilemix_attention_from_host(const void* hQ, const void* hK, const void* hV, const uint64_t* h_words,
+                                float* hO, const tilemix_device_buffers* dev, int heads, int M, int N, int d,
+                                float score_scale, int causal, int key_tiles_per_group, int chunk_heads,
+                                void* stream) {
+    return static_cast<int>(from_host_impl(static_cast<const __half*>(hQ), static_cast<const __half*>(hK),
+                                           static_cast<const __half*>(hV), h_words, hO, dev, heads, M, N, d,
+                                           score_scale, causal != 0, key_tiles_per_group, chunk_heads,
+                                           static_cast<cudaStream_t>(stream)));
 }
 
 size_t tilemix_routing_word_count_c(int M, int N, int key_tiles_per_group) {

@@ -42,6 +42,11 @@ class _Quantized(ctypes.Structure):
     _fields_ = [("q", _P), ("k", _P), ("q_scales", _P), ("k_scales", _P), ("score_dots", _P)]
 
 
+class _DeviceBuffers(ctypes.Structure):
+    _fields_ = [("q", _P), ("k", _P), ("v", _P), ("q8", _P), ("k8", _P), ("q_scales", _P),
+                ("k_scales", _P), ("words", _P), ("o", _P)]
+
+
 def _load():
     if not LIB_PATH.exists():
         raise RuntimeError(f"{LIB_PATH} is not built; run __graft_entry__.build() "
@@ -68,6 +73,9 @@ def _load():
     lib.tilemix_reference_shared_bytes.restype = ctypes.c_size_t
     lib.tilemix_b200_shared_bytes_c.argtypes = [_I, _I]
     lib.tilemix_b200_shared_bytes_c.restype = ctypes.c_size_t
+    lib.tilemix_attention_from_host.argtypes = [_P, _P, _P, _P, _P, ctypes.POINTER(_DeviceBuffers),
+                                                _I, _I, _I, _I, ctypes.c_float, _I, _I, _I, _P]
+    lib.tilemix_attention_from_host.restype = _I
     lib.tilemix_read_and_clear_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
     lib.tilemix_read_and_clear_status.restype = _I
     return lib
@@ -78,7 +86,7 @@ lib = _load()
 # every symbol include/tilemix_c_api.h declares
 C_ABI_SYMBOLS = (
     "tilemix_abi_version", "tilemix_quantize_qk", "tilemix_fused_attention",
-    "tilemix_quantize_qk_batched", "tilemix_attention_batched",
+    "tilemix_quantize_qk_batched", "tilemix_attention_batched", "tilemix_attention_from_host",
     "tilemix_routing_word_count_c", "tilemix_routing_words_per_row_c",
     "tilemix_reference_shared_bytes", "tilemix_b200_shared_bytes_c",
     "tilemix_read_and_clear_status",
@@ -180,6 +188,48 @@ def tilemix_attention_batched(Q, K, V, O, heads: int, M: int, N: int, d: int,
     return lib.tilemix_attention_batched(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
                                          float(score_scale), int(bool(causal)), _stream(stream),
                                          ctypes.byref(r), ctypes.byref(q))
+
+
+def _host_addr(x) -> int | None:
+    """Host address of a CPU torch tensor / numpy array / raw int / None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x or None
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr() or None
+    return x.ctypes.data or None
+
+
+@dataclass
+class TileMixDeviceBuffers:
+    """Device buffers of tilemix_attention_from_host, sized for all heads."""
+    q: object = None
+    k: object = None
+    v: object = None
+    q8: object = None
+    k8: object = None
+    q_scales: object = None
+    k_scales: object = None
+    words: object = None
+    o: object = None
+
+    def _c(self) -> _DeviceBuffers:
+        return _DeviceBuffers(*(_addr(getattr(self, f)) for f, _ in _DeviceBuffers._fields_))
+
+
+def tilemix_attention_from_host(hQ, hK, hV, h_words, hO, dev: TileMixDeviceBuffers, heads: int,
+                                M: int, N: int, d: int, score_scale: float, causal: bool = False,
+                                key_tiles_per_group: int = 2, chunk_heads: int = 0,
+                                stream=None) -> int:
+    """H2D copies, quantization, routed attention and the D2H copy of O for
+    host (pinned) buffers, pipelined over chunks of heads. Returns a cudaError_t code."""
+    b = dev._c() if dev is not None else None
+    return lib.tilemix_attention_from_host(_host_addr(hQ), _host_addr(hK), _host_addr(hV),
+                                           _host_addr(h_words), _host_addr(hO),
+                                           ctypes.byref(b) if b is not None else None,
+                                           heads, M, N, d, float(score_scale), int(bool(causal)),
+                                           key_tiles_per_group, chunk_heads, _stream(stream))
 
 
 def read_and_clear_status() -> tuple[int, int]:
