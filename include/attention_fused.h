@@ -123,3 +123,31 @@ cudaError_t tilemix_attention_batched(const __half* Q, const __half* K, const __
                                       cudaStream_t stream = nullptr,
                                       const TileMixRouting& routing = {},
                                       const TileMixQuantized& quantized = {});
+
+// Output element types of TileMixOutput.
+enum TileMixOutputType : int { kTileMixOutF32 = 0, kTileMixOutF16 = 1, kTileMixOutBF16 = 2 };
+
+// A strided output: head h = b * heads_per_batch + hh (of `heads`), row m,
+// column c is written at data + b * stride_batch + hh * stride_head +
+// m * stride_row + c (strides in elements), rounded to nearest even for fp16
+// and bf16. A [B, S, H, D] (BSHD) tensor is heads_per_batch = H,
+// stride_batch = S * H * D, stride_head = D, stride_row = H * D.
+struct TileMixOutput {
+    void* data = nullptr;
+    int dtype = kTileMixOutF32;
+    int heads_per_batch = 1;
+    long long stride_batch = 0;
+    long long stride_head = 0;
+    long long stride_row = 0;
+};
+
+// tilemix_attention_batched with the output written through `out` (the values
+// stored are the roundings of the fp32 outputs tilemix_attention_batched
+// produces). Routing trace outputs (decoded_bits, score_dots) are not
+// supported here: cudaErrorNotSupported.
+cudaError_t tilemix_attention_batched_out(const __half* Q, const __half* K, const __half* V,
+                                          const TileMixOutput& out, int heads, int M, int N, int d,
+                                          float score_scale, bool causal,
+                                          cudaStream_t stream = nullptr,
+                                          const TileMixRouting& routing = {},
+                                          const TileMixQuantized& quantized = {});

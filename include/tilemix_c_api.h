@@ -61,6 +61,32 @@ int tilemix_attention_batched(const void* Q, const void* K, const void* V, float
                               void* stream, const tilemix_routing* routing,
                               const tilemix_quantized* quantized);
 
+/* Strided output of tilemix_attention_batched_out (layout-compatible with
+ * TileMixOutput in attention_fused.h): head h = b * heads_per_batch + hh,
+ * row m, column c goes to data + b * stride_batch + hh * stride_head +
+ * m * stride_row + c (element units), as fp32 (dtype 0), fp16 (1) or bf16 (2),
+ * rounded to nearest even. BSHD [B, S, H, D]: heads_per_batch = H,
+ * stride_batch = S*H*D, stride_head = D, stride_row = H*D. */
+typedef struct tilemix_output {
+    void* data;
+    int dtype;
+    int heads_per_batch;
+    long long stride_batch;
+    long long stride_head;
+    long long stride_row;
+} tilemix_output;
+
+/* tilemix_attention_batched writing O through `out` (no reference
+ * counterpart: the reference writes fp32 [M, d] only, include/attention_fused.h:68-69).
+ * Invalid layouts (null data, bad dtype, heads_per_batch < 1 or not dividing
+ * heads, negative strides) return cudaErrorInvalidValue; routing trace
+ * outputs together with a strided output return cudaErrorNotSupported. */
+int tilemix_attention_batched_out(const void* Q, const void* K, const void* V,
+                                  const tilemix_output* out, int heads, int M, int N, int d,
+                                  float score_scale, int causal, void* stream,
+                                  const tilemix_routing* routing,
+                                  const tilemix_quantized* quantized);
+
 /* Caller-owned device buffers of tilemix_attention_from_host, each sized for
  * all `heads` heads: q, k, v fp16 [heads, M|N, d]; q8, k8 int8 of the same
  * shapes; q_scales fp16 [heads, ceil(M/128)]; k_scales fp16 [heads, ceil(N/64)];

@@ -126,3 +126,23 @@ def test_from_host_validation_without_cuda():
     # routed (host words given) needs every quantized device buffer
     assert f(X, X, X, X, X, tm.TileMixDeviceBuffers(X, X, X, o=X), 1, 4, 4, 16, 1.0) == INVALID
     assert f(X, X, X, X, X, full, 1, 4, 4, 129, 1.0) == NOT_SUPPORTED
+
+
+def test_strided_output_validation_without_cuda():
+    """tilemix_attention_batched_out rejects bad output layouts before any CUDA call."""
+    x = ctypes.create_string_buffer(64)
+    X = ctypes.addressof(x)
+    f = tm.tilemix_attention_batched_out
+    ok = tm.TileMixOutput(X, tm.kTileMixOutF16, 2, 0, 0, 0)
+    assert f(X, X, X, None, 2, 4, 4, 16, 1.0) == INVALID
+    assert f(X, X, X, tm.TileMixOutput(None, 1, 2), 2, 4, 4, 16, 1.0) == INVALID
+    for dtype in (-1, 3):
+        assert f(X, X, X, tm.TileMixOutput(X, dtype, 2), 2, 4, 4, 16, 1.0) == INVALID
+    assert f(X, X, X, tm.TileMixOutput(X, 1, 0), 2, 4, 4, 16, 1.0) == INVALID
+    assert f(X, X, X, tm.TileMixOutput(X, 1, 3), 2, 4, 4, 16, 1.0) == INVALID      # 3 does not divide 2
+    for strides in ((-1, 0, 0), (0, -1, 0), (0, 0, -1)):
+        assert f(X, X, X, tm.TileMixOutput(X, 1, 2, *strides), 2, 4, 4, 16, 1.0) == INVALID
+    assert f(X, X, X, ok, 2, 4, 4, 129, 1.0) == NOT_SUPPORTED
+    # trace outputs are not available with a strided output
+    quant = tm.TileMixQuantized(X, X, X, X, score_dots=X)
+    assert f(X, X, X, ok, 2, 4, 4, 16, 1.0, quantized=quant) == NOT_SUPPORTED

@@ -17,6 +17,7 @@ from tilemix_b200 import ops  # noqa: F401  (registers torch.ops.tilemix.*)
 def test_ops_registered():
     assert hasattr(torch.ops.tilemix, "quantize_qk")
     assert hasattr(torch.ops.tilemix, "attention")
+    assert hasattr(torch.ops.tilemix, "attention_bshd")
 
 
 def test_fake_shapes():
@@ -33,6 +34,8 @@ def test_fake_shapes():
         assert o.shape == q.shape and o.dtype == torch.float32
         o2 = torch.ops.tilemix.attention(q[0], k[0], v[0], None, None, None, None, None, 2, 0.088, False)
         assert o2.shape == (300, 128) and o2.dtype == torch.float32
+        o3 = torch.ops.tilemix.attention_bshd(q, k, v, q8, k8, qs, ks, words, 2, 0.088, True, 3, torch.bfloat16)
+        assert o3.shape == (1, 300, 3, 128) and o3.dtype == torch.bfloat16
 
 
 @pytest.mark.gpu
@@ -61,3 +64,19 @@ def test_ops_match_c_abi_bitwise():
     assert torch.equal(o2, e)
     err, status = tm.read_and_clear_status()
     assert err == 0 and status == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_attention_bshd_op_is_rounded_default(dtype):
+    """torch.ops.tilemix.attention_bshd == the fp32 operator's output, permuted
+    to [B, S, H, D] and rounded to the requested type."""
+    from tilemix_b200 import workloads
+    B, H = 2, 2
+    w = workloads.make_inputs("c3", batch=B, heads=H, seq=256)
+    q, k, v = (w[n].cuda() for n in ("q", "k", "v"))
+    q8, k8, qs, ks = torch.ops.tilemix.quantize_qk(q, k)
+    words = w["words"].cuda().view(torch.int64)
+    ref = torch.ops.tilemix.attention(q, k, v, q8, k8, qs, ks, words, 2, w["score_scale"], True)
+    got = torch.ops.tilemix.attention_bshd(q, k, v, q8, k8, qs, ks, words, 2, w["score_scale"], True, H, dtype)
+    assert torch.equal(got, ref.view(B, H, 256, -1).permute(0, 2, 1, 3).to(dtype))

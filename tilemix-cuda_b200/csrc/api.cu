@@ -52,9 +52,10 @@ cudaError_t quantize_impl(const __half* Q, const __half* K, std::int8_t* Q8, std
 
 cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, float* O, int heads,
                            int M, int N, int d, float score_scale, bool causal, cudaStream_t stream,
-                           const TileMixRouting& routing, const TileMixQuantized& quantized) {
+                           const TileMixRouting& routing, const TileMixQuantized& quantized,
+                           const TileMixOutput* strided = nullptr) {
     // Same checks, same order as src/tilemix.cu:242-253.
-    if (!Q || !K || !V || !O || heads <= 0 || M <= 0 || N <= 0 || d <= 0 ||
+    if (!Q || !K || !V || (!O && !strided) || heads <= 0 || M <= 0 || N <= 0 || d <= 0 ||
         !std::isfinite(score_scale) || routing.key_tiles_per_group <= 0 ||
         (!routing.words && routing.word_count != 0)) {
         return cudaErrorInvalidValue;
@@ -69,6 +70,14 @@ cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, fl
                                quantized.score_dots;
     if ((any_quantized && !has_quantized) || (routing.words && !has_quantized)) return cudaErrorInvalidValue;
     if (!fits(heads, M, d) || !fits(heads, N, d)) return cudaErrorInvalidValue;
+    if (strided) {
+        if (!strided->data || strided->dtype < kTileMixOutF32 || strided->dtype > kTileMixOutBF16 ||
+            strided->heads_per_batch < 1 || heads % strided->heads_per_batch != 0 || strided->stride_batch < 0 ||
+            strided->stride_head < 0 || strided->stride_row < 0) {
+            return cudaErrorInvalidValue;
+        }
+        if (routing.decoded_bits || quantized.score_dots) return cudaErrorNotSupported;
+    }
     cudaError_t status = check_device();
     if (status != cudaSuccess) return status;
     if (static_cast<long long>((M - 1) / 128 + 1) * heads > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
@@ -86,6 +95,14 @@ cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, fl
     prob.heads = heads; prob.M = M; prob.N = N; prob.d = d;
     prob.score_scale = score_scale;
     prob.causal = causal;
+    if (strided) {
+        prob.o_data = strided->data;
+        prob.o_dtype = strided->dtype;
+        prob.o_heads_per_batch = strided->heads_per_batch;
+        prob.o_stride_batch = strided->stride_batch;
+        prob.o_stride_head = strided->stride_head;
+        prob.o_stride_row = strided->stride_row;
+    }
     return tilemix::launch_attention(prob, stream);
 }
 
@@ -258,6 +275,14 @@ cudaError_t tilemix_attention_batched(const __half* Q, const __half* K, const __
     return attention_impl(Q, K, V, O, heads, M, N, d, score_scale, causal, stream, routing, quantized);
 }
 
+cudaError_t tilemix_attention_batched_out(const __half* Q, const __half* K, const __half* V,
+                                          const TileMixOutput& out, int heads, int M, int N, int d,
+                                          float score_scale, bool causal, cudaStream_t stream,
+                                          const TileMixRouting& routing, const TileMixQuantized& quantized) {
+    return attention_impl(Q, K, V, nullptr, heads, M, N, d, score_scale, causal, stream, routing, quantized,
+                          &out);
+}
+
 // ---------------------------------------------------------------------- C-ABI
 extern "C" {
 
@@ -295,6 +320,23 @@ int tilemix_attention_batched(const void* Q, const void* K, const void* V, float
                                            static_cast<const __half*>(V), O, heads, M, N, d,
                                            score_scale, causal != 0, static_cast<cudaStream_t>(stream),
                                            to_cpp(routing), to_cpp(quantized)));
+}
+
+int tilemix_attention_batched_out(const void* Q, const void* K, const void* V, const tilemix_output* out,
+                                  int heads, int M, int N, int d, float score_scale, int causal, void* stream,
+                                  const tilemix_routing* routing, const tilemix_quantized* quantized) {
+    if (!out) return static_cast<int>(cudaErrorInvalidValue);
+    TileMixOutput o;
+    o.data = out->data;
+    o.dtype = out->dtype;
+    o.heads_per_batch = out->heads_per_batch;
+    o.stride_batch = out->stride_batch;
+    o.stride_head = out->stride_head;
+    o.stride_row = out->stride_row;
+    return static_cast<int>(attention_impl(static_cast<const __half*>(Q), static_cast<const __half*>(K),
+                                           static_cast<const __half*>(V), nullptr, heads, M, N, d, score_scale,
+                                           causal != 0, static_cast<cudaStream_t>(stream), to_cpp(routing),
+                                           to_cpp(quantized), &o));
 }
 
 int tilemix_attention_from_host(const void* hQ, const void* hK, const void* hV, const uint64_t* h_words,

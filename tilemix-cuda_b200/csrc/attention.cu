@@ -204,6 +204,11 @@ struct Params {
     int f16_ksteps, i8_ksteps, pv_n;
     int o_vec;
     int head_group;      // heads scheduled together (their K/V stay L2-resident)
+    // strided output (kStrided variants)
+    void* o_data;
+    int o_dtype;         // 0 fp32, 1 fp16, 2 bf16
+    int o_hpb;           // heads per batch
+    long long o_sb, o_sh, o_sm;
 };
 
 // Bounded wait, called by all 32 lanes of a warp; returns a warp-uniform
@@ -358,7 +363,54 @@ __device__ void manual_tile_i8(uint8_t* dst, const std::int8_t* src, int row0, i
     }
 }
 
-template <int kAtoms, bool kUseTma, bool kTrace>
+// Strided output: 32 consecutive columns [c, c + 32) of one row, starting at
+// element offset row_off, as fp32 / fp16 / bf16 (round to nearest even).
+// 16-byte stores when p.o_vec says the base, the strides and d allow them.
+__device__ __forceinline__ void store_strided_row(const Params& p, long long row_off, int c,
+                                                  const uint32_t (&x)[32]) {
+    if (p.o_dtype == 0) {
+        float* out = static_cast<float*>(p.o_data) + row_off;
+        if (p.o_vec) {
+            #pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+                if (c + i < p.d) {
+                    reinterpret_cast<float4*>(out + c + i)[0] = make_float4(
+                        __uint_as_float(x[i]), __uint_as_float(x[i + 1]),
+                        __uint_as_float(x[i + 2]), __uint_as_float(x[i + 3]));
+                }
+            }
+        } else {
+            #pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                if (c + i < p.d) out[c + i] = __uint_as_float(x[i]);
+            }
+        }
+        return;
+    }
+    uint32_t h[16];
+    #pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        h[i] = p.o_dtype == 1 ? pack_half2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1]))
+                              : pack_bf162(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1]));
+    }
+    uint16_t* out = static_cast<uint16_t*>(p.o_data) + row_off;
+    if (p.o_vec) {
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (c + 8 * i < p.d) {
+                reinterpret_cast<uint4*>(out + c + 8 * i)[0] =
+                    make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+            }
+        }
+    } else {
+        #pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (c + i < p.d) out[c + i] = static_cast<uint16_t>((i & 1) ? h[i >> 1] >> 16 : h[i >> 1] & 0xffffu);
+        }
+    }
+}
+
+template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
@@ -903,17 +955,28 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const float inv_l = 1.0f / (l_run * a_me + l_oth * a_oth);
                 const float w_me = a_me * inv_l, w_oth = a_oth * inv_l;
                 const uint32_t o_oth = tmem + lane_base + kColO + 128u * (half ^ 1);
+                // fp32 O in [heads][M][d], or the strided output's row
                 float* out = p.o + (static_cast<std::size_t>(head) * p.M + q_row) * p.d;
+                long long row_off = 0;
+                if (kStrided) {
+                    const int hb = head / p.o_hpb;
+                    row_off = hb * p.o_sb + (head - hb * p.o_hpb) * p.o_sh + static_cast<long long>(q_row) * p.o_sm;
+                }
                 #pragma unroll 1
                 for (int c = 64 * half; c < 64 * half + 64 && c < p.pv_n; c += 32) {
                     tmem_ld32(o_addr + c, xa);
                     tmem_ld32(o_oth + c, xb);
                     tc_wait_ld();
+                    // explicit roundings, so every output variant stores (a
+                    // rounding of) the same fp32 value
                     #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        xa[i] = __float_as_uint(__uint_as_float(xa[i]) * w_me + __uint_as_float(xb[i]) * w_oth);
+                        xa[i] = __float_as_uint(__fmaf_rn(__uint_as_float(xa[i]), w_me,
+                                                          __fmul_rn(__uint_as_float(xb[i]), w_oth)));
                     }
-                    if (row_valid) {
+                    if (kStrided) {
+                        if (row_valid) store_strided_row(p, row_off, c, xa);
+                    } else if (row_valid) {
                         if (p.o_vec) {
                             #pragma unroll
                             for (int i = 0; i < 32; i += 4) {
@@ -979,9 +1042,9 @@ bool encode_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, in
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int kAtoms, bool kUseTma, bool kTrace>
+template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided = false>
 cudaError_t launch_variant(const CUtensorMap* maps, const Params& p, unsigned grid, cudaStream_t stream) {
-    auto kernel = tilemix_attention_kernel<kAtoms, kUseTma, kTrace>;
+    auto kernel = tilemix_attention_kernel<kAtoms, kUseTma, kTrace, kStrided>;
     const int smem = static_cast<int>(SmemLayout<kAtoms>::kBytes);
     // The opt-in attribute is per device; set it the first time a device is seen.
     static int configured[64] = {0};
@@ -1037,6 +1100,19 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     p.i8_ksteps = (prob.d + 31) / 32;
     p.pv_n = (prob.d + 15) / 16 * 16;
     p.o_vec = (prob.d % 4 == 0 && aligned16(prob.o)) ? 1 : 0;
+    const bool strided = prob.o_data != nullptr;
+    if (strided) {
+        p.o_data = prob.o_data;
+        p.o_dtype = prob.o_dtype;
+        p.o_hpb = prob.o_heads_per_batch;
+        p.o_sb = prob.o_stride_batch;
+        p.o_sh = prob.o_stride_head;
+        p.o_sm = prob.o_stride_row;
+        // 16-byte stores need the base, every stride and d in 16-byte units
+        const long long unit = prob.o_dtype == 0 ? 4 : 8;     // elements per 16 bytes
+        p.o_vec = (prob.d % unit == 0 && p.o_sb % unit == 0 && p.o_sh % unit == 0 && p.o_sm % unit == 0 &&
+                   aligned16(prob.o_data)) ? 1 : 0;
+    }
     p.head_group = std::min(prob.heads, 8);
 
     const long long grid = static_cast<long long>(p.q_tiles) * p.heads;
@@ -1058,6 +1134,13 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
         }
     }
     const unsigned g = static_cast<unsigned>(grid);
+    if (strided) {
+        // strided outputs carry no trace outputs (checked by the API layer)
+        if (atoms == 1) return tma ? launch_variant<1, true, false, true>(maps, p, g, stream)
+                                   : launch_variant<1, false, false, true>(maps, p, g, stream);
+        return tma ? launch_variant<2, true, false, true>(maps, p, g, stream)
+                   : launch_variant<2, false, false, true>(maps, p, g, stream);
+    }
     if (atoms == 1) {
         if (tma) return trace ? launch_variant<1, true, true>(maps, p, g, stream)
                               : launch_variant<1, true, false>(maps, p, g, stream);

@@ -35,6 +35,14 @@ struct AttentionProblem {
     int key_tiles_per_group;
     float score_scale;
     bool causal;
+    // Optional strided output (used instead of `o` when o_data is set):
+    // element (row m, column c) of head h = b * o_heads_per_batch + hh sits at
+    // o_data + b * o_stride_batch + hh * o_stride_head + m * o_stride_row + c
+    // (element units), as fp32 (o_dtype 0), fp16 (1) or bf16 (2).
+    void* o_data;
+    int o_dtype;
+    int o_heads_per_batch;
+    long long o_stride_batch, o_stride_head, o_stride_row;
 };
 
 // Shared memory the attention kernel requests for head dim d.

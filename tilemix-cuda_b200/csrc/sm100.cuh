@@ -5,6 +5,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ != 1000)
@@ -316,6 +317,11 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);   // .x (low 16 bits) = lo
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);   // .x (low 16 bits) = lo
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 

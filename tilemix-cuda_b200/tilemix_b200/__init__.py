@@ -42,6 +42,11 @@ class _Quantized(ctypes.Structure):
     _fields_ = [("q", _P), ("k", _P), ("q_scales", _P), ("k_scales", _P), ("score_dots", _P)]
 
 
+class _Output(ctypes.Structure):
+    _fields_ = [("data", _P), ("dtype", _I), ("heads_per_batch", _I), ("stride_batch", ctypes.c_longlong),
+                ("stride_head", ctypes.c_longlong), ("stride_row", ctypes.c_longlong)]
+
+
 class _DeviceBuffers(ctypes.Structure):
     _fields_ = [("q", _P), ("k", _P), ("v", _P), ("q8", _P), ("k8", _P), ("q_scales", _P),
                 ("k_scales", _P), ("words", _P), ("o", _P)]
@@ -73,6 +78,10 @@ def _load():
     lib.tilemix_reference_shared_bytes.restype = ctypes.c_size_t
     lib.tilemix_b200_shared_bytes_c.argtypes = [_I, _I]
     lib.tilemix_b200_shared_bytes_c.restype = ctypes.c_size_t
+    lib.tilemix_attention_batched_out.argtypes = [_P, _P, _P, ctypes.POINTER(_Output), _I, _I, _I, _I,
+                                                  ctypes.c_float, _I, _P, ctypes.POINTER(_Routing),
+                                                  ctypes.POINTER(_Quantized)]
+    lib.tilemix_attention_batched_out.restype = _I
     lib.tilemix_attention_from_host.argtypes = [_P, _P, _P, _P, _P, ctypes.POINTER(_DeviceBuffers),
                                                 _I, _I, _I, _I, ctypes.c_float, _I, _I, _I, _P]
     lib.tilemix_attention_from_host.restype = _I
@@ -86,7 +95,8 @@ lib = _load()
 # every symbol include/tilemix_c_api.h declares
 C_ABI_SYMBOLS = (
     "tilemix_abi_version", "tilemix_quantize_qk", "tilemix_fused_attention",
-    "tilemix_quantize_qk_batched", "tilemix_attention_batched", "tilemix_attention_from_host",
+    "tilemix_quantize_qk_batched", "tilemix_attention_batched", "tilemix_attention_batched_out",
+    "tilemix_attention_from_host",
     "tilemix_routing_word_count_c", "tilemix_routing_words_per_row_c",
     "tilemix_reference_shared_bytes", "tilemix_b200_shared_bytes_c",
     "tilemix_read_and_clear_status",
@@ -188,6 +198,51 @@ def tilemix_attention_batched(Q, K, V, O, heads: int, M: int, N: int, d: int,
     return lib.tilemix_attention_batched(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
                                          float(score_scale), int(bool(causal)), _stream(stream),
                                          ctypes.byref(r), ctypes.byref(q))
+
+
+kTileMixOutF32, kTileMixOutF16, kTileMixOutBF16 = 0, 1, 2
+
+
+@dataclass
+class TileMixOutput:
+    """Strided output (include/attention_fused.h TileMixOutput): head
+    h = b * heads_per_batch + hh, row m, column c at data + b * stride_batch +
+    hh * stride_head + m * stride_row + c, in elements of `dtype`."""
+    data: object = None
+    dtype: int = kTileMixOutF32
+    heads_per_batch: int = 1
+    stride_batch: int = 0
+    stride_head: int = 0
+    stride_row: int = 0
+
+    def _c(self) -> _Output:
+        return _Output(_addr(self.data), int(self.dtype), int(self.heads_per_batch), int(self.stride_batch),
+                       int(self.stride_head), int(self.stride_row))
+
+    @classmethod
+    def bshd(cls, tensor, heads_per_batch: int):
+        """A [B, S, H, D] torch tensor (fp32 / fp16 / bf16, contiguous or strided)."""
+        import torch
+        dt = {torch.float32: kTileMixOutF32, torch.float16: kTileMixOutF16,
+              torch.bfloat16: kTileMixOutBF16}[tensor.dtype]
+        sb, ss, sh, sd = tensor.stride()
+        if sd != 1:
+            raise ValueError("the head dimension must be contiguous")
+        return cls(tensor, dt, heads_per_batch, sb, sh, ss)
+
+
+def tilemix_attention_batched_out(Q, K, V, out: TileMixOutput | None, heads: int, M: int, N: int, d: int,
+                                  score_scale: float, causal: bool = False, stream=None,
+                                  routing: TileMixRouting | None = None,
+                                  quantized: TileMixQuantized | None = None) -> int:
+    """tilemix_attention_batched writing O through a strided fp32/fp16/bf16 output."""
+    r = (routing or TileMixRouting())._c()
+    q = (quantized or TileMixQuantized())._c()
+    o = out._c() if out is not None else None
+    return lib.tilemix_attention_batched_out(_addr(Q), _addr(K), _addr(V),
+                                             ctypes.byref(o) if o is not None else None, heads, M, N, d,
+                                             float(score_scale), int(bool(causal)), _stream(stream),
+                                             ctypes.byref(r), ctypes.byref(q))
 
 
 def _host_addr(x) -> int | None:

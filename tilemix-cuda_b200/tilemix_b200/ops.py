@@ -1,5 +1,5 @@
-"""PyTorch operators over the C-ABI: ``torch.ops.tilemix.quantize_qk`` and
-``torch.ops.tilemix.attention``.
+"""PyTorch operators over the C-ABI: ``torch.ops.tilemix.quantize_qk``,
+``torch.ops.tilemix.attention`` and ``torch.ops.tilemix.attention_bshd``.
 
 They call the same extern "C" entry points as the ctypes functions in
 ``tilemix_b200`` (``tilemix_quantize_qk_batched``, ``tilemix_attention_batched``)
@@ -16,8 +16,8 @@ import math
 
 import torch
 
-from . import (TileMixQuantized, TileMixRouting, check, quantize_tilemix_qk_batched,
-               tilemix_attention_batched)
+from . import (TileMixOutput, TileMixQuantized, TileMixRouting, check, quantize_tilemix_qk_batched,
+               tilemix_attention_batched, tilemix_attention_batched_out)
 
 _Q_ROWS, _K_ROWS = 128, 64   # quantization block rows (include/attention_fused.h:13-14)
 
@@ -74,6 +74,33 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q8: torch.Tenso
 @attention.register_fake
 def _(q, k, v, q8, k8, q_scales, k_scales, words, key_tiles_per_group, score_scale, causal):
     return q.new_empty(q.shape, dtype=torch.float32)
+
+
+@torch.library.custom_op("tilemix::attention_bshd", mutates_args=())
+def attention_bshd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q8: torch.Tensor | None,
+                   k8: torch.Tensor | None, q_scales: torch.Tensor | None, k_scales: torch.Tensor | None,
+                   words: torch.Tensor | None, key_tiles_per_group: int, score_scale: float, causal: bool,
+                   heads_per_batch: int, out_dtype: torch.dtype) -> torch.Tensor:
+    """``attention`` with the output written by the kernel as [B, S, H, D]
+    (heads = B * H of q's [heads, S, d]) in fp32, fp16 or bf16 (rounded to
+    nearest even from the fp32 result)."""
+    q3, k3, v3 = _heads3(q).contiguous(), _heads3(k).contiguous(), _heads3(v).contiguous()
+    heads, m, d = q3.shape
+    n = k3.shape[1]
+    out = torch.empty((heads // heads_per_batch, m, heads_per_batch, d), dtype=out_dtype, device=q.device)
+    routing = TileMixRouting(words, 0 if words is None else words.numel(), key_tiles_per_group)
+    quantized = TileMixQuantized(q8, k8, q_scales, k_scales) if q8 is not None else None
+    check(tilemix_attention_batched_out(q3, k3, v3, TileMixOutput.bshd(out, heads_per_batch), heads, m, n, d,
+                                        score_scale, causal, torch.cuda.current_stream(q.device), routing,
+                                        quantized), "tilemix::attention_bshd")
+    return out
+
+
+@attention_bshd.register_fake
+def _(q, k, v, q8, k8, q_scales, k_scales, words, key_tiles_per_group, score_scale, causal, heads_per_batch,
+      out_dtype):
+    heads = 1 if q.dim() == 2 else q.shape[0]
+    return q.new_empty((heads // heads_per_batch, q.shape[-2], heads_per_batch, q.shape[-1]), dtype=out_dtype)
 
 
 def tilemix_attention(q, k, v, words=None, *, key_tiles_per_group: int = 2, score_scale: float | None = None,
