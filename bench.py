@@ -141,8 +141,10 @@ def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    # keep stdout to the one JSON line (NCCL would print its version banner there)
-    os.environ.setdefault("NCCL_DEBUG", "WARN")
+    # Keep stdout to the one JSON line: NCCL writes its log (and, at
+    # NCCL_DEBUG=WARN or VERSION, a version banner) to stdout unless
+    # NCCL_DEBUG_FILE names another file.
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     if world > 1:
         import torch.distributed as dist
         if args.impl == "tilemix":
@@ -180,6 +182,8 @@ def cpu_reference_sample(w_host: dict, cfg: dict, target_s: float) -> dict:
         oracle.build()
     kind = "reference" if oracle.ref_available() else "port"
     use_ref = kind == "reference"
+    # every host core this process may use (torchrun sets OMP_NUM_THREADS=1)
+    oracle.set_threads(len(os.sched_getaffinity(0)))
     q, k, v = w_host["q"], w_host["k"], w_host["v"]
     avail, S, D = q.shape
     H = cfg["B"] * cfg["H"]            # heads of the whole workload

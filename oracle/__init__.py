@@ -75,6 +75,7 @@ def lib():
         _lib.orc_dense_attention.argtypes = [_P, _P, _P, _I, _I, _I, _P]
         _lib.orc_reference_inputs.argtypes = [_I, _I, _I, _P, _P, _P]
         _lib.orc_max_threads.restype = _I
+        _lib.orc_set_threads.argtypes = [_I]
     return _lib
 
 
@@ -95,6 +96,7 @@ def ref_lib():
         _ref.ref_tilemix_sampled.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _F,
                                              _I, _P, _I, _P, _I, _P]
         _ref.ref_max_threads.restype = _I
+        _ref.ref_set_threads.argtypes = [_I]
     return _ref
 
 
@@ -269,6 +271,14 @@ def dense_attention(q, k, v) -> np.ndarray:
 
 def max_threads() -> int:
     return int(lib().orc_max_threads())
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads of both CPU checkers' later parallel regions on the
+    calling thread (the reference build's too, when present)."""
+    lib().orc_set_threads(int(n))
+    if ref_available():
+        ref_lib().ref_set_threads(int(n))
 
 
 # ---------------------------------------------- the reference's own functions

@@ -120,4 +120,14 @@ int ref_max_threads(void) {
 #endif
 }
 
+// Thread count for the calling thread's later OpenMP regions (n > 0); a
+// launcher such as torchrun may have set OMP_NUM_THREADS=1 for the process.
+void ref_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 }  // extern "C"

@@ -316,3 +316,11 @@ int orc_max_threads(void) {
     return 1;
 #endif
 }
+
+void orc_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}

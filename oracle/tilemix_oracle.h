@@ -97,6 +97,8 @@ void orc_dense_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v
 void orc_reference_inputs(int m, int n, int d, uint16_t* q, uint16_t* k, uint16_t* v);
 
 int orc_max_threads(void);
+/* Thread count of the calling thread's later OpenMP regions (n > 0). */
+void orc_set_threads(int n);
 
 #ifdef __cplusplus
 }
