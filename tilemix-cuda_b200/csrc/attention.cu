@@ -203,6 +203,7 @@ struct Params {
     int routed;
     int f16_ksteps, i8_ksteps, pv_n;
     int o_vec;
+    int o_tma;           // fp32 O written by TMA stores from shared memory
     int head_group;      // heads scheduled together (their K/V stay L2-resident)
     // strided output (kStrided variants)
     void* o_data;
@@ -417,6 +418,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_v,
                          const __grid_constant__ CUtensorMap tm_q8,
                          const __grid_constant__ CUtensorMap tm_k8,
+                         const __grid_constant__ CUtensorMap tm_o,
                          const Params p) {
     using L = SmemLayout<kAtoms>;
     extern __shared__ uint8_t smem_raw[];
@@ -976,6 +978,23 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     }
                     if (kStrided) {
                         if (row_valid) store_strided_row(p, row_off, c, xa);
+                    } else if (p.o_tma) {
+                        // Coalesced output: the warp stages its 32 rows x 32
+                        // columns in shared memory (the K stages: every MMA has
+                        // completed), 128-byte swizzled as the TMA store
+                        // expects, and one lane stores the box.
+                        const uint32_t box_off = L::kK + static_cast<uint32_t>(c >> 5) * 16384u +
+                                                 static_cast<uint32_t>(warp & 3) * 4096u;
+                        #pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const uint32_t off = box_off + lane * 128u + ((static_cast<uint32_t>(i) ^ (lane & 7u)) << 4);
+                            *reinterpret_cast<uint4*>(smem + off) = make_uint4(xa[4 * i], xa[4 * i + 1], xa[4 * i + 2],
+                                                                               xa[4 * i + 3]);
+                        }
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        const int y0 = qt * kTileRows + (warp & 3) * 32;
+                        if (lane == 0 && y0 < p.M && c < p.d) tma_store_3d(&tm_o, sbase + box_off, c, y0, head);
                     } else if (row_valid) {
                         if (p.o_vec) {
                             #pragma unroll
@@ -993,6 +1012,11 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                             }
                         }
                     }
+                }
+                if (!kStrided && p.o_tma && lane == 0) {
+                    // the stores must have read shared memory before the CTA exits
+                    bulk_commit_group();
+                    bulk_wait_group_read0();
                 }
             }
         }
@@ -1028,14 +1052,14 @@ EncodeTiledFn encode_fn() {
 
 // 3-D map over [heads][rows][d] with a 128-byte-swizzled {box_x, 128, 1} box.
 bool encode_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int elem_bytes,
-                int heads, int rows, int d, int box_x) {
+                int heads, int rows, int d, int box_x, int box_y = 128) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(rows),
                                 static_cast<cuuint64_t>(heads)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * elem_bytes,
                                    static_cast<cuuint64_t>(rows) * d * elem_bytes};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_x), 128u, 1u};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_x), static_cast<cuuint32_t>(box_y), 1u};
     const cuuint32_t elem_strides[3] = {1u, 1u, 1u};
     return fn(map, type, 3, const_cast<void*>(base), dims, strides, box, elem_strides,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1057,7 +1081,7 @@ cudaError_t launch_variant(const CUtensorMap* maps, const Params& p, unsigned gr
         if (status != cudaSuccess) return status;
         configured[device] = 1;
     }
-    kernel<<<grid, kAttnThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], p);
+    kernel<<<grid, kAttnThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
     return cudaGetLastError();
 }
 
@@ -1120,7 +1144,7 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     const int atoms = prob.d <= 64 ? 1 : 2;
     const bool trace = prob.decoded_bits != nullptr || prob.score_dots != nullptr;
 
-    CUtensorMap maps[5];
+    CUtensorMap maps[6];
     std::memset(maps, 0, sizeof(maps));
     bool tma = prob.d % 16 == 0 && aligned16(prob.q) && aligned16(prob.k) && aligned16(prob.v) &&
                (!p.routed || (aligned16(prob.q8) && aligned16(prob.k8)));
@@ -1133,6 +1157,9 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
                   encode_map(&maps[4], prob.k8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.heads, p.N, p.d, 128);
         }
     }
+    // fp32 O by TMA stores of 32 x 32 boxes (128-byte rows, swizzled)
+    p.o_tma = (!strided && prob.d % 32 == 0 && aligned16(prob.o) &&
+               encode_map(&maps[5], prob.o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.heads, p.M, p.d, 32, 32)) ? 1 : 0;
     const unsigned g = static_cast<unsigned>(grid);
     if (strided) {
         // strided outputs carry no trace outputs (checked by the API layer)
