@@ -205,6 +205,7 @@ struct Params {
     int o_vec;
     int o_tma;           // fp32 O written by TMA stores from shared memory
     int head_group;      // heads scheduled together (their K/V stay L2-resident)
+    int prefetch_ahead;  // CTA distance of the Q tile prefetched into L2 (the SM count)
     // strided output (kStrided variants)
     void* o_data;
     int o_dtype;         // 0 fp32, 1 fp16, 2 bf16
@@ -411,6 +412,18 @@ __device__ __forceinline__ void store_strided_row(const Params& p, long long row
     }
 }
 
+// Work item of CTA `bid`: heads are scheduled in groups (their K/V stay in
+// L2 while the group runs); inside a group the heaviest (last) query tiles go
+// first.
+__device__ __forceinline__ void tile_of(const Params& p, int bid, int& head, int& qt) {
+    const int per_group = p.head_group * p.q_tiles;
+    const int group0 = (bid / per_group) * p.head_group;
+    const int group_heads = min(p.head_group, p.heads - group0);
+    const int in_group = bid - (bid / per_group) * per_group;
+    qt = p.q_tiles - 1 - in_group / group_heads;
+    head = group0 + in_group % group_heads;
+}
+
 template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -433,15 +446,8 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31u;
 
-    // Work item: heads are scheduled in groups (their K/V stay in L2 while the
-    // group runs); inside a group the heaviest (last) query tiles go first.
-    const int bid = static_cast<int>(blockIdx.x);
-    const int per_group = p.head_group * p.q_tiles;
-    const int group0 = (bid / per_group) * p.head_group;
-    const int group_heads = min(p.head_group, p.heads - group0);
-    const int in_group = bid - (bid / per_group) * per_group;
-    const int qt = p.q_tiles - 1 - in_group / group_heads;
-    const int head = group0 + in_group % group_heads;
+    int head, qt;
+    tile_of(p, static_cast<int>(blockIdx.x), head, qt);
     const int nblk = p.causal ? min(p.kv_blocks, qt + 1) : p.kv_blocks;
     const int load_i8 = p.routed;
 
@@ -460,6 +466,22 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         *abort_flag = 0;
         mbar_init_fence();
         fence_proxy_async_smem();
+    }
+    // The producer's first global loads (routing words, K scales) and the L2
+    // prefetch of the Q tile of the CTA one SM-count ahead (likely the next
+    // to run on some SM) go out before the set-up barrier, so their latency
+    // overlaps the barrier and TMEM set-up.
+    RouteFetch route;
+    if (warp == kProducerWarp) {
+        route.init(p, head, qt, lane);
+        route.fetch(p, head, 0, nblk, lane);
+        const int ahead = static_cast<int>(blockIdx.x) + p.prefetch_ahead;
+        if (kUseTma && lane == 0 && p.prefetch_ahead > 0 && ahead < static_cast<int>(gridDim.x)) {
+            int head2, qt2;
+            tile_of(p, ahead, head2, qt2);
+            for (int a = 0; a < kAtoms; ++a) tma_prefetch_l2_3d(&tm_q, a * 64, qt2 * kTileRows, head2);
+            if (load_i8) tma_prefetch_l2_3d(&tm_q8, 0, qt2 * kTileRows, head2);
+        }
     }
     for (int i = threadIdx.x; i < 2 * kSoftmaxThreads; i += kAttnThreads) {
         reinterpret_cast<std::uint64_t*>(smem + L::kXchg)[i] = ~0ull;    // no tag matches
@@ -496,9 +518,6 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarQFull));
         }
-        RouteFetch route;
-        route.init(p, head, qt, lane);
-        route.fetch(p, head, 0, nblk, lane);
         RouteSlot* ring = reinterpret_cast<RouteSlot*>(smem + L::kRoute);
         int k_issued = 0, v_issued = 0;
         // K (and the routing summary) of block i go out one block ahead of V
@@ -1085,6 +1104,23 @@ cudaError_t launch_variant(const CUtensorMap* maps, const Params& p, unsigned gr
     return cudaGetLastError();
 }
 
+// SM count of the current device, queried once per device.
+cudaError_t sm_count(int* out) {
+    static int cached[64] = {0};
+    int device = 0;
+    cudaError_t status = cudaGetDevice(&device);
+    if (status != cudaSuccess) return status;
+    if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+    if (cached[device] == 0) {
+        int n = 0;
+        status = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+        if (status != cudaSuccess) return status;
+        cached[device] = n > 0 ? n : 1;
+    }
+    *out = cached[device];
+    return cudaSuccess;
+}
+
 bool aligned16(const void* ptr) {
     return (reinterpret_cast<std::uintptr_t>(ptr) & 15u) == 0;
 }
@@ -1138,6 +1174,8 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
                    aligned16(prob.o_data)) ? 1 : 0;
     }
     p.head_group = std::min(prob.heads, 8);
+    const cudaError_t sm_status = sm_count(&p.prefetch_ahead);
+    if (sm_status != cudaSuccess) return sm_status;
 
     const long long grid = static_cast<long long>(p.q_tiles) * p.heads;
     if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;

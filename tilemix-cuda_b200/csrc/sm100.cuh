@@ -118,6 +118,12 @@ __device__ __forceinline__ void bulk_wait_group_read0() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
+// L2 prefetch of one tiled box (no shared-memory destination, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int x, int y, int z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];"
+                 :: "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z) : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
