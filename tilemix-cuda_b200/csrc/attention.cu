@@ -663,7 +663,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             if (!wait_bar(bar(kBarKFull + ks), (j / kKStages) & 1, abort_flag, kStatusMma)) return false;
             const std::uint64_t plan = ring[j % kRouteSlots].plan;
             tc_fence_after();
-            if (lane == 0) {
+            if (elect_one()) {
                 const uint32_t s_tmem = tmem + col_s(j & 1);
                 const bool base_i8 = plan & 1ull;
                 mma_run(s_tmem, ks, base_i8, 0, static_cast<int>((plan >> 1) & 7u), none);
@@ -696,7 +696,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             for (int h = 0; h < 2; ++h) {
                 if (!wait_bar(bar(kBarPFull + 2 * (j & 1) + h), (j >> 1) & 1, abort_flag, kStatusMma)) return false;
                 tc_fence_after();
-                if (lane == 0) {
+                if (elect_one()) {
                     const uint32_t o_tmem = tmem + kColO + 128u * h;
                     const uint32_t a0 = p_tmem + 64u * h;
                     const uint32_t b0 = v_lo + 512u * h;
@@ -711,7 +711,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 }
                 __syncwarp();
             }
-            if (lane == 0) {
+            if (elect_one()) {
                 tc_commit(bar(kBarVEmpty + vs));
                 tc_commit(bar(kBarPvDone + (j & 1)));
             }

@@ -19,6 +19,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// One lane of the (converged) warp, chosen by elect.sync.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile("{\n\t.reg .pred P1;\n\telect.sync _|P1, 0xffffffff;\n\tselp.b32 %0, 1, 0, P1;\n\t}"
+                 : "+r"(pred));
+    return pred != 0;
+}
+
 __device__ __forceinline__ uint32_t lane_id() {
     uint32_t lane;
     asm volatile("mov.u32 %0, %%laneid;" : "=r"(lane));
