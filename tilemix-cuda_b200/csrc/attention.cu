@@ -504,7 +504,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         const std::size_t q_off = static_cast<std::size_t>(head) * p.M * p.d;
         const std::size_t kv_off = static_cast<std::size_t>(head) * p.N * p.d;
         if (kUseTma) {
-            if (lane == 0) {
+            if (elect_one()) {
                 mbar_arrive_expect_tx(bar(kBarQFull), L::kTileF16 + (load_i8 ? kAtomBytes : 0u));
                 for (int a = 0; a < kAtoms; ++a) {
                     tma_load_3d(sbase + L::kQ + a * kAtomBytes, &tm_q, bar(kBarQFull), a * 64, qt * kTileRows, head);
@@ -543,7 +543,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const int ks = j % kKStages;
                 if (!wait_bar(bar(kBarKEmpty + ks), ((j / kKStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
                 if (kUseTma) {
-                    if (lane == 0) {
+                    if (elect_one()) {
                         const uint32_t bytes = (need_f16 ? L::kTileF16 : 0u) + (need_i8 ? kAtomBytes : 0u);
                         mbar_arrive_expect_tx(bar(kBarKFull + ks), bytes);
                         if (need_f16) {
@@ -571,7 +571,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const int vs = j % kVStages;
                 if (!wait_bar(bar(kBarVEmpty + vs), ((j / kVStages) & 1) ^ 1, abort_flag, kStatusProducer)) break;
                 if (kUseTma) {
-                    if (lane == 0) {
+                    if (elect_one()) {
                         mbar_arrive_expect_tx(bar(kBarVFull + vs), L::kTileF16);
                         for (int a = 0; a < kAtoms; ++a) {
                             tma_load_3d(sbase + L::kV + vs * L::kTileF16 + a * kAtomBytes, &tm_v, bar(kBarVFull + vs),
