@@ -182,8 +182,34 @@ cudaError_t from_host_impl(const __half* hQ, const __half* hK, const __half* hV,
     int device = 0;
     TM_TRY(cudaGetDevice(&device));
 
-    const int chunk = chunk_heads > 0 ? std::min(chunk_heads, heads) : std::max(1, (heads + 15) / 16);
-    const int chunks = (heads - 1) / chunk + 1;
+    // Chunk sizes: `chunk_heads` each, or by default ~heads/16 each with the
+    // first and last two chunks at a quarter and a half of that, so the
+    // pipeline fills (first H2D, nothing to overlap yet) and drains (last
+    // kernels and D2H) quickly.
+    std::vector<int> sizes;
+    if (chunk_heads > 0) {
+        const int c = std::min(chunk_heads, heads);
+        for (int h0 = 0; h0 < heads; h0 += c) sizes.push_back(std::min(c, heads - h0));
+    } else {
+        const int c = std::max(1, (heads + 15) / 16);
+        const int ramp[2] = {std::max(1, c / 4), std::max(1, c / 2)};
+        int left = heads;
+        std::vector<int> tail;
+        for (int r = 0; r < 2 && left > 0; ++r) {            // ramp up
+            sizes.push_back(std::min(ramp[r], left));
+            left -= sizes.back();
+        }
+        for (int r = 0; r < 2 && left > 0; ++r) {            // ramp down (taken from the end)
+            tail.push_back(std::min(ramp[r], left));
+            left -= tail.back();
+        }
+        while (left > 0) {
+            sizes.push_back(std::min(c, left));
+            left -= sizes.back();
+        }
+        sizes.insert(sizes.end(), tail.rbegin(), tail.rend());
+    }
+    const int chunks = static_cast<int>(sizes.size());
     const std::size_t q_elems = static_cast<std::size_t>(M) * d;     // per head
     const std::size_t kv_elems = static_cast<std::size_t>(N) * d;
     const std::size_t words_per_head = routed ? tilemix_routing_word_count(M, N, g) : 0;
@@ -202,9 +228,9 @@ cudaError_t from_host_impl(const __half* hQ, const __half* hK, const __half* hV,
     TM_TRY(cudaEventRecord(start, stream));
     TM_TRY(cudaStreamWaitEvent(ctx.h2d, start, 0));
     TM_TRY(cudaStreamWaitEvent(ctx.d2h, start, 0));
-    for (int c = 0; c < chunks; ++c) {
-        const int h0 = c * chunk;
-        const int hn = std::min(chunk, heads - h0);
+    int h0 = 0;
+    for (int c = 0; c < chunks; h0 += sizes[c], ++c) {
+        const int hn = sizes[c];
         const std::size_t qo = h0 * q_elems, kvo = h0 * kv_elems;
         cudaEvent_t in = ctx.events[2 + 2 * c], out = ctx.events[3 + 2 * c];
         TM_TRY(cudaMemcpyAsync(dq + qo, hQ + qo, hn * q_elems * sizeof(__half), cudaMemcpyHostToDevice, ctx.h2d));
