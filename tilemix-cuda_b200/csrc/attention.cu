@@ -16,28 +16,34 @@
 // running max only moved when it grows by more than 2^15 (the final result is
 // unchanged mathematically; P stays <= 32768, inside fp16's range).
 //
-// CTA = one 128-row query tile of one head, 320 threads:
+// CTA = one 128-row query tile of one head, 352 threads:
 //   warps 0-7  softmax: warp w serves TMEM lanes 32*(w%4).. (query rows) and
 //              the 64-key half (w/4) of every 128-key block, so each SM
-//              sub-partition runs two softmax warps on the same block; the
-//              halves exchange row maxima through shared memory
-//   warp 8     MMA issuer (one lane) + TMEM owner: S_a | S_b | O (384 of 512
-//              columns); S is double-buffered so QK of block j+2 runs while
-//              the softmax works on block j+1
+//              sub-partition runs two softmax warps on the same block; each
+//              half keeps its own running max, row sum and O accumulator
+//   warps 8,10 MMA issuers, one per 64-key half h (warp 8 also owns TMEM:
+//              S_a | S_b | O_0 | O_1, all 512 columns); S is double-buffered
+//              so QK of block j+2 runs while the softmax works on block j+1
 //   warp 9     producer: TMA (or, for head dims TMA cannot address, plain
 //              loads) of Q/Q8 once, then per 128-key block K/K8 and V (two
 //              stages each), 128-byte swizzled; publishes each block's
-//              routing summary, MMA plan and K scales in a shared-memory ring
-// MMA order: QK(0), QK(1), then per block j: PV(j) as soon as P(j) is
-// published, then QK(j+2) into the S buffer PV(j) just read (the in-order
-// tensor pipe guarantees PV(j) reads P before QK(j+2) overwrites it). P
-// overwrites S in TMEM (per 32-key chunk: fp16 hi in the chunk's first 16
-// columns, lo in the last 16) and is the TMEM A operand of the PV MMAs.
+//              routing summary, per-half MMA plans and K scales in a
+//              shared-memory ring
+// MMA order, per key half h (one MMA warp each): QK(0), QK(1), then per block
+// j: PV(j) of half h as soon as softmax half h has published P(j), then
+// QK(j+2) of half h (N = 64) into the S columns that PV(j) just read (same
+// issuing thread: the in-order tensor pipe guarantees PV(j) reads P before
+// QK(j+2) overwrites it). The halves touch disjoint S and O columns, so their
+// P -> PV -> QK -> S chains run in parallel; the K and V stages both halves
+// read are released after both MMA warps' commits. P overwrites S in TMEM (per
+// 32-key chunk: fp16 hi in the chunk's first 16 columns, lo in the last 16)
+// and is the TMEM A operand of the PV MMAs. tcgen05.mma is issued under
+// elect.sync (a lane == 0 test made every issue several times slower).
 //
 // Routing inside the 128-row tile: for each 32-key tile the 8 routing bits of
-// the tile's 16-row query tiles select INT8 or FP16 per 16 rows. A uniform
-// block is one full-width MMA (N = 128) of its precision. A mixed block is one
-// full-width "base" MMA of one precision for all rows, then "overlay" MMAs of
+// the tile's 16-row query tiles select INT8 or FP16 per 16 rows. Per key half,
+// a uniform half-block is one MMA (N = 64) of its precision per K step; a mixed
+// one is a "base" MMA of one precision for all rows, then "overlay" MMAs of
 // the other precision over the key-tile runs that need it, with the TMEM lanes
 // of rows that keep the base result disabled (tcgen05.mma disable-output-lane);
 // the in-order tensor pipe makes the overlay overwrite the base exactly where
@@ -74,9 +80,10 @@ constexpr int kVStages = 2;
 constexpr int kRouteSlots = 8;               // the producer runs at most ~3 blocks ahead
 constexpr int kSoftmaxWarps = 8;
 constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
-constexpr int kMmaWarp = 8;
+constexpr int kMmaWarp = 8;           // MMA issuer of key half 0, TMEM owner
+constexpr int kMmaWarp1 = 10;         // MMA issuer of key half 1
 constexpr int kProducerWarp = 9;
-constexpr int kAttnThreads = 320;
+constexpr int kAttnThreads = 352;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;              // S_a at 0, S_b at 128, O_0 at 256, O_1 at 384
 constexpr uint32_t kAtomBytes = 128 * 128;   // 128 rows x 128 bytes
@@ -100,11 +107,12 @@ enum : unsigned int {
 // latency; only the producer touches the routing words and K scales):
 //   pats   bits [8 kt, 8 kt + 8): INT8 bit of the tile's 8 query tiles for key tile kt
 //   scales the block's two 64-key K scales (fp16, 0 when unrouted)
-//   plan   the block's QK MMA plan (see make_plan)
+//   plan   the block's QK MMA plan per 64-key half (see make_plan; key
+//          tiles counted from the half's first)
 struct RouteSlot {
     uint32_t pats;
     uint32_t scales;
-    std::uint64_t plan;
+    std::uint64_t plan[2];
 };
 
 template <int kAtoms>
@@ -118,15 +126,17 @@ struct SmemLayout {
     static constexpr uint32_t kRoute = kV + kVStages * kTileF16;       // [kRouteSlots]
     static constexpr uint32_t kXchg = kRoute + kRouteSlots * sizeof(RouteSlot);  // [2][256] u64 pair handshake words
     static constexpr uint32_t kBars = kXchg + 2 * kSoftmaxThreads * 8;
-    static constexpr uint32_t kNumBars = 18 + kRouteSlots;
+    static constexpr uint32_t kNumBars = 23 + kRouteSlots;
     static constexpr uint32_t kMisc = kBars + kNumBars * 8;            // tmem base, abort flag
     static constexpr uint32_t kEnd = kMisc + 16;
     static constexpr uint32_t kBytes = kEnd + 1024;                     // + alignment slack
 };
 
+// S-full, P-full and PV-done are per (S buffer b, key half h) at base + 2 b + h;
+// the drain barrier per MMA warp.
 enum Bar : int {
     kBarQFull = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7,
-    kBarSFull = 9, kBarPFull = 11, kBarPvDone = 15, kBarDrain = 17, kBarRoute = 18,
+    kBarSFull = 9, kBarPFull = 13, kBarPvDone = 17, kBarDrain = 21, kBarRoute = 23,
 };
 
 // QK plan of the tile for one key block, packed in 64 bits:
@@ -453,15 +463,16 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
 
     if (threadIdx.x == 0) {
         mbar_init(bar(kBarQFull), 1);
-        for (int s = 0; s < kKStages; ++s) { mbar_init(bar(kBarKFull + s), 1); mbar_init(bar(kBarKEmpty + s), 1); }
-        for (int s = 0; s < kVStages; ++s) { mbar_init(bar(kBarVFull + s), 1); mbar_init(bar(kBarVEmpty + s), 1); }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(bar(kBarSFull + b), 1);
-            mbar_init(bar(kBarPFull + 2 * b), kSoftmaxWarps / 2);       // one arrival per warp of the half
-            mbar_init(bar(kBarPFull + 2 * b + 1), kSoftmaxWarps / 2);
-            mbar_init(bar(kBarPvDone + b), 1);
+        // K and V stages are free once both MMA warps' reads have completed
+        for (int s = 0; s < kKStages; ++s) { mbar_init(bar(kBarKFull + s), 1); mbar_init(bar(kBarKEmpty + s), 2); }
+        for (int s = 0; s < kVStages; ++s) { mbar_init(bar(kBarVFull + s), 1); mbar_init(bar(kBarVEmpty + s), 2); }
+        for (int i = 0; i < 4; ++i) {
+            mbar_init(bar(kBarSFull + i), 1);
+            mbar_init(bar(kBarPFull + i), kSoftmaxWarps / 2);           // one arrival per warp of the half
+            mbar_init(bar(kBarPvDone + i), 1);
         }
         mbar_init(bar(kBarDrain), 1);
+        mbar_init(bar(kBarDrain + 1), 1);
         for (int r = 0; r < kRouteSlots; ++r) mbar_init(bar(kBarRoute + r), 1);
         *abort_flag = 0;
         mbar_init_fence();
@@ -535,7 +546,9 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     RouteSlot slot;
                     slot.pats = pats;
                     slot.scales = scales;
-                    slot.plan = make_plan(pats, valid & ~pats, min(4, p.k32_tiles - 4 * j));
+                    const int kt_here = min(4, p.k32_tiles - 4 * j);
+                    slot.plan[0] = make_plan(pats & 0xffffu, (valid & ~pats) & 0xffffu, min(2, kt_here));
+                    slot.plan[1] = make_plan(pats >> 16, (valid & ~pats) >> 16, min(2, kt_here - 2));
                     ring[j % kRouteSlots] = slot;
                     mbar_arrive(bar(kBarRoute + j % kRouteSlots));   // release: slot visible to its waiters
                 }
@@ -598,8 +611,13 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 wait_bar(bar(kBarVFull + j % kVStages), (j / kVStages) & 1, abort_flag, kStatusDrain);
             }
         }
-    } else if (warp == kMmaWarp) {
+    } else if (warp == kMmaWarp || warp == kMmaWarp1) {
         // ----------------------------------------------------------------- MMA
+        // Two MMA warps, one per 64-key half mh (on different sub-partitions):
+        // each issues its half's PV(j) and QK(j + 2) into S and O columns only
+        // that half uses, so the halves' P -> PV -> QK -> S chains run in
+        // parallel; the K and V stages both read are released by two commits.
+        const int mh = warp == kMmaWarp ? 0 : 1;
         const uint32_t pv_idesc = idesc_f16_f32(kTileRows, p.pv_n, true);
         const RouteSlot* ring = reinterpret_cast<const RouteSlot*>(smem + L::kRoute);
         // Descriptor words: every operand here is 128-byte swizzled with
@@ -655,79 +673,83 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 }
             }
         };
-        // QK^T of block j into S[j % 2], following the producer's plan.
-        auto issue_qk = [&](int j) -> bool {
-            // The producer publishes block j's routing slot before it arms
-            // K(j)'s barrier, so waiting for K(j) also makes the slot visible.
+        // QK^T of block j, key half mh (keys and S columns 64 mh ..), following
+        // the producer's plan for that half (the caller has waited for K(j),
+        // which also makes block j's routing slot visible).
+        auto issue_qk_half = [&](int j) {
             const int ks = j % kKStages;
-            if (!wait_bar(bar(kBarKFull + ks), (j / kKStages) & 1, abort_flag, kStatusMma)) return false;
-            const std::uint64_t plan = ring[j % kRouteSlots].plan;
-            tc_fence_after();
+            const std::uint64_t plan = ring[j % kRouteSlots].plan[mh];
             if (elect_one()) {
                 const uint32_t s_tmem = tmem + col_s(j & 1);
                 const bool base_i8 = plan & 1ull;
-                mma_run(s_tmem, ks, base_i8, 0, static_cast<int>((plan >> 1) & 7u), none);
+                const int nkt = static_cast<int>((plan >> 1) & 7u);
+                if (nkt > 0) mma_run(s_tmem, ks, base_i8, 2 * mh, nkt, none);
                 const int overlays = static_cast<int>((plan >> 4) & 7u);
                 #pragma unroll 1
                 for (int r = 0; r < overlays; ++r) {
                     const uint32_t ov = static_cast<uint32_t>(plan >> (8 + 13 * r)) & 0x1fffu;
                     uint32_t off[4];
                     lane_mask(~(ov >> 5) & 0xffu, off);
-                    mma_run(s_tmem, ks, !base_i8, static_cast<int>(ov & 3u), static_cast<int>((ov >> 2) & 7u), off);
+                    mma_run(s_tmem, ks, !base_i8, 2 * mh + static_cast<int>(ov & 3u),
+                            static_cast<int>((ov >> 2) & 7u), off);
                 }
+                tc_commit(bar(kBarSFull + 2 * (j & 1) + mh));
                 tc_commit(bar(kBarKEmpty + ks));
-                tc_commit(bar(kBarSFull + (j & 1)));
             }
             __syncwarp();
-            return true;
         };
-        // PV of block j, per 64-key half h: O_h (+)= (P_hi + P_lo) V_j[keys of h].
-        // Each half of the softmax publishes its own P, so half 0's MMAs can
-        // start while half 1 is still exponentiating.
-        auto issue_pv = [&](int j) -> bool {
+        // PV of block j, key half mh: O_mh (+)= (P_hi + P_lo) V_j[keys of mh].
+        // V tile is MN-major for this MMA: 64-wide d atoms LBO apart, 8-key
+        // groups 1024 B apart; each K step covers 16 keys (2048 B). P_hi and
+        // P_lo of a 16-key step share the V operand.
+        auto issue_pv_half = [&](int j) {
             const int vs = j % kVStages;
-            if (!wait_bar(bar(kBarVFull + vs), (j / kVStages) & 1, abort_flag, kStatusMma)) return false;
-            // V tile is MN-major for this MMA: 64-wide d atoms LBO apart,
-            // 8-key groups 1024 B apart; each K step covers 16 keys (2048 B).
-            // P_hi and P_lo of a 16-key step share the V operand.
-            const uint32_t v_lo = v_lo0 + static_cast<uint32_t>(vs) * (L::kTileF16 >> 4);
-            const uint32_t p_tmem = tmem + col_s(j & 1);
-            #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                if (!wait_bar(bar(kBarPFull + 2 * (j & 1) + h), (j >> 1) & 1, abort_flag, kStatusMma)) return false;
-                tc_fence_after();
-                if (elect_one()) {
-                    const uint32_t o_tmem = tmem + kColO + 128u * h;
-                    const uint32_t a0 = p_tmem + 64u * h;
-                    const uint32_t b0 = v_lo + 512u * h;
-                    mma_f16_ts_w(o_tmem, a0, b0, dhi, pv_idesc, j > 0 ? 1u : 0u);
-                    mma_f16_ts_w(o_tmem, a0 + 16, b0, dhi, pv_idesc, 1u);
-                    #pragma unroll
-                    for (int t = 1; t < 4; ++t) {
-                        const uint32_t a_hi = a0 + 32 * (t >> 1) + 8 * (t & 1);
-                        mma_f16_ts_w(o_tmem, a_hi, b0 + 128 * t, dhi, pv_idesc, 1u);
-                        mma_f16_ts_w(o_tmem, a_hi + 16, b0 + 128 * t, dhi, pv_idesc, 1u);
-                    }
-                }
-                __syncwarp();
-            }
             if (elect_one()) {
+                const uint32_t v_lo = v_lo0 + static_cast<uint32_t>(vs) * (L::kTileF16 >> 4);
+                const uint32_t o_tmem = tmem + kColO + 128u * mh;
+                const uint32_t a0 = tmem + col_s(j & 1) + 64u * mh;
+                const uint32_t b0 = v_lo + 512u * mh;
+                mma_f16_ts_w(o_tmem, a0, b0, dhi, pv_idesc, j > 0 ? 1u : 0u);
+                mma_f16_ts_w(o_tmem, a0 + 16, b0, dhi, pv_idesc, 1u);
+                #pragma unroll
+                for (int t = 1; t < 4; ++t) {
+                    const uint32_t a_hi = a0 + 32 * (t >> 1) + 8 * (t & 1);
+                    mma_f16_ts_w(o_tmem, a_hi, b0 + 128 * t, dhi, pv_idesc, 1u);
+                    mma_f16_ts_w(o_tmem, a_hi + 16, b0 + 128 * t, dhi, pv_idesc, 1u);
+                }
+                tc_commit(bar(kBarPvDone + 2 * (j & 1) + mh));
                 tc_commit(bar(kBarVEmpty + vs));
-                tc_commit(bar(kBarPvDone + (j & 1)));
             }
             __syncwarp();
-            return true;
         };
-        // QK(0), QK(1), then PV(j), QK(j + 2) for each block j (one call site
-        // per lambda keeps this warp's code small).
+        // QK(0), QK(1), then per block j: PV(j) of this half as soon as the
+        // softmax half has published P(j), then QK(j + 2) of this half into
+        // the S columns that PV just read (same thread: the in-order tensor
+        // pipe makes PV(j) read P before QK(j + 2) overwrites it).
         for (int j = -2; ok && j < nblk; ++j) {
-            if (j >= 0 && !issue_pv(j)) { ok = false; break; }
-            if (j + 2 < nblk && !issue_qk(j + 2)) { ok = false; break; }
+            if (j >= 0) {
+                if (!wait_bar(bar(kBarVFull + j % kVStages), (j / kVStages) & 1, abort_flag, kStatusMma) ||
+                    !wait_bar(bar(kBarPFull + 2 * (j & 1) + mh), (j >> 1) & 1, abort_flag, kStatusMma)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                issue_pv_half(j);
+            }
+            const int q = j + 2;
+            if (q < nblk) {
+                if (!wait_bar(bar(kBarKFull + q % kKStages), (q / kKStages) & 1, abort_flag, kStatusMma)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                issue_qk_half(q);
+            }
         }
         // Drain every MMA this thread issued before TMEM can be released.
-        if (lane == 0) tc_commit(bar(kBarDrain));
+        if (lane == 0) tc_commit(bar(kBarDrain + mh));
         __syncwarp();
-        wait_bar(bar(kBarDrain), 0, abort_flag, kStatusDrain);
+        wait_bar(bar(kBarDrain + mh), 0, abort_flag, kStatusDrain);
     } else if (warp < kSoftmaxWarps) {
         // ------------------------------------------------------------- softmax
         // Thread = (query row, 64-key half h). Per block it reads its half's
@@ -790,7 +812,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             // fast: no key of the block is masked for any row of the warp and
             // score_scale > 0, so FP16 raw units are the accumulator values.
             const bool fast = __all_sync(0xffffffffu, pos_scale && key0 + kTileKeys <= limit);
-            if (!s_ready && !wait_bar(bar(kBarSFull + b), (j >> 1) & 1, abort_flag, kStatusSoftmax)) {
+            if (!s_ready && !wait_bar(bar(kBarSFull + 2 * b + half), (j >> 1) & 1, abort_flag, kStatusSoftmax)) {
                 ok = false;
                 break;
             }
@@ -927,7 +949,8 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             }
             l_run += (sum0 + sum1) + (sum2 + sum3);
             if (j > 0 && __any_sync(0xffffffffu, rescale != 1.0f)) {
-                if (!wait_bar(bar(kBarPvDone + ((j - 1) & 1)), ((j - 1) >> 1) & 1, abort_flag, kStatusSoftmax)) {
+                if (!wait_bar(bar(kBarPvDone + 2 * ((j - 1) & 1) + half), ((j - 1) >> 1) & 1, abort_flag,
+                              kStatusSoftmax)) {
                     ok = false;
                     break;
                 }
@@ -947,7 +970,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     tmem_st32(o_addr + c + 32, xb);
                 }
             }
-            s_ready = j + 1 < nblk && mbar_test_wait(bar(kBarSFull + (b ^ 1)), ((j + 1) >> 1) & 1);
+            s_ready = j + 1 < nblk && mbar_test_wait(bar(kBarSFull + 2 * (b ^ 1) + half), ((j + 1) >> 1) & 1);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -968,7 +991,10 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             float m_oth = 0.0f, l_oth = 0.0f;
             ok = pair_exchange(xchg + kSoftmaxThreads, me, 1u, m_run, m_oth, abort_flag) &&
                  pair_exchange(xchg, me, 2u, l_run, l_oth, abort_flag);
-            if (ok && wait_bar(bar(kBarPvDone + ((nblk - 1) & 1)), ((nblk - 1) >> 1) & 1, abort_flag, kStatusSoftmax)) {
+            // the combine reads both halves' accumulators
+            const int bl = (nblk - 1) & 1;
+            if (ok && wait_bar(bar(kBarPvDone + 2 * bl), ((nblk - 1) >> 1) & 1, abort_flag, kStatusSoftmax) &&
+                wait_bar(bar(kBarPvDone + 2 * bl + 1), ((nblk - 1) >> 1) & 1, abort_flag, kStatusSoftmax)) {
                 tc_fence_after();
                 const float m = fmaxf(m_run, m_oth);
                 const float a_me = m_run == -INFINITY ? 0.0f : ex2((m_run - m) * c_exp);
