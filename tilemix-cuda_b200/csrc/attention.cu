@@ -754,9 +754,10 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         // ------------------------------------------------------------- softmax
         // Thread = (query row, 64-key half h). Per block it reads its half's
         // two 32-key chunks from TMEM once, turns INT8 chunks into exact
-        // floats, takes the half's max and swaps it with the other half of
-        // the row (pair handshake), then exponentiates the two chunks from
-        // the same registers and writes P (hi, lo) over them. Precision is
+        // floats, takes the half's max (each half keeps its own running max,
+        // sum and O; the two halves of a row meet only in the epilogue), then
+        // exponentiates the two chunks from the same registers and writes
+        // P (hi, lo) over them. Precision is
         // chosen per 16-row query tile, so a warp (32 rows) can mix INT8 and
         // FP16 chunks: per-lane differences are selects, branches are on
         // warp votes.
@@ -874,8 +875,14 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 if (__any_sync(0xffffffffu, is_i8)) {
                     const uint32_t addi = is_i8 ? 0x4B400000u : 0u;
                     const float subf = is_i8 ? 12582912.0f : 0.0f;
+                    const float2 nsub = make_float2(-subf, -subf);
                     #pragma unroll
-                    for (int i = 0; i < 32; ++i) x[i] = __float_as_uint(__uint_as_float(x[i] + addi) - subf);
+                    for (int i = 0; i < 32; i += 2) {
+                        const float2 t = __fadd2_rn(make_float2(__uint_as_float(x[i] + addi),
+                                                                __uint_as_float(x[i + 1] + addi)), nsub);
+                        x[i] = __float_as_uint(t.x);
+                        x[i + 1] = __float_as_uint(t.y);
+                    }
                 }
             }
             const float mul0 = ((types & 1u) ? ratio : 1.0f) * c_exp;   // score_log2 = x * mul
@@ -919,35 +926,44 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             // parity tolerance needs once V has large-magnitude (outlier)
             // channels. Chunk c's P_hi goes to its columns [32c, 32c+16), P_lo
             // to [32c+16, 32c+32).
-            float sum0 = 0.0f, sum1 = 0.0f, sum2 = 0.0f, sum3 = 0.0f;
+            // Element pairs go through the packed f32x2 FMA/add (one instruction
+            // per pair, rounding exactly like the scalar forms).
+            float2 s01 = make_float2(0.0f, 0.0f), s23 = make_float2(0.0f, 0.0f);
+            const float2 nm2 = make_float2(neg_m, neg_m);
+            const float2 minus1 = make_float2(-1.0f, -1.0f);
             #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 const uint32_t (&x)[32] = c ? xb : xa;
                 const float mul = c ? mul1 : mul0;
-                float arg[32];
+                const float2 mul2 = make_float2(mul, mul);
+                float2 arg[16];
                 #pragma unroll
-                for (int i = 0; i < 32; ++i) arg[i] = fmaf(__uint_as_float(x[i]), mul, neg_m);
+                for (int i = 0; i < 16; ++i) {
+                    arg[i] = __ffma2_rn(make_float2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])),
+                                        mul2, nm2);
+                }
                 uint32_t hi[16], lo[16];
                 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
-                    const float p0 = ex2(arg[2 * i]);
-                    const float p1 = ex2(arg[2 * i + 1]);
-                    const float p2 = ex2(arg[2 * i + 2]);
-                    const float p3 = ex2(arg[2 * i + 3]);
-                    sum0 += p0; sum1 += p1; sum2 += p2; sum3 += p3;
-                    const float h0 = __uint_as_float(__float_as_uint(p0) & 0xFFFFE000u);
-                    const float h1 = __uint_as_float(__float_as_uint(p1) & 0xFFFFE000u);
-                    const float h2 = __uint_as_float(__float_as_uint(p2) & 0xFFFFE000u);
-                    const float h3 = __uint_as_float(__float_as_uint(p3) & 0xFFFFE000u);
-                    hi[i] = pack_half2(h0, h1);
-                    hi[i + 1] = pack_half2(h2, h3);
-                    lo[i] = pack_half2(p0 - h0, p1 - h1);
-                    lo[i + 1] = pack_half2(p2 - h2, p3 - h3);
+                    const float2 p01 = make_float2(ex2(arg[i].x), ex2(arg[i].y));
+                    const float2 p23 = make_float2(ex2(arg[i + 1].x), ex2(arg[i + 1].y));
+                    s01 = __fadd2_rn(s01, p01);
+                    s23 = __fadd2_rn(s23, p23);
+                    const float2 h01 = make_float2(__uint_as_float(__float_as_uint(p01.x) & 0xFFFFE000u),
+                                                   __uint_as_float(__float_as_uint(p01.y) & 0xFFFFE000u));
+                    const float2 h23 = make_float2(__uint_as_float(__float_as_uint(p23.x) & 0xFFFFE000u),
+                                                   __uint_as_float(__float_as_uint(p23.y) & 0xFFFFE000u));
+                    hi[i] = pack_half2(h01.x, h01.y);
+                    hi[i + 1] = pack_half2(h23.x, h23.y);
+                    const float2 l01 = __ffma2_rn(h01, minus1, p01);      // p - P_hi, exact
+                    const float2 l23 = __ffma2_rn(h23, minus1, p23);
+                    lo[i] = pack_half2(l01.x, l01.y);
+                    lo[i + 1] = pack_half2(l23.x, l23.y);
                 }
                 tmem_st16(s_own + 32 * c, hi);
                 tmem_st16(s_own + 32 * c + 16, lo);
             }
-            l_run += (sum0 + sum1) + (sum2 + sum3);
+            l_run += (s01.x + s01.y) + (s23.x + s23.y);
             if (j > 0 && __any_sync(0xffffffffu, rescale != 1.0f)) {
                 if (!wait_bar(bar(kBarPvDone + 2 * ((j - 1) & 1) + half), ((j - 1) >> 1) & 1, abort_flag,
                               kStatusSoftmax)) {
@@ -961,10 +977,15 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     tmem_ld32(o_addr + c, xa);
                     tmem_ld32(o_addr + c + 32, xb);
                     tc_wait_ld();
+                    const float2 r2 = make_float2(rescale, rescale);
                     #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        xa[i] = __float_as_uint(__uint_as_float(xa[i]) * rescale);
-                        xb[i] = __float_as_uint(__uint_as_float(xb[i]) * rescale);
+                    for (int i = 0; i < 32; i += 2) {
+                        const float2 ta = __fmul2_rn(make_float2(__uint_as_float(xa[i]), __uint_as_float(xa[i + 1])), r2);
+                        const float2 tb = __fmul2_rn(make_float2(__uint_as_float(xb[i]), __uint_as_float(xb[i + 1])), r2);
+                        xa[i] = __float_as_uint(ta.x);
+                        xa[i + 1] = __float_as_uint(ta.y);
+                        xb[i] = __float_as_uint(tb.x);
+                        xb[i + 1] = __float_as_uint(tb.y);
                     }
                     tmem_st32(o_addr + c, xa);
                     tmem_st32(o_addr + c + 32, xb);
@@ -1016,10 +1037,15 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     tc_wait_ld();
                     // explicit roundings, so every output variant stores (a
                     // rounding of) the same fp32 value
+                    const float2 w_me2 = make_float2(w_me, w_me), w_oth2 = make_float2(w_oth, w_oth);
                     #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        xa[i] = __float_as_uint(__fmaf_rn(__uint_as_float(xa[i]), w_me,
-                                                          __fmul_rn(__uint_as_float(xb[i]), w_oth)));
+                    for (int i = 0; i < 32; i += 2) {
+                        const float2 t = __fmul2_rn(make_float2(__uint_as_float(xb[i]), __uint_as_float(xb[i + 1])),
+                                                    w_oth2);
+                        const float2 o = __ffma2_rn(make_float2(__uint_as_float(xa[i]), __uint_as_float(xa[i + 1])),
+                                                    w_me2, t);
+                        xa[i] = __float_as_uint(o.x);
+                        xa[i + 1] = __float_as_uint(o.y);
                     }
                     if (kStrided) {
                         if (row_valid) store_strided_row(p, row_off, c, xa);
