@@ -123,13 +123,17 @@ struct SmemLayout {
     static constexpr uint32_t kK = kQ8 + kAtomBytes;                    // [2 stages] fp16
     static constexpr uint32_t kK8 = kK + kKStages * kTileF16;          // [2 stages] int8
     static constexpr uint32_t kV = kK8 + kKStages * kAtomBytes;        // [2 stages]
-    static constexpr uint32_t kRoute = kV + kVStages * kTileF16;       // [kRouteSlots]
+    static constexpr uint32_t kBiasA = kV + kVStages * kTileF16;       // 8 x 128 B of fp16 2048
+    static constexpr uint32_t kBiasB = kBiasA + 1024;                   // 8 x 128 B of fp16 384
+    static constexpr uint32_t kRoute = kBiasB + 1024;                   // [kRouteSlots]
     static constexpr uint32_t kXchg = kRoute + kRouteSlots * sizeof(RouteSlot);  // [2][256] u64 pair handshake words
     static constexpr uint32_t kBars = kXchg + 2 * kSoftmaxThreads * 8;
     static constexpr uint32_t kNumBars = 23 + kRouteSlots;
     static constexpr uint32_t kMisc = kBars + kNumBars * 8;            // tmem base, abort flag
     static constexpr uint32_t kEnd = kMisc + 16;
     static constexpr uint32_t kBytes = kEnd + 1024;                     // + alignment slack
+    static_assert(kBytes <= 232448, "exceeds the 227 KB of shared memory a CTA can opt into");
+    static_assert(kBiasA % 1024 == 0, "128-byte-swizzled operands start on 1024-byte boundaries");
 };
 
 // S-full, P-full and PV-done are per (S buffer b, key half h) at base + 2 b + h;
@@ -497,6 +501,12 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     for (int i = threadIdx.x; i < 2 * kSoftmaxThreads; i += kAttnThreads) {
         reinterpret_cast<std::uint64_t*>(smem + L::kXchg)[i] = ~0ull;    // no tag matches
     }
+    // Constant operands of the INT8 bias MMA: 16 products 2048 * 384 sum to
+    // 1.5 * 2^23, exactly, whose fp32 bits are 0x4B400000.
+    for (int i = threadIdx.x; i < 512; i += kAttnThreads) {
+        reinterpret_cast<uint32_t*>(smem + L::kBiasA)[i] = i < 256 ? 0x68006800u : 0x5E005E00u;
+    }
+    fence_proxy_async_smem();
     if (warp == kMmaWarp) {
         tmem_alloc(sbase + L::kMisc, kTmemCols);
         tmem_relinquish();
@@ -629,6 +639,11 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         const uint32_t kf_lo0 = smem_desc_sw128_lo(sbase + L::kK, 16);
         const uint32_t ki_lo0 = smem_desc_sw128_lo(sbase + L::kK8, 16);
         const uint32_t v_lo0 = smem_desc_sw128_lo(sbase + L::kV, kAtomBytes);
+        // The bias operands are one 8-row swizzle group each, read for every
+        // row group (group stride 0): every element is the same constant.
+        const uint32_t bias_a_lo = smem_desc_sw128_lo(sbase + L::kBiasA, 16);
+        const uint32_t bias_b_lo = smem_desc_sw128_lo(sbase + L::kBiasB, 16);
+        const uint32_t bias_hi = smem_desc_sw128_hi(0);
         const bool f16_full = p.f16_ksteps == 4 * kAtoms;
         const bool i8_full = p.i8_ksteps == 4;
         const uint32_t none[4] = {0u, 0u, 0u, 0u};
@@ -642,16 +657,20 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             const uint32_t d = d_tmem + 32 * kt0;
             const uint32_t kofs = static_cast<uint32_t>(kt0) * 256u;
             if (int8) {
+                // The s32 accumulators start at 0x4B400000 (the bits of the
+                // float 1.5 * 2^23, written by one f16 MMA of the constant
+                // tiles), so they leave the tensor core as the float bits of
+                // 1.5 * 2^23 + dot (|dot| < 2^22): the softmax gets the exact
+                // float dot with one subtraction.
+                mma_f16_ss_w<0>(d, bias_a_lo, bias_b_lo, bias_hi, idesc_f16_f32(kTileRows, 32 * nkt, false), off);
                 const uint32_t k_lo = ki_lo0 + static_cast<uint32_t>(stage) * (kAtomBytes >> 4) + kofs;
                 const uint32_t idesc = idesc_s8_s32(kTileRows, 32 * nkt);
                 if (i8_full) {
-                    mma_i8_ss_w<0>(d, qi_lo, k_lo, dhi, idesc, off);
                     #pragma unroll
-                    for (int ks = 1; ks < 4; ++ks) mma_i8_ss_w<1>(d, qi_lo + 2 * ks, k_lo + 2 * ks, dhi, idesc, off);
+                    for (int ks = 0; ks < 4; ++ks) mma_i8_ss_w<1>(d, qi_lo + 2 * ks, k_lo + 2 * ks, dhi, idesc, off);
                 } else {
-                    mma_i8_ss_w<0>(d, qi_lo, k_lo, dhi, idesc, off);
                     #pragma unroll 1
-                    for (int ks = 1; ks < p.i8_ksteps; ++ks) mma_i8_ss_w<1>(d, qi_lo + 2 * ks, k_lo + 2 * ks, dhi, idesc, off);
+                    for (int ks = 0; ks < p.i8_ksteps; ++ks) mma_i8_ss_w<1>(d, qi_lo + 2 * ks, k_lo + 2 * ks, dhi, idesc, off);
                 }
             } else {
                 const uint32_t k_lo = kf_lo0 + static_cast<uint32_t>(stage) * (L::kTileF16 >> 4) + kofs;
@@ -833,7 +852,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                         for (int i = 0; i < 32; ++i) {
                             if (k0 + i < p.N) {
                                 p.score_dots[(static_cast<std::size_t>(head) * p.M + q_row) * p.N + k0 + i] =
-                                    static_cast<int32_t>(x[i]);
+                                    static_cast<int32_t>(x[i] - 0x4B400000u);   // accumulators carry the bias
                             }
                         }
                     }
@@ -852,34 +871,32 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 for (int c = 0; c < 2; ++c) {
                     uint32_t (&x)[32] = c ? xb : xa;
                     const bool is_i8 = (types >> c) & 1u;
-                    const uint32_t addi = is_i8 ? 0x4B400000u : 0u;
                     const float subf = is_i8 ? 12582912.0f : 0.0f;
                     const float mul = is_i8 ? ratio : a_f16;
                     const int k0 = key0 + 64 * half + 32 * c;
                     #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        const float r = (__uint_as_float(x[i] + addi) - subf) * mul;
+                        const float r = (__uint_as_float(x[i]) - subf) * mul;
                         x[i] = __float_as_uint(k0 + i >= limit ? -INFINITY : r);
                     }
                 }
                 types = 0;
             }
-            // INT8 chunks become exact floats in place (s32 -> f32 through
-            // the 1.5 * 2^23 bias, |dot| <= 127^2 * 128 < 2^22), so the max
-            // and the exponent below are one code path for both precisions;
-            // FP16 lanes of a mixed warp pass through unchanged.
+            // INT8 chunks become exact floats in place: their accumulators
+            // hold the float bits of 1.5 * 2^23 + dot (|dot| <= 127^2 * 128 <
+            // 2^22), so one subtraction leaves the dot; the max and the
+            // exponent below are then one code path for both precisions. FP16
+            // lanes of a mixed warp pass through unchanged.
             #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t (&x)[32] = c ? xb : xa;
                 const bool is_i8 = (types >> c) & 1u;
                 if (__any_sync(0xffffffffu, is_i8)) {
-                    const uint32_t addi = is_i8 ? 0x4B400000u : 0u;
                     const float subf = is_i8 ? 12582912.0f : 0.0f;
                     const float2 nsub = make_float2(-subf, -subf);
                     #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
-                        const float2 t = __fadd2_rn(make_float2(__uint_as_float(x[i] + addi),
-                                                                __uint_as_float(x[i + 1] + addi)), nsub);
+                        const float2 t = __fadd2_rn(make_float2(__uint_as_float(x[i]), __uint_as_float(x[i + 1])), nsub);
                         x[i] = __float_as_uint(t.x);
                         x[i + 1] = __float_as_uint(t.y);
                     }
