@@ -16,11 +16,15 @@
 // running max only moved when it grows by more than 2^15 (the final result is
 // unchanged mathematically; P stays <= 32768, inside fp16's range).
 //
-// CTA = one 128-row query tile of one head, 352 threads:
+// CTA = one 128-row query tile of one head, 512 threads:
 //   warps 0-7  softmax: warp w serves TMEM lanes 32*(w%4).. (query rows) and
 //              the 64-key half (w/4) of every 128-key block, so each SM
 //              sub-partition runs two softmax warps on the same block; each
 //              half keeps its own running max, row sum and O accumulator
+//   warps 12-15 O rescale: warp w rescales O_0 and O_1 of TMEM lanes
+//              32*(w%4).. when a softmax warp of those rows has moved its
+//              running max, off the softmax warps' path (they publish the
+//              per-row factor and go on to the exponent)
 //   warps 8,10 MMA issuers, one per 64-key half h (warp 8 also owns TMEM:
 //              S_a | S_b | O_0 | O_1, all 512 columns); S is double-buffered
 //              so QK of block j+2 runs while the softmax works on block j+1
@@ -83,7 +87,15 @@ constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
 constexpr int kMmaWarp = 8;           // MMA issuer of key half 0, TMEM owner
 constexpr int kMmaWarp1 = 10;         // MMA issuer of key half 1
 constexpr int kProducerWarp = 9;
-constexpr int kAttnThreads = 352;
+constexpr int kCorrWarp0 = 12;        // warps 12-15: O rescale of TMEM lane quarter (warp % 4)
+constexpr int kAttnThreads = 512;
+// Registers per thread after the role split (setmaxnreg; per warpgroup:
+// softmax warps 0-7, control warps 8-11, rescale warps 12-15). The three
+// shares add up to the 65536 registers of the SM exactly.
+constexpr int kSoftmaxRegs = 160;
+constexpr int kCtrlRegs = 80;
+constexpr int kCorrRegs = 112;
+static_assert(2 * 128 * kSoftmaxRegs + 128 * kCtrlRegs + 128 * kCorrRegs <= 65536, "register split");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;              // S_a at 0, S_b at 128, O_0 at 256, O_1 at 384
 constexpr uint32_t kAtomBytes = 128 * 128;   // 128 rows x 128 bytes
@@ -125,10 +137,11 @@ struct SmemLayout {
     static constexpr uint32_t kV = kK8 + kKStages * kAtomBytes;        // [2 stages]
     static constexpr uint32_t kBiasA = kV + kVStages * kTileF16;       // 8 x 128 B of fp16 2048
     static constexpr uint32_t kBiasB = kBiasA + 1024;                   // 8 x 128 B of fp16 384
-    static constexpr uint32_t kRoute = kBiasB + 1024;                   // [kRouteSlots]
+    static constexpr uint32_t kAlpha = kBiasB + 1024;                   // [S buffer][half][row] O rescale factors
+    static constexpr uint32_t kRoute = kAlpha + 2 * 2 * kTileRows * 4;  // [kRouteSlots]
     static constexpr uint32_t kXchg = kRoute + kRouteSlots * sizeof(RouteSlot);  // [2][256] u64 pair handshake words
     static constexpr uint32_t kBars = kXchg + 2 * kSoftmaxThreads * 8;
-    static constexpr uint32_t kNumBars = 23 + kRouteSlots;
+    static constexpr uint32_t kNumBars = 23 + kRouteSlots + 16;
     static constexpr uint32_t kMisc = kBars + kNumBars * 8;            // tmem base, abort flag
     static constexpr uint32_t kEnd = kMisc + 16;
     static constexpr uint32_t kBytes = kEnd + 1024;                     // + alignment slack
@@ -137,10 +150,12 @@ struct SmemLayout {
 };
 
 // S-full, P-full and PV-done are per (S buffer b, key half h) at base + 2 b + h;
-// the drain barrier per MMA warp.
+// the drain barrier per MMA warp; alpha-ready per (b, h, lane quarter q) at
+// base + 4 (2 b + h) + q.
 enum Bar : int {
     kBarQFull = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7,
     kBarSFull = 9, kBarPFull = 13, kBarPvDone = 17, kBarDrain = 21, kBarRoute = 23,
+    kBarAlpha = 23 + kRouteSlots,
 };
 
 // QK plan of the tile for one key block, packed in 64 bits:
@@ -472,12 +487,14 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int s = 0; s < kVStages; ++s) { mbar_init(bar(kBarVFull + s), 1); mbar_init(bar(kBarVEmpty + s), 2); }
         for (int i = 0; i < 4; ++i) {
             mbar_init(bar(kBarSFull + i), 1);
-            mbar_init(bar(kBarPFull + i), kSoftmaxWarps / 2);           // one arrival per warp of the half
+            // one arrival per softmax warp of the half and per rescale warp
+            mbar_init(bar(kBarPFull + i), kSoftmaxWarps / 2 + 4);
             mbar_init(bar(kBarPvDone + i), 1);
         }
         mbar_init(bar(kBarDrain), 1);
         mbar_init(bar(kBarDrain + 1), 1);
         for (int r = 0; r < kRouteSlots; ++r) mbar_init(bar(kBarRoute + r), 1);
+        for (int i = 0; i < 16; ++i) mbar_init(bar(kBarAlpha + i), 1);
         *abort_flag = 0;
         mbar_init_fence();
         fence_proxy_async_smem();
@@ -515,7 +532,12 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
+    // Registers follow the roles, one setmaxnreg per warpgroup at the top of
+    // its branch: the softmax warpgroups take what the control and rescale
+    // warpgroups give up.
+    if (warp >= kSoftmaxWarps && warp < kCorrWarp0) {
+    // control warpgroup: producer, the two MMA warps and one spare warp
+    reg_dealloc<kCtrlRegs>();
     if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer
         if (kUseTma && lane == 0) {
@@ -769,7 +791,9 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         if (lane == 0) tc_commit(bar(kBarDrain + mh));
         __syncwarp();
         wait_bar(bar(kBarDrain + mh), 0, abort_flag, kStatusDrain);
+    }
     } else if (warp < kSoftmaxWarps) {
+        reg_alloc<kSoftmaxRegs>();
         // ------------------------------------------------------------- softmax
         // Thread = (query row, 64-key half h). Per block it reads its half's
         // two 32-key chunks from TMEM once, turns INT8 chunks into exact
@@ -801,6 +825,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         float l_run = 0.0f;         // this half's share of the row sum
         bool ok = true;
         const uint32_t o_addr = tmem + lane_base + kColO + 128u * half;     // O_h
+        float* alpha_slots = reinterpret_cast<float*>(smem + L::kAlpha);
         volatile std::uint64_t* xchg = reinterpret_cast<volatile std::uint64_t*>(smem + L::kXchg);
         const int me = static_cast<int>(threadIdx.x);
         uint32_t xa[32], xb[32];
@@ -911,9 +936,9 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 if (r_ready) decode(j + 1);
             }
             // ---- this half's max; the running max moves only when the block
-            // exceeds it by more than 2^15 in p. O_h is then rescaled, after
-            // P is written: by then the previous block's PV, which must land
-            // first, has mostly finished.
+            // exceeds it by more than 2^15 in p. The factor for O_h goes to
+            // the rescale warp of these rows, which applies it once the
+            // previous block's PV has landed, while this warp exponentiates.
             float rescale = 1.0f;
             {
                 float m0 = max3f(__uint_as_float(xa[0]), __uint_as_float(xa[1]), __uint_as_float(xa[2]));
@@ -935,6 +960,9 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 l_run *= alpha;
                 rescale = alpha;
             }
+            alpha_slots[(2 * b + half) * kTileRows + row] = rescale;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarAlpha + 4 * (2 * b + half) + (warp & 3)));   // release
             const float neg_m = m_run == -INFINITY ? 0.0f : -m_run * c_exp;
             // ---- P = 2^(score_log2 - m) as P_hi + P_lo, both fp16. P_hi keeps
             // the top 11 significant bits of p (exact in fp16), P_lo = p - P_hi
@@ -981,33 +1009,6 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 tmem_st16(s_own + 32 * c + 16, lo);
             }
             l_run += (s01.x + s01.y) + (s23.x + s23.y);
-            if (j > 0 && __any_sync(0xffffffffu, rescale != 1.0f)) {
-                if (!wait_bar(bar(kBarPvDone + 2 * ((j - 1) & 1) + half), ((j - 1) >> 1) & 1, abort_flag,
-                              kStatusSoftmax)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                // 64 columns per round trip (xa, xb are free again here)
-                #pragma unroll 1
-                for (int c = 0; c < p.pv_n; c += 64) {
-                    tmem_ld32(o_addr + c, xa);
-                    tmem_ld32(o_addr + c + 32, xb);
-                    tc_wait_ld();
-                    const float2 r2 = make_float2(rescale, rescale);
-                    #pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        const float2 ta = __fmul2_rn(make_float2(__uint_as_float(xa[i]), __uint_as_float(xa[i + 1])), r2);
-                        const float2 tb = __fmul2_rn(make_float2(__uint_as_float(xb[i]), __uint_as_float(xb[i + 1])), r2);
-                        xa[i] = __float_as_uint(ta.x);
-                        xa[i + 1] = __float_as_uint(ta.y);
-                        xb[i] = __float_as_uint(tb.x);
-                        xb[i + 1] = __float_as_uint(tb.y);
-                    }
-                    tmem_st32(o_addr + c, xa);
-                    tmem_st32(o_addr + c + 32, xb);
-                }
-            }
             s_ready = j + 1 < nblk && mbar_test_wait(bar(kBarSFull + 2 * (b ^ 1) + half), ((j + 1) >> 1) & 1);
             tc_wait_st();
             tc_fence_before();
@@ -1106,6 +1107,62 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     bulk_commit_group();
                     bulk_wait_group_read0();
                 }
+            }
+        }
+    } else {
+        reg_dealloc<kCorrRegs>();
+        // ------------------------------------------------------------ rescale
+        // Warp w owns TMEM lanes 32*(w%4).. (the rows of softmax warps w%4 and
+        // w%4 + 4). Per block and key half: wait for the rows' factors; if any
+        // is not 1, wait for the previous block's PV of that half to land,
+        // then scale O_h in place. Its arrival on P-full (with the softmax
+        // warps') lets the half's PV(j) go ahead.
+        const int quarter = warp & 3;
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        const float* alpha_slots = reinterpret_cast<const float*>(smem + L::kAlpha);
+        uint32_t xa[32], xb[32];
+        bool ok = true;
+        for (int j = 0; ok && j < nblk; ++j) {
+            const int b = j & 1;
+            #pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+                if (!wait_bar(bar(kBarAlpha + 4 * (2 * b + h) + quarter), (j >> 1) & 1, abort_flag, kStatusSoftmax)) {
+                    ok = false;
+                    break;
+                }
+                const float alpha = alpha_slots[(2 * b + h) * kTileRows + quarter * 32 + static_cast<int>(lane)];
+                if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+                    if (!wait_bar(bar(kBarPvDone + 2 * ((j - 1) & 1) + h), ((j - 1) >> 1) & 1, abort_flag,
+                                  kStatusSoftmax)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t o_addr = tmem + lane_base + kColO + 128u * h;
+                    const float2 a2 = make_float2(alpha, alpha);
+                    // 64 columns per round trip
+                    #pragma unroll 1
+                    for (int c = 0; c < p.pv_n; c += 64) {
+                        tmem_ld32(o_addr + c, xa);
+                        tmem_ld32(o_addr + c + 32, xb);
+                        tc_wait_ld();
+                        #pragma unroll
+                        for (int i = 0; i < 32; i += 2) {
+                            const float2 ta = __fmul2_rn(make_float2(__uint_as_float(xa[i]), __uint_as_float(xa[i + 1])), a2);
+                            const float2 tb = __fmul2_rn(make_float2(__uint_as_float(xb[i]), __uint_as_float(xb[i + 1])), a2);
+                            xa[i] = __float_as_uint(ta.x);
+                            xa[i + 1] = __float_as_uint(ta.y);
+                            xb[i] = __float_as_uint(tb.x);
+                            xb[i + 1] = __float_as_uint(tb.y);
+                        }
+                        tmem_st32(o_addr + c, xa);
+                        tmem_st32(o_addr + c + 32, xb);
+                    }
+                    tc_wait_st();
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kBarPFull + 2 * b + h));
             }
         }
     }
