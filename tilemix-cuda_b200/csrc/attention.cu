@@ -33,6 +33,8 @@
 //              stages each), 128-byte swizzled; publishes each block's
 //              routing summary, per-half MMA plans and K scales in a
 //              shared-memory ring
+//   warp 11    spare: completes the control warpgroup (warps 8-11), whose
+//              registers setmaxnreg lowers so the softmax warps get more
 // MMA order, per key half h (one MMA warp each): QK(0), QK(1), then per block
 // j: PV(j) of half h as soon as softmax half h has published P(j), then
 // QK(j+2) of half h (N = 64) into the S columns that PV(j) just read (same
