@@ -52,6 +52,31 @@ __device__ __forceinline__ std::int8_t quantize_one(float x, float scale, float 
     return quantize_exact(x, scale);
 }
 
+// quantize_one for the two elements of a half2, the multiply and the adds on
+// packed f32x2 (one instruction per pair, same roundings). Returns the two
+// signed bytes in bits [0, 16).
+__device__ __forceinline__ uint32_t quantize_pair(__half2 h, float scale, float2 recip2) {
+    const float2 x = __half22float2(h);
+    const float2 t = __fadd2_rn(__fmul2_rn(make_float2(fabsf(x.x), fabsf(x.y)), recip2), make_float2(0.5f, 0.5f));
+    const float2 whole = make_float2(truncf(t.x), truncf(t.y));
+    const float2 frac = __ffma2_rn(whole, make_float2(-1.0f, -1.0f), t);   // exact
+    uint32_t out = 0u;
+    #pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const float f = k ? frac.y : frac.x;
+        const float xv = k ? x.y : x.x;
+        std::int8_t q;
+        if (f > 0x1p-14f && f < 1.0f - 0x1p-14f) {        // false for NaN
+            const int mag = min(127, __float2int_rz(k ? whole.y : whole.x));
+            q = static_cast<std::int8_t>(xv < 0.0f ? -mag : mag);
+        } else {
+            q = quantize_exact(xv, scale);
+        }
+        out |= static_cast<uint32_t>(static_cast<uint8_t>(q)) << (8 * k);
+    }
+    return out;
+}
+
 __device__ __forceinline__ float block_max(float value, float* scratch) {
     #pragma unroll
     for (int offset = 16; offset > 0; offset >>= 1) {
@@ -76,7 +101,7 @@ struct QuantTensor {
     bool vector_ok;  // 16-byte aligned input, 8-byte aligned output, d % 8 == 0
 };
 
-__global__ void __launch_bounds__(kQuantThreads)
+__global__ void __launch_bounds__(kQuantThreads, 5)
 quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
     __shared__ float scratch[kQuantThreads / 32];
     const int q_ctas = heads * qt.blocks;
@@ -94,31 +119,32 @@ quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
     if (t.vector_ok) {
         uint4 chunk[kMaxChunksPerThread];
         const int chunks = count >> 3;
-        float local = 0.0f;
+        // absmax on packed halves: |x| and max are exact in fp16, and __hmax2
+        // ignores a NaN input like fmaxf
+        __half2 m2 = __float2half2_rn(0.0f);
         #pragma unroll
         for (int i = 0; i < kMaxChunksPerThread; ++i) {
             const int c = threadIdx.x + i * kQuantThreads;
             if (c < chunks) {
                 chunk[i] = __ldg(reinterpret_cast<const uint4*>(src) + c);
-                const __half* h = reinterpret_cast<const __half*>(&chunk[i]);
+                const __half2* h = reinterpret_cast<const __half2*>(&chunk[i]);
                 #pragma unroll
-                for (int e = 0; e < 8; ++e) local = fmaxf(local, fabsf(__half2float(h[e])));
+                for (int e = 0; e < 4; ++e) m2 = __hmax2(m2, __habs2(h[e]));
             }
         }
+        const float local = fmaxf(__low2float(m2), __high2float(m2));
         const float scale = __fdiv_rn(block_max(local, scratch), 127.0f);
         const float recip = scale > 0.0f ? __frcp_rn(scale) : 0.0f;
+        const float2 recip2 = make_float2(recip, recip);
         if (threadIdx.x == 0) t.scales[static_cast<std::size_t>(head) * t.blocks + block] = __float2half_rn(scale);
         #pragma unroll
         for (int i = 0; i < kMaxChunksPerThread; ++i) {
             const int c = threadIdx.x + i * kQuantThreads;
             if (c < chunks) {
-                const __half* h = reinterpret_cast<const __half*>(&chunk[i]);
+                const __half2* h = reinterpret_cast<const __half2*>(&chunk[i]);
                 uint32_t packed[2] = {0u, 0u};
                 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const uint32_t byte = static_cast<uint8_t>(quantize_one(__half2float(h[e]), scale, recip));
-                    packed[e >> 2] |= byte << ((e & 3) * 8);
-                }
+                for (int e = 0; e < 4; ++e) packed[e >> 1] |= quantize_pair(h[e], scale, recip2) << ((e & 1) * 16);
                 reinterpret_cast<uint2*>(dst)[c] = make_uint2(packed[0], packed[1]);
             }
         }
