@@ -482,22 +482,19 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int nblk = p.causal ? min(p.kv_blocks, qt + 1) : p.kv_blocks;
     const int load_i8 = p.routed;
 
-    if (threadIdx.x == 0) {
-        mbar_init(bar(kBarQFull), 1);
-        // K and V stages are free once both MMA warps' reads have completed
-        for (int s = 0; s < kKStages; ++s) { mbar_init(bar(kBarKFull + s), 1); mbar_init(bar(kBarKEmpty + s), 2); }
-        for (int s = 0; s < kVStages; ++s) { mbar_init(bar(kBarVFull + s), 1); mbar_init(bar(kBarVEmpty + s), 2); }
-        for (int i = 0; i < 4; ++i) {
-            mbar_init(bar(kBarSFull + i), 1);
-            // one arrival per softmax warp of the half and per rescale warp
-            mbar_init(bar(kBarPFull + i), kSoftmaxWarps / 2 + 4);
-            mbar_init(bar(kBarPvDone + i), 1);
+    if (warp == 0) {
+        // One barrier per lane (the set-up barrier waits for the slowest
+        // lane, not for ~50 initialisations in a row). Arrival counts: the
+        // K and V stages are released by both MMA warps' commits; P-full
+        // takes one arrival per softmax warp of the half and per rescale
+        // warp; every other barrier one arrival (or one commit).
+        for (int i = static_cast<int>(lane); i < static_cast<int>(L::kNumBars); i += 32) {
+            const bool stage_empty = (i >= kBarKEmpty && i < kBarKEmpty + kKStages) ||
+                                     (i >= kBarVEmpty && i < kBarVEmpty + kVStages);
+            const bool p_full = i >= kBarPFull && i < kBarPFull + 4;
+            mbar_init(bar(i), p_full ? kSoftmaxWarps / 2 + 4 : stage_empty ? 2 : 1);
         }
-        mbar_init(bar(kBarDrain), 1);
-        mbar_init(bar(kBarDrain + 1), 1);
-        for (int r = 0; r < kRouteSlots; ++r) mbar_init(bar(kBarRoute + r), 1);
-        for (int i = 0; i < 16; ++i) mbar_init(bar(kBarAlpha + i), 1);
-        *abort_flag = 0;
+        if (lane == 0) *abort_flag = 0;
         mbar_init_fence();
         fence_proxy_async_smem();
     }
