@@ -188,7 +188,7 @@ def cpu_reference_sample(w_host: dict, cfg: dict, target_s: float) -> dict:
     Falls back to the C restatement (kind "port") without the reference build."""
     import numpy as np
     import oracle
-    if not oracle.ORACLE_SO.exists() or (not oracle.ref_available() and Path("/root/reference").exists()):
+    if not oracle.ORACLE_SO.exists() or (not oracle.ref_available() and oracle.reference_tree_present()):
         oracle.build()
     kind = "reference" if oracle.ref_available() else "port"
     use_ref = kind == "reference"

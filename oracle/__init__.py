@@ -42,11 +42,18 @@ _ref = None
 _ref_gpu = None
 
 
+# Where the reference checkout lives when it is present (build hosts only; the
+# prebuilt oracle/_ref libraries travel without it).
+REFERENCE_ROOT = Path(os.environ.get("TILEMIX_REFERENCE_ROOT", "/root/reference"))
+
+
+def reference_tree_present() -> bool:
+    return (REFERENCE_ROOT / "src" / "tests" / "reference_tilemix.h").is_file()
+
+
 def build(reference_root: str | None = None) -> None:
     """Compile the C oracle (and the reference shim when the tree exists)."""
-    cmd = ["bash", str(HERE / "build_ref.sh")]
-    if reference_root:
-        cmd.append(reference_root)
+    cmd = ["bash", str(HERE / "build_ref.sh"), reference_root or str(REFERENCE_ROOT)]
     subprocess.run(cmd, check=True, stdout=subprocess.DEVNULL)
 
 

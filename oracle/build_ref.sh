@@ -8,11 +8,11 @@
 #                                        (src/tilemix.cu) for sm_100a, compiled
 #                                        where they lie, behind ref_gpu_shim.cu
 #                                        (bench.py's "reference GPU" column)
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default /root/reference)
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: $TILEMIX_REFERENCE_ROOT)
 # The reference build is skipped, not failed, when the reference tree is absent.
 set -euo pipefail
 here="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-ref_root="${1:-/root/reference}"
+ref_root="${1:-${TILEMIX_REFERENCE_ROOT:-/root/reference}}"
 cuda_inc="${CUDA_HOME:-/usr/local/cuda}/include"
 
 mkdir -p "$here/_build"
