@@ -145,6 +145,26 @@ class ClockSampler:
                 "power_w_max": max(power) if power else None}
 
 
+# ------------------------------------------------------------------ output
+_JSON_OUT = None
+
+
+def claim_stdout() -> None:
+    """Keep the process's stdout for the one JSON line and point file
+    descriptor 1 at stderr, so nothing a library prints on its own (NCCL's
+    version banner on hosts that set NCCL_DEBUG, for one) can reach stdout."""
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 # -------------------------------------------------------------- distributed
 def dist_setup(args):
     import torch
@@ -393,7 +413,7 @@ def run_tilemix(args, rank, world, local):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ----------------------------------------------------------- reference arm
@@ -435,7 +455,7 @@ def run_reference(args, rank, world):
     gpu = reference_gpu_sample(args, cfg)
     if gpu is not None:
         line["reference_gpu"] = gpu
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def reference_gpu_sample(args, cfg, heads: int = 4, reps: int = 3):
@@ -487,6 +507,7 @@ def reference_gpu_sample(args, cfg, heads: int = 4, reps: int = 3):
 
 def main():
     args = parse_args()
+    claim_stdout()
     rank, world, local = dist_setup(args)
     try:
         if args.impl == "reference":
