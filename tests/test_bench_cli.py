@@ -1,0 +1,51 @@
+"""CPU: bench.py's output contract and constants the attention kernel relies on.
+
+The reference arm runs without a GPU (it times the reference's own CPU path),
+so the one-JSON-line-on-stdout contract is checked here; the GPU arm prints
+through the same function.
+"""
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def test_reference_arm_prints_exactly_one_json_line():
+    env = dict(os.environ, WORLD_SIZE="1", RANK="0", LOCAL_RANK="0")
+    proc = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", "1",
+                           "--warmup", "1", "--cpu-seconds", "0.2"],
+                          cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = proc.stdout.splitlines()
+    assert len(lines) == 1, proc.stdout
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference"
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    assert line["value"] > 0
+
+
+def test_int8_bias_constants():
+    """The attention kernel seeds INT8 accumulators with one f16 MMA of two
+    constant tiles: 16 products of fp16 0x6800 and 0x5E00 must sum exactly to
+    1.5 * 2^23, whose fp32 bits are 0x4B400000, and a dot |d| < 2^22 added to
+    those bits as an integer must read back as the float 1.5 * 2^23 + d."""
+    a = np.array([0x6800], np.uint16).view(np.float16)[0]
+    b = np.array([0x5E00], np.uint16).view(np.float16)[0]
+    assert float(a) == 2048.0 and float(b) == 384.0
+    total = np.float32(0)
+    for _ in range(16):
+        total = np.float32(total + np.float32(a) * np.float32(b))
+    assert total == np.float32(1.5 * 2**23)
+    assert int(np.array([total], np.float32).view(np.uint32)[0]) == 0x4B400000
+    dots = np.array([-(2**22) + 1, -16129 * 128, -1, 0, 1, 16129 * 128, 2**22 - 1], np.int64)
+    bits = (0x4B400000 + dots).astype(np.uint32)
+    back = bits.view(np.float32).astype(np.float64) - 12582912.0
+    assert np.array_equal(back, dots.astype(np.float64))
