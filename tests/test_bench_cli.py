@@ -32,6 +32,22 @@ def test_reference_arm_prints_exactly_one_json_line():
     assert line["value"] > 0
 
 
+def test_reference_arm_under_torchrun_two_ranks_prints_one_line():
+    """Under torchrun with two (gloo) ranks, rank 0 alone times and prints; the
+    other rank exits 0 without output."""
+    env = {k: v for k, v in os.environ.items() if k not in ("WORLD_SIZE", "RANK", "LOCAL_RANK")}
+    proc = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                           "--master-addr", "127.0.0.1", "--master-port", "29547", str(REPO / "bench.py"),
+                           "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "1",
+                           "--cpu-seconds", "0.2"],
+                          cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = proc.stdout.splitlines()
+    assert len(lines) == 1, proc.stdout
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["value"] > 0
+
+
 def test_int8_bias_constants():
     """The attention kernel seeds INT8 accumulators with one f16 MMA of two
     constant tiles: 16 products of fp16 0x6800 and 0x5E00 must sum exactly to
