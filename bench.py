@@ -11,10 +11,12 @@ quoted on.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--p P]
   python bench.py --impl reference ...   (the reference's CPU path, rank 0)
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own full batch
-of heads (independent (b, h) shards, no collective on the data path; weak
-scaling); NCCL is used only for the start/stop barriers and the max-over-ranks
-reduction of the device times. Rank 0 prints one JSON line.
+Multi-GPU (torchrun, one process per GPU): the batch's B*H heads are split
+into contiguous per-rank shards (strong scaling: the job is one config-3 batch
+at every N; independent (b, h) heads, no collective on the data path;
+--scaling weak gives every rank its own full batch instead). NCCL is used only
+for the start/stop barriers and the max-over-ranks reduction of the device
+times. Rank 0 prints one JSON line.
 """
 from __future__ import annotations
 
@@ -36,7 +38,6 @@ for p in (REPO, REPO / "tilemix-cuda_b200"):
         sys.path.insert(0, str(p))
 
 METRIC = "effective attention TFLOP/s and % of mix-weighted tensor peak, 1/2/4/8 B200"
-L2_BYTES = 126 * 2**20
 
 
 def parse_args():
@@ -49,8 +50,8 @@ def parse_args():
     ap.add_argument("--p", type=float, default=None, help="override the INT8 routing fraction")
     ap.add_argument("--cpu-seconds", type=float, default=6.0,
                     help="target CPU time of one reference-arm sample")
-    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
-                    help="weak: every rank runs a full batch; strong: the batch's heads are split over ranks")
+    ap.add_argument("--scaling", default="strong", choices=["weak", "strong"],
+                    help="strong (default): the batch's heads are split over ranks; weak: every rank runs a full batch")
     return ap.parse_args()
 
 
@@ -197,6 +198,37 @@ def barrier(world: int):
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
+
+
+def repo_libraries() -> list[str]:
+    """Shared objects under this repository mapped into this process (from
+    /proc/self/maps): which native code an arm actually ran."""
+    found = set()
+    try:
+        with open("/proc/self/maps") as f:
+            for line in f:
+                path = line.split()[-1] if len(line.split()) >= 6 else ""
+                if path.startswith(str(REPO)) and ".so" in Path(path).name:
+                    found.add(str(Path(path).relative_to(REPO)))
+    except OSError:
+        pass
+    return sorted(found)
+
+
+# ------------------------------------------------------------------ config
+def config_block(args, world: int) -> dict:
+    """The `config` object of the JSON line; both arms print it identically."""
+    from tilemix_b200 import workloads
+    cfg = workloads.config(args.config, p=args.p)
+    label = (f"{args.config}: B{cfg['B']} H{cfg['H']} S{cfg['S']} D{cfg['D']}"
+             f"{' causal' if cfg['causal'] else ''}, INT8 routing p={cfg['p']}"
+             f"{', x20 outlier channels' if cfg['outliers'] else ''}")
+    split = ("heads split into contiguous per-rank shards" if args.scaling == "strong"
+             else "every rank runs its own full batch")
+    return {"workload": label, "B": cfg["B"], "H": cfg["H"], "S": cfg["S"], "D": cfg["D"],
+            "causal": cfg["causal"], "int8_fraction_requested": cfg["p"],
+            "parallelism": f"batch x head shards over {world} GPU rank(s) ({args.scaling}: {split}), no collective",
+            "l2": "inputs larger than L2 (126 MiB) at the default configs; no flush"}
 
 
 # ------------------------------------------------------------- CPU baseline
@@ -373,24 +405,29 @@ def run_tilemix(args, rank, world, local):
         return
     peaks = measured_peaks()
     achieved = f_eff / (attn_avg * 1e-3) / 1e12
-    peak = peaks["bf16_tflops"]
     traffic_per_head = profiled_traffic().get(args.config)
     value = job_flops / (step_ms * 1e-3) / 1e12
     p_mix = workloads.mix_peak(f_eff, f_real) / 1e12
     i8_meas = measured_int8_tops()
     p_mix_meas = (workloads.mix_peak(f_eff, f_real, p_f16=peaks["bf16_tflops"] * 1e12, p_i8=i8_meas * 1e12) / 1e12
                   if i8_meas else None)
+    # The op's own peak: the mix-weighted tensor peak at this launch's realised
+    # INT8 share, from the measured bf16 GEMM (burst) and the measured INT8 GEMM.
+    if p_mix_meas is not None:
+        peak = p_mix_meas
+        peak_source = (f"mix-weighted peak at INT8 share {f_real:.3f} of the QK work: {peaks['source']} bf16 dense "
+                       f"{peaks['bf16_tflops']} TFLOP/s (burst, MEASURED_PEAKS.json) and measured INT8 GEMM "
+                       f"{i8_meas} TOPS (profiles/gemm_peaks_int8_fp16.txt)")
+    else:
+        peak = peaks["bf16_tflops"]
+        peak_source = f"{peaks['source']} bf16 dense (burst), MEASURED_PEAKS.json (no INT8 figure found)"
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": n, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "f16+i8 (f32 accumulate)", "data": "synthetic",
-        "config": {"workload": f"{args.config}: B{cfg0['B']} H{cfg0['H']} S{S} D{D}"
-                               f"{' causal' if cfg['causal'] else ''}, INT8 routing p={cfg['p']}"
-                               f"{', x20 outlier channels' if cfg['outliers'] else ''}",
-                   "B": cfg0["B"], "H": cfg0["H"], "S": S, "D": D, "causal": cfg["causal"],
-                   "int8_fraction_requested": cfg["p"], "int8_fraction_realised": round(f_real, 4),
-                   "per_gpu_heads": H, "parallelism": f"batch x head shards ({args.scaling}), {world} rank(s), no collective",
-                   "l2": f"inputs {3 * q.numel() * 2 / 2**20:.0f} MiB > L2 {L2_BYTES / 2**20:.0f} MiB; no flush"},
+        "config": config_block(args, world),
+        "int8_fraction_realised": round(f_real, 4), "per_gpu_heads": H,
+        "inputs_mib_per_gpu": round(3 * q.numel() * 2 / 2**20, 1),
         "pct_of_mix_peak": round(100 * (f_eff / (step_ms * 1e-3) / 1e12) / p_mix, 2),
         "mix_peak_tflops": round(p_mix, 1),
         "mix_peak_basis": "NVIDIA dense figures: 2250 TFLOP/s fp16, 4500 TOPS int8",
@@ -399,9 +436,10 @@ def run_tilemix(args, rank, world, local):
         "mix_peak_measured_tflops": round(p_mix_meas, 1) if p_mix_meas else None,
         "attention_ms": round(attn_avg, 4), "quantize_ms": round(quant_avg, 4),
         "quantize_gbs": round(3 * 2 * H * S * D / (quant_avg * 1e-3) / 1e9, 1),
-        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4),
-                     "peak_source": f"{peaks['source']} bf16 dense (burst), MEASURED_PEAKS.json",
+                     "peak_source": peak_source,
+                     "frac_of_bf16_peak": round(achieved / peaks["bf16_tflops"], 4),
                      "traffic": None if traffic_per_head is None else traffic_per_head * H,
                      "kernel": "tilemix_attention_kernel",
                      "work": "F_eff = 4*B*H*S^2*D/2 (causal) algorithmic FLOPs per launch"},
@@ -410,6 +448,7 @@ def run_tilemix(args, rank, world, local):
                 "api": "tilemix_attention_from_host (C-ABI, pinned host buffers, pipelined over head chunks)"},
         "clocks": clk,
         "gpu_launches": 2 * n,
+        "repo_native_so": repo_libraries(),
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
@@ -429,14 +468,19 @@ def run_reference(args, rank, world):
     # a few heads of the workload, drawn with the CPU generator (the sample uses whole heads)
     w = workloads.make_inputs(args.config, p=args.p, batch=1, heads=min(cfg["H"], 16))
     host = {"q": w["q"].numpy(), "k": w["k"].numpy(), "v": w["v"].numpy(), "words": w["words"].numpy()}
-    values = []
+    values, walls = [], []
     last = None
-    # each step is a bounded sample, so that the whole run ends within a few minutes
+    # Each step is one bounded sample of the workload (whole heads), so that
+    # the whole run ends within a few minutes; the throughput of a sample is
+    # the full workload's FLOPs over its extrapolated step time.
     per_step = max(0.5, min(args.cpu_seconds, 150.0 / (args.warmup + args.steps)))
     for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
         last = cpu_reference_sample(host, cfg, per_step)
+        wall = time.perf_counter() - t0
         if i >= args.warmup:
             values.append(last["step_seconds"])
+            walls.append(wall)
     step_s = statistics.median(values)
     f_eff = workloads.effective_flops(cfg)
     value = f_eff / step_s / 1e12
@@ -444,17 +488,20 @@ def run_reference(args, rank, world):
            "sample": last["sample"]}
     line = {"metric": METRIC, "impl": "reference", "value": round(value, 6), "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(step_s * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+            # time that actually ran per step: one bounded sample (steps x this is the timed wall time)
+            "ms_per_step": round(statistics.median(walls) * 1e3, 1),
+            "ms_per_step_basis": "wall time of one bounded sample step (whole heads), not of a full-workload step",
+            "extrapolated_ms_per_full_step": round(step_s * 1e3, 1),
+            "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": None, "dtype": "f64 (reference CPU emulation)", "data": "synthetic",
-            "config": {"workload": f"{args.config}: B{cfg['B']} H{cfg['H']} S{cfg['S']} D{cfg['D']}"
-                                   f"{' causal' if cfg['causal'] else ''}, INT8 routing p={cfg['p']}",
-                       "B": cfg["B"], "H": cfg["H"], "S": cfg["S"], "D": cfg["D"], "causal": cfg["causal"]},
+            "config": config_block(args, world),
             "cpu_baseline": cpu,
             "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     gpu = reference_gpu_sample(args, cfg)
     if gpu is not None:
         line["reference_gpu"] = gpu
+    line["repo_native_so"] = repo_libraries()
     emit(line)
 
 

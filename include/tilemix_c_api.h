@@ -118,7 +118,9 @@ typedef struct tilemix_device_buffers {
  * is ordered after the work already queued on `stream`, and once `stream`
  * reaches the point of the call's return, hO holds the output. Same error
  * contract as tilemix_attention_batched; nothing is queued when an argument is
- * invalid. */
+ * invalid. If a launch fails after copies were queued, `stream` is made to wait
+ * for the copy streams before the error returns: the host buffers must stay
+ * valid until `stream` reaches that point (as on success). */
 int tilemix_attention_from_host(const void* hQ, const void* hK, const void* hV,
                                 const uint64_t* h_words, float* hO,
                                 const tilemix_device_buffers* dev, int heads, int M, int N,

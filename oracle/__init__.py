@@ -22,6 +22,7 @@ reference. The product library never imports it.
 from __future__ import annotations
 
 import ctypes
+import json
 import os
 import subprocess
 from pathlib import Path
@@ -42,18 +43,33 @@ _ref = None
 _ref_gpu = None
 
 
-# Where the reference checkout lives when it is present (build hosts only; the
-# prebuilt oracle/_ref libraries travel without it).
-REFERENCE_ROOT = Path(os.environ.get("TILEMIX_REFERENCE_ROOT", "/root/reference"))
+def _reference_root() -> Path | None:
+    """Where the reference checkout lives, when it is present (build hosts
+    only; the prebuilt oracle/_ref libraries travel without it): the
+    TILEMIX_REFERENCE_ROOT environment variable, else the `reference_path`
+    field of the repository's BASELINE.json. None when neither names one."""
+    env = os.environ.get("TILEMIX_REFERENCE_ROOT")
+    if env:
+        return Path(env)
+    baseline = HERE.parent / "BASELINE.json"
+    try:
+        path = json.loads(baseline.read_text()).get("reference_path")
+    except (OSError, ValueError):
+        path = None
+    return Path(path) if path else None
+
+
+REFERENCE_ROOT = _reference_root()
 
 
 def reference_tree_present() -> bool:
-    return (REFERENCE_ROOT / "src" / "tests" / "reference_tilemix.h").is_file()
+    return REFERENCE_ROOT is not None and (REFERENCE_ROOT / "src" / "tests" / "reference_tilemix.h").is_file()
 
 
 def build(reference_root: str | None = None) -> None:
     """Compile the C oracle (and the reference shim when the tree exists)."""
-    cmd = ["bash", str(HERE / "build_ref.sh"), reference_root or str(REFERENCE_ROOT)]
+    root = reference_root or (str(REFERENCE_ROOT) if REFERENCE_ROOT is not None else "")
+    cmd = ["bash", str(HERE / "build_ref.sh"), root]
     subprocess.run(cmd, check=True, stdout=subprocess.DEVNULL)
 
 

@@ -8,18 +8,19 @@
 #                                        (src/tilemix.cu) for sm_100a, compiled
 #                                        where they lie, behind ref_gpu_shim.cu
 #                                        (bench.py's "reference GPU" column)
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: $TILEMIX_REFERENCE_ROOT)
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: $TILEMIX_REFERENCE_ROOT;
+# oracle/__init__.py passes the reference_path of BASELINE.json when unset)
 # The reference build is skipped, not failed, when the reference tree is absent.
 set -euo pipefail
 here="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-ref_root="${1:-${TILEMIX_REFERENCE_ROOT:-/root/reference}}"
+ref_root="${1:-${TILEMIX_REFERENCE_ROOT:-}}"
 cuda_inc="${CUDA_HOME:-/usr/local/cuda}/include"
 
 mkdir -p "$here/_build"
 gcc -std=c11 -O3 -march=x86-64-v3 -ffp-contract=off -fopenmp -fPIC -shared -Wall -Wextra \
     "$here/tilemix_oracle.c" -o "$here/_build/libtilemix_oracle.so" -lm
 
-if [[ -f "$ref_root/src/tests/reference_tilemix.h" ]]; then
+if [[ -n "$ref_root" && -f "$ref_root/src/tests/reference_tilemix.h" ]]; then
     mkdir -p "$here/_ref"
     g++ -std=c++17 -O3 -march=x86-64-v3 -ffp-contract=off -fopenmp -fPIC -shared \
         -I"$cuda_inc" -I"$ref_root/src/tests" -I"$ref_root/include" \

@@ -30,6 +30,42 @@ def test_reference_arm_prints_exactly_one_json_line():
         assert key in line, key
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     assert line["value"] > 0
+    # the reference arm runs the reference's code only: no library of this
+    # repository's product is mapped (only oracle/ builds of the reference)
+    assert line["repo_native_so"], line
+    assert all(p.startswith("oracle/") for p in line["repo_native_so"]), line["repo_native_so"]
+    # steps x ms_per_step is time that ran (one bounded sample per step)
+    assert line["ms_per_step"] * line["steps"] < 600e3
+    assert line["extrapolated_ms_per_full_step"] > 0
+
+
+def _bench_module():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", REPO / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    return bench
+
+
+def test_reference_arm_config_is_the_tilemix_arms():
+    """Both arms build `config` with the same function from the same arguments,
+    so the driver's same-config check holds (outlier note included)."""
+    bench = _bench_module()
+    env = dict(os.environ, WORLD_SIZE="1", RANK="0", LOCAL_RANK="0")
+    proc = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", "1",
+                           "--warmup", "1", "--cpu-seconds", "0.2"],
+                          cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    line = json.loads(proc.stdout.splitlines()[0])
+    sys_argv, sys.argv = sys.argv, ["bench.py"]
+    try:
+        args = bench.parse_args()
+    finally:
+        sys.argv = sys_argv
+    assert line["config"] == bench.config_block(args, 1)
+    assert "outlier" in line["config"]["workload"]
+    src = (REPO / "bench.py").read_text()
+    assert src.count('"config": config_block(args, world)') == 2
 
 
 def test_reference_arm_under_torchrun_two_ranks_prints_one_line():

@@ -80,3 +80,51 @@ def test_attention_bshd_op_is_rounded_default(dtype):
     ref = torch.ops.tilemix.attention(q, k, v, q8, k8, qs, ks, words, 2, w["score_scale"], True)
     got = torch.ops.tilemix.attention_bshd(q, k, v, q8, k8, qs, ks, words, 2, w["score_scale"], True, H, dtype)
     assert torch.equal(got, ref.view(B, H, 256, -1).permute(0, 2, 1, 3).to(dtype))
+
+
+def _meta(shape, dtype=torch.float16):
+    return torch.empty(shape, dtype=dtype, device="meta")
+
+
+@pytest.mark.parametrize("case", [
+    "k_heads", "k_dim", "v_shape", "q_dtype", "v_dtype", "q8_shape", "k8_dtype", "q_scales_size",
+    "k_scales_size", "words_dtype", "words_short", "words_without_quantized", "partial_quantized", "q_rank"])
+def test_validate_rejects_mismatched_tensors(case):
+    """The operators and convenience wrappers refuse tensors whose dtype or
+    shape disagrees with q's before a device pointer reaches the C-ABI (the
+    kernel takes heads and d from q and would read past a smaller tensor)."""
+    import tilemix_b200 as tm
+    heads, m, n, d = 3, 300, 257, 128
+    args = dict(q=_meta((heads, m, d)), k=_meta((heads, n, d)), v=_meta((heads, n, d)),
+                q8=_meta((heads, m, d), torch.int8), k8=_meta((heads, n, d), torch.int8),
+                q_scales=_meta((heads, 3)), k_scales=_meta((heads, 5)),
+                words=_meta((heads * tm.tilemix_routing_word_count(m, n, 2),), torch.int64))
+    tm.validate_attention_args(**args, key_tiles_per_group=2, device_check=False)   # the good case passes
+    bad = {
+        "k_heads": dict(k=_meta((2, n, d)), v=_meta((2, n, d))),
+        "k_dim": dict(k=_meta((heads, n, 64)), v=_meta((heads, n, 64))),
+        "v_shape": dict(v=_meta((heads, n - 1, d))),
+        "q_dtype": dict(q=_meta((heads, m, d), torch.float32)),
+        "v_dtype": dict(v=_meta((heads, n, d), torch.bfloat16)),
+        "q8_shape": dict(q8=_meta((heads, m - 1, d), torch.int8)),
+        "k8_dtype": dict(k8=_meta((heads, n, d), torch.uint8)),
+        "q_scales_size": dict(q_scales=_meta((heads, 2))),
+        "k_scales_size": dict(k_scales=_meta((heads, 5), torch.float32)),
+        "words_dtype": dict(words=_meta((heads * 19,), torch.int32)),
+        "words_short": dict(words=_meta((heads * tm.tilemix_routing_word_count(m, n, 2) - 1,), torch.int64)),
+        "words_without_quantized": dict(q8=None, k8=None, q_scales=None, k_scales=None),
+        "partial_quantized": dict(k8=None, words=None),
+        "q_rank": dict(q=_meta((1, heads, m, d))),
+    }[case]
+    args.update(bad)
+    with pytest.raises(ValueError):
+        tm.validate_attention_args(**args, key_tiles_per_group=2, device_check=False)
+
+
+def test_validate_rejects_host_tensors():
+    import tilemix_b200 as tm
+    q = torch.zeros((2, 64, 64), dtype=torch.float16)
+    with pytest.raises(ValueError):
+        tm.validate_quantize_args(q, q)
+    with pytest.raises(ValueError):
+        torch.ops.tilemix.attention(q, q, q, None, None, None, None, None, 2, 0.125, False)

@@ -226,22 +226,36 @@ cudaError_t from_host_impl(const __half* hQ, const __half* hK, const __half* hV,
     TM_TRY(pipeline_context(ctx, 2 * static_cast<std::size_t>(chunks) + 2));
     cudaEvent_t start = ctx.events[0], done = ctx.events[1];
     TM_TRY(cudaEventRecord(start, stream));
-    TM_TRY(cudaStreamWaitEvent(ctx.h2d, start, 0));
-    TM_TRY(cudaStreamWaitEvent(ctx.d2h, start, 0));
+    // From here on copies may be queued on the library's copy streams. If a
+    // later step fails, `stream` is made to wait for both copy streams before
+    // the error returns, so the caller's host buffers are no longer read or
+    // written once `stream` reaches the point of the return.
+    auto join_on_error = [&](cudaError_t failure) {
+        if (cudaEventRecord(start, ctx.h2d) == cudaSuccess) cudaStreamWaitEvent(stream, start, 0);
+        if (cudaEventRecord(done, ctx.d2h) == cudaSuccess) cudaStreamWaitEvent(stream, done, 0);
+        return failure;
+    };
+#define TM_TRY_JOIN(expr)                                          \
+    do {                                                           \
+        const cudaError_t tm_status_ = (expr);                     \
+        if (tm_status_ != cudaSuccess) return join_on_error(tm_status_); \
+    } while (0)
+    TM_TRY_JOIN(cudaStreamWaitEvent(ctx.h2d, start, 0));
+    TM_TRY_JOIN(cudaStreamWaitEvent(ctx.d2h, start, 0));
     int h0 = 0;
     for (int c = 0; c < chunks; h0 += sizes[c], ++c) {
         const int hn = sizes[c];
         const std::size_t qo = h0 * q_elems, kvo = h0 * kv_elems;
         cudaEvent_t in = ctx.events[2 + 2 * c], out = ctx.events[3 + 2 * c];
-        TM_TRY(cudaMemcpyAsync(dq + qo, hQ + qo, hn * q_elems * sizeof(__half), cudaMemcpyHostToDevice, ctx.h2d));
-        TM_TRY(cudaMemcpyAsync(dk + kvo, hK + kvo, hn * kv_elems * sizeof(__half), cudaMemcpyHostToDevice, ctx.h2d));
-        TM_TRY(cudaMemcpyAsync(dv + kvo, hV + kvo, hn * kv_elems * sizeof(__half), cudaMemcpyHostToDevice, ctx.h2d));
+        TM_TRY_JOIN(cudaMemcpyAsync(dq + qo, hQ + qo, hn * q_elems * sizeof(__half), cudaMemcpyHostToDevice, ctx.h2d));
+        TM_TRY_JOIN(cudaMemcpyAsync(dk + kvo, hK + kvo, hn * kv_elems * sizeof(__half), cudaMemcpyHostToDevice, ctx.h2d));
+        TM_TRY_JOIN(cudaMemcpyAsync(dv + kvo, hV + kvo, hn * kv_elems * sizeof(__half), cudaMemcpyHostToDevice, ctx.h2d));
         TileMixRouting routing{};
         routing.key_tiles_per_group = g;
         TileMixQuantized quantized{};
         if (routed) {
             const std::size_t wo = h0 * words_per_head;
-            TM_TRY(cudaMemcpyAsync(dev->words + wo, h_words + wo, hn * words_per_head * sizeof(std::uint64_t),
+            TM_TRY_JOIN(cudaMemcpyAsync(dev->words + wo, h_words + wo, hn * words_per_head * sizeof(std::uint64_t),
                                    cudaMemcpyHostToDevice, ctx.h2d));
             routing.words = dev->words + wo;
             routing.word_count = hn * words_per_head;
@@ -250,22 +264,23 @@ cudaError_t from_host_impl(const __half* hQ, const __half* hK, const __half* hV,
             quantized.q_scales = dqs + h0 * q_scale_blocks;
             quantized.k_scales = dks + h0 * k_scale_blocks;
         }
-        TM_TRY(cudaEventRecord(in, ctx.h2d));
-        TM_TRY(cudaStreamWaitEvent(stream, in, 0));
+        TM_TRY_JOIN(cudaEventRecord(in, ctx.h2d));
+        TM_TRY_JOIN(cudaStreamWaitEvent(stream, in, 0));
         if (routed) {
-            TM_TRY(quantize_impl(dq + qo, dk + kvo, dev->q8 + qo, dev->k8 + kvo, dqs + h0 * q_scale_blocks,
+            TM_TRY_JOIN(quantize_impl(dq + qo, dk + kvo, dev->q8 + qo, dev->k8 + kvo, dqs + h0 * q_scale_blocks,
                                  dks + h0 * k_scale_blocks, hn, M, N, d, stream));
         }
-        TM_TRY(attention_impl(dq + qo, dk + kvo, dv + kvo, dev->o + qo, hn, M, N, d, score_scale, causal, stream,
+        TM_TRY_JOIN(attention_impl(dq + qo, dk + kvo, dv + kvo, dev->o + qo, hn, M, N, d, score_scale, causal, stream,
                               routing, quantized));
-        TM_TRY(cudaEventRecord(out, stream));
-        TM_TRY(cudaStreamWaitEvent(ctx.d2h, out, 0));
-        TM_TRY(cudaMemcpyAsync(hO + qo, dev->o + qo, hn * q_elems * sizeof(float), cudaMemcpyDeviceToHost, ctx.d2h));
+        TM_TRY_JOIN(cudaEventRecord(out, stream));
+        TM_TRY_JOIN(cudaStreamWaitEvent(ctx.d2h, out, 0));
+        TM_TRY_JOIN(cudaMemcpyAsync(hO + qo, dev->o + qo, hn * q_elems * sizeof(float), cudaMemcpyDeviceToHost, ctx.d2h));
     }
-    TM_TRY(cudaEventRecord(done, ctx.d2h));
+    TM_TRY_JOIN(cudaEventRecord(done, ctx.d2h));
     return cudaStreamWaitEvent(stream, done, 0);
 }
 
+#undef TM_TRY_JOIN
 #undef TM_TRY
 
 }  // namespace

@@ -5,8 +5,10 @@ The names, argument meaning and error behaviour follow the reference's C++ API
 ``cudaError_t`` code as an int (0 = success) instead of raising, exactly like the
 C++ entry points, and take device tensors (torch CUDA tensors or raw device
 addresses). Everything goes through the extern "C" ABI declared in
-``include/tilemix_c_api.h``; there is no CPU fallback: importing this module on a
-machine without the built library raises.
+``include/tilemix_c_api.h``; there is no CPU fallback: every entry point raises
+on a machine without the built library. The library is mapped on the first
+call, not at import, so pure-Python helpers such as ``workloads`` load no
+native code.
 """
 from __future__ import annotations
 
@@ -90,7 +92,24 @@ def _load():
     return lib
 
 
-lib = _load()
+_lib = None
+
+
+def _native():
+    """The loaded libtilemix_b200.so. Loaded on first use, so that importing the
+    package (or its pure-Python helpers such as ``workloads``) maps no native
+    code; a call on a machine without the built library raises."""
+    global _lib
+    if _lib is None:
+        _lib = _load()
+    return _lib
+
+
+def __getattr__(name):
+    if name == "lib":
+        return _native()
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
+
 
 # every symbol include/tilemix_c_api.h declares
 C_ABI_SYMBOLS = (
@@ -149,26 +168,26 @@ class TileMixQuantized:
 
 
 def tilemix_routing_words_per_row(n: int, key_tiles_per_group: int) -> int:
-    return int(lib.tilemix_routing_words_per_row_c(n, key_tiles_per_group))
+    return int(_native().tilemix_routing_words_per_row_c(n, key_tiles_per_group))
 
 
 def tilemix_routing_word_count(m: int, n: int, key_tiles_per_group: int) -> int:
-    return int(lib.tilemix_routing_word_count_c(m, n, key_tiles_per_group))
+    return int(_native().tilemix_routing_word_count_c(m, n, key_tiles_per_group))
 
 
 def tilemix_shared_bytes(d: int, quantized: bool) -> int:
-    return int(lib.tilemix_reference_shared_bytes(d, int(quantized)))
+    return int(_native().tilemix_reference_shared_bytes(d, int(quantized)))
 
 
 def tilemix_b200_shared_bytes(d: int, quantized: bool = True) -> int:
-    return int(lib.tilemix_b200_shared_bytes_c(d, int(quantized)))
+    return int(_native().tilemix_b200_shared_bytes_c(d, int(quantized)))
 
 
 def quantize_tilemix_qk(Q, K, Q8, K8, q_scales, k_scales, M: int, N: int, d: int,
                         stream=None) -> int:
     """Stage 1 (reference src/tilemix.cu:223-236). Returns a cudaError_t code."""
-    return lib.tilemix_quantize_qk(_addr(Q), _addr(K), _addr(Q8), _addr(K8), _addr(q_scales),
-                                   _addr(k_scales), M, N, d, _stream(stream))
+    return _native().tilemix_quantize_qk(_addr(Q), _addr(K), _addr(Q8), _addr(K8), _addr(q_scales),
+                                         _addr(k_scales), M, N, d, _stream(stream))
 
 
 def launch_fused_fp16_attention(Q, K, V, O, M: int, N: int, d: int, score_scale: float,
@@ -177,16 +196,16 @@ def launch_fused_fp16_attention(Q, K, V, O, M: int, N: int, d: int, score_scale:
     """Stages 2-5 (reference src/tilemix.cu:238-278). Returns a cudaError_t code."""
     r = (routing or TileMixRouting())._c()
     q = (quantized or TileMixQuantized())._c()
-    return lib.tilemix_fused_attention(_addr(Q), _addr(K), _addr(V), _addr(O), M, N, d,
-                                       float(score_scale), _stream(stream), ctypes.byref(r),
-                                       ctypes.byref(q))
+    return _native().tilemix_fused_attention(_addr(Q), _addr(K), _addr(V), _addr(O), M, N, d,
+                                             float(score_scale), _stream(stream), ctypes.byref(r),
+                                             ctypes.byref(q))
 
 
 def quantize_tilemix_qk_batched(Q, K, Q8, K8, q_scales, k_scales, heads: int, M: int, N: int,
                                 d: int, stream=None) -> int:
-    return lib.tilemix_quantize_qk_batched(_addr(Q), _addr(K), _addr(Q8), _addr(K8),
-                                           _addr(q_scales), _addr(k_scales), heads, M, N, d,
-                                           _stream(stream))
+    return _native().tilemix_quantize_qk_batched(_addr(Q), _addr(K), _addr(Q8), _addr(K8),
+                                                 _addr(q_scales), _addr(k_scales), heads, M, N, d,
+                                                 _stream(stream))
 
 
 def tilemix_attention_batched(Q, K, V, O, heads: int, M: int, N: int, d: int,
@@ -195,9 +214,9 @@ def tilemix_attention_batched(Q, K, V, O, heads: int, M: int, N: int, d: int,
                               quantized: TileMixQuantized | None = None) -> int:
     r = (routing or TileMixRouting())._c()
     q = (quantized or TileMixQuantized())._c()
-    return lib.tilemix_attention_batched(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
-                                         float(score_scale), int(bool(causal)), _stream(stream),
-                                         ctypes.byref(r), ctypes.byref(q))
+    return _native().tilemix_attention_batched(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
+                                               float(score_scale), int(bool(causal)), _stream(stream),
+                                               ctypes.byref(r), ctypes.byref(q))
 
 
 kTileMixOutF32, kTileMixOutF16, kTileMixOutBF16 = 0, 1, 2
@@ -239,10 +258,10 @@ def tilemix_attention_batched_out(Q, K, V, out: TileMixOutput | None, heads: int
     r = (routing or TileMixRouting())._c()
     q = (quantized or TileMixQuantized())._c()
     o = out._c() if out is not None else None
-    return lib.tilemix_attention_batched_out(_addr(Q), _addr(K), _addr(V),
-                                             ctypes.byref(o) if o is not None else None, heads, M, N, d,
-                                             float(score_scale), int(bool(causal)), _stream(stream),
-                                             ctypes.byref(r), ctypes.byref(q))
+    return _native().tilemix_attention_batched_out(_addr(Q), _addr(K), _addr(V),
+                                                   ctypes.byref(o) if o is not None else None, heads, M, N, d,
+                                                   float(score_scale), int(bool(causal)), _stream(stream),
+                                                   ctypes.byref(r), ctypes.byref(q))
 
 
 def _host_addr(x) -> int | None:
@@ -280,17 +299,17 @@ def tilemix_attention_from_host(hQ, hK, hV, h_words, hO, dev: TileMixDeviceBuffe
     """H2D copies, quantization, routed attention and the D2H copy of O for
     host (pinned) buffers, pipelined over chunks of heads. Returns a cudaError_t code."""
     b = dev._c() if dev is not None else None
-    return lib.tilemix_attention_from_host(_host_addr(hQ), _host_addr(hK), _host_addr(hV),
-                                           _host_addr(h_words), _host_addr(hO),
-                                           ctypes.byref(b) if b is not None else None,
-                                           heads, M, N, d, float(score_scale), int(bool(causal)),
-                                           key_tiles_per_group, chunk_heads, _stream(stream))
+    return _native().tilemix_attention_from_host(_host_addr(hQ), _host_addr(hK), _host_addr(hV),
+                                                 _host_addr(h_words), _host_addr(hO),
+                                                 ctypes.byref(b) if b is not None else None,
+                                                 heads, M, N, d, float(score_scale), int(bool(causal)),
+                                                 key_tiles_per_group, chunk_heads, _stream(stream))
 
 
 def read_and_clear_status() -> tuple[int, int]:
     """(cudaError_t, watchdog word) of the current device; synchronises."""
     s = ctypes.c_uint(0)
-    err = lib.tilemix_read_and_clear_status(ctypes.byref(s))
+    err = _native().tilemix_read_and_clear_status(ctypes.byref(s))
     return err, int(s.value)
 
 
@@ -304,19 +323,93 @@ def check(err: int, what: str = "tilemix call") -> None:
 
 
 # ------------------------------------------------- torch convenience wrappers
+def _current_stream(t):
+    """torch's current stream on t's device (the kernels are ordered with the
+    producers and consumers of t), as a raw cudaStream_t."""
+    import torch
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _heads3_shape(t, name: str):
+    _require(t.dim() in (2, 3), f"{name} must be [S, d] or [heads, S, d], got shape {tuple(t.shape)}")
+    return tuple(t.shape) if t.dim() == 3 else (1, *t.shape)
+
+
+def _on_device(t, like, device_check: bool) -> bool:
+    return not device_check or (t.is_cuda and t.device == like.device)
+
+
+def validate_quantize_args(q, k, device_check: bool = True) -> tuple[int, int, int, int]:
+    """Checks the tensors of a quantization call before any device pointer is
+    taken: fp16 CUDA tensors on one device, q [heads, M, d] and k [heads, N, d]
+    with equal heads and d (the kernel takes heads and d from q, so a smaller k
+    would be read past its end). Raises ValueError; returns (heads, M, N, d).
+    device_check=False skips the CUDA-device checks (shape checks on meta
+    tensors)."""
+    import torch
+    for t, name in ((q, "q"), (k, "k")):
+        _require(isinstance(t, torch.Tensor) and _on_device(t, q, device_check), f"{name} must be a CUDA tensor")
+        _require(t.dtype == torch.float16, f"{name} must be float16, got {t.dtype}")
+    _require(q.dim() == k.dim(), "q and k must have the same number of dimensions")
+    heads, m, d = _heads3_shape(q, "q")
+    kh, n, kd = _heads3_shape(k, "k")
+    _require(kh == heads and kd == d, f"k {tuple(k.shape)} does not match q {tuple(q.shape)} in heads and d")
+    return heads, m, n, d
+
+
+def validate_attention_args(q, k, v, q8=None, k8=None, q_scales=None, k_scales=None, words=None,
+                            key_tiles_per_group: int = 2, device_check: bool = True) -> tuple[int, int, int, int]:
+    """Checks dtypes, devices and cross-tensor shapes of an attention call:
+    q [heads, M, d], k and v [heads, N, d] fp16; q8/k8 int8 of q's/k's shape;
+    scales fp16 with heads * ceil(M/128) and heads * ceil(N/64) elements; the
+    routing words 64-bit with at least heads * tilemix_routing_word_count
+    elements. The C-ABI checks the scalar arguments; these checks keep it from
+    reading past the end of a tensor whose shape disagrees with q's.
+    Returns (heads, M, N, d)."""
+    import torch
+    heads, m, n, d = validate_quantize_args(q, k, device_check)
+    _require(isinstance(v, torch.Tensor) and _on_device(v, q, device_check), "v must be a CUDA tensor on q's device")
+    _require(v.dtype == torch.float16, f"v must be float16, got {v.dtype}")
+    _require(tuple(v.shape) == tuple(k.shape), f"v {tuple(v.shape)} must have k's shape {tuple(k.shape)}")
+    quant = (q8, k8, q_scales, k_scales)
+    if any(t is not None for t in quant):
+        _require(all(t is not None for t in quant), "q8, k8, q_scales and k_scales go together")
+        for t, name, dt, shape in ((q8, "q8", torch.int8, None), (k8, "k8", torch.int8, None),
+                                   (q_scales, "q_scales", torch.float16, heads * ((m - 1) // 128 + 1)),
+                                   (k_scales, "k_scales", torch.float16, heads * ((n - 1) // 64 + 1))):
+            _require(_on_device(t, q, device_check), f"{name} must be a CUDA tensor on q's device")
+            _require(t.dtype == dt, f"{name} must be {dt}, got {t.dtype}")
+            if shape is not None:
+                _require(t.numel() == shape, f"{name} must hold {shape} elements, got {t.numel()}")
+        _require(tuple(q8.shape) == tuple(q.shape), f"q8 {tuple(q8.shape)} must have q's shape")
+        _require(tuple(k8.shape) == tuple(k.shape), f"k8 {tuple(k8.shape)} must have k's shape")
+    if words is not None:
+        _require(_on_device(words, q, device_check), "words must be a CUDA tensor on q's device")
+        _require(words.dtype in (torch.int64, torch.uint64), f"words must be 64-bit, got {words.dtype}")
+        _require(q8 is not None, "routing words need the quantized operands (q8, k8, q_scales, k_scales)")
+        need = heads * tilemix_routing_word_count(m, n, key_tiles_per_group)
+        _require(words.numel() >= need, f"words must hold at least {need} elements, got {words.numel()}")
+    return heads, m, n, d
+
+
 def quantize(q, k, stream=None):
     """Allocate outputs and quantize [heads,M,d] / [heads,N,d] (or 2-D) fp16
-    CUDA tensors. Returns (q8, k8, q_scales, k_scales)."""
+    CUDA tensors. Returns (q8, k8, q_scales, k_scales). Runs on torch's current
+    stream of q's device unless `stream` is given."""
     import torch
-    q3 = q if q.dim() == 3 else q.unsqueeze(0)
-    k3 = k if k.dim() == 3 else k.unsqueeze(0)
-    heads, m, d = q3.shape
-    n = k3.shape[1]
+    heads, m, n, d = validate_quantize_args(q, k)
+    q, k = q.contiguous(), k.contiguous()
     q8 = torch.empty_like(q, dtype=torch.int8)
     k8 = torch.empty_like(k, dtype=torch.int8)
     qs = torch.empty((heads, (m - 1) // 128 + 1), dtype=torch.float16, device=q.device)
     ks = torch.empty((heads, (n - 1) // 64 + 1), dtype=torch.float16, device=q.device)
-    check(quantize_tilemix_qk_batched(q, k, q8, k8, qs, ks, heads, m, n, d, stream), "quantize")
+    check(quantize_tilemix_qk_batched(q, k, q8, k8, qs, ks, heads, m, n, d,
+                                      _current_stream(q) if stream is None else stream), "quantize")
     if q.dim() == 2:
         qs, ks = qs[0], ks[0]
     return q8, k8, qs, ks
@@ -325,17 +418,26 @@ def quantize(q, k, stream=None):
 def attention(q, k, v, *, q8=None, k8=None, q_scales=None, k_scales=None, words=None,
               key_tiles_per_group: int = 2, score_scale: float | None = None,
               causal: bool = False, out=None, stream=None):
-    """[heads,M,d] (or 2-D) fp16 CUDA tensors -> fp32 output through the C-ABI."""
+    """[heads,M,d] (or 2-D) fp16 CUDA tensors -> fp32 output through the C-ABI.
+    Runs on torch's current stream of q's device unless `stream` is given."""
     import torch
-    q3 = q if q.dim() == 3 else q.unsqueeze(0)
-    heads, m, d = q3.shape
-    n = (k if k.dim() == 3 else k.unsqueeze(0)).shape[1]
+    heads, m, n, d = validate_attention_args(q, k, v, q8, k8, q_scales, k_scales, words, key_tiles_per_group)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    if q8 is not None:
+        q8, k8, q_scales, k_scales = (t.contiguous() for t in (q8, k8, q_scales, k_scales))
+    if words is not None:
+        words = words.contiguous()
     if score_scale is None:
         score_scale = 1.0 / math.sqrt(d)
     if out is None:
         out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    else:
+        _require(out.is_cuda and out.device == q.device and out.dtype == torch.float32 and
+                 tuple(out.shape) == tuple(q.shape) and out.is_contiguous(),
+                 "out must be a contiguous float32 CUDA tensor of q's shape on q's device")
     routing = TileMixRouting(words, 0 if words is None else words.numel(), key_tiles_per_group)
     quantized = TileMixQuantized(q8, k8, q_scales, k_scales) if q8 is not None else None
-    check(tilemix_attention_batched(q, k, v, out, heads, m, n, d, score_scale, causal, stream,
-                                    routing, quantized), "attention")
+    check(tilemix_attention_batched(q, k, v, out, heads, m, n, d, score_scale, causal,
+                                    _current_stream(q) if stream is None else stream, routing, quantized),
+          "attention")
     return out

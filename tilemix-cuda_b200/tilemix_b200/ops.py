@@ -5,7 +5,9 @@ They call the same extern "C" entry points as the ctypes functions in
 ``tilemix_b200`` (``tilemix_quantize_qk_batched``, ``tilemix_attention_batched``)
 on the current CUDA stream, and register fake (meta) kernels so that shape
 propagation, ``torch.compile`` tracing and CUDA-graph capture see the outputs
-without running the GPU code. Layout: [heads, S, d] contiguous fp16 (a 2-D
+without running the GPU code. Every operator checks dtypes, devices and
+cross-tensor shapes (``validate_attention_args``) before a device pointer
+reaches the C-ABI. Layout: [heads, S, d] contiguous fp16 (a 2-D
 [S, d] tensor is one head), the reference's layout per head; the routing words
 are the reference's per-head mask words (``include/attention_fused.h:47-52``),
 ``words_per_head`` apart.
@@ -17,7 +19,8 @@ import math
 import torch
 
 from . import (TileMixOutput, TileMixQuantized, TileMixRouting, check, quantize_tilemix_qk_batched,
-               tilemix_attention_batched, tilemix_attention_batched_out)
+               tilemix_attention_batched, tilemix_attention_batched_out, validate_attention_args,
+               validate_quantize_args)
 
 _Q_ROWS, _K_ROWS = 128, 64   # quantization block rows (include/attention_fused.h:13-14)
 
@@ -26,13 +29,16 @@ def _heads3(x: torch.Tensor) -> torch.Tensor:
     return x if x.dim() == 3 else x.unsqueeze(0)
 
 
+def _contiguous(*ts):
+    return tuple(None if t is None else t.contiguous() for t in ts)
+
+
 @torch.library.custom_op("tilemix::quantize_qk", mutates_args=())
 def quantize_qk(q: torch.Tensor, k: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     """Per-block symmetric INT8 quantization of Q (128-row blocks) and K (64-row
     blocks): returns (q8, k8, q_scales [heads, ceil(M/128)], k_scales [heads, ceil(N/64)])."""
+    heads, m, n, d = validate_quantize_args(q, k)
     q3, k3 = _heads3(q).contiguous(), _heads3(k).contiguous()
-    heads, m, d = q3.shape
-    n = k3.shape[1]
     q8 = torch.empty(q.shape, dtype=torch.int8, device=q.device)
     k8 = torch.empty(k.shape, dtype=torch.int8, device=k.device)
     qs = torch.empty((heads, (m - 1) // _Q_ROWS + 1), dtype=torch.float16, device=q.device)
@@ -59,9 +65,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q8: torch.Tenso
     """Routed mixed-precision attention, fp32 output of q's shape. With
     ``words`` (uint64 mask words viewed as int64) the quantized operands are
     required; without, every tile runs FP16 (the reference's unrouted path)."""
+    heads, m, n, d = validate_attention_args(q, k, v, q8, k8, q_scales, k_scales, words, key_tiles_per_group)
     q3, k3, v3 = _heads3(q).contiguous(), _heads3(k).contiguous(), _heads3(v).contiguous()
-    heads, m, d = q3.shape
-    n = k3.shape[1]
+    q8, k8, q_scales, k_scales, words = _contiguous(q8, k8, q_scales, k_scales, words)
     out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
     routing = TileMixRouting(words, 0 if words is None else words.numel(), key_tiles_per_group)
     quantized = TileMixQuantized(q8, k8, q_scales, k_scales) if q8 is not None else None
@@ -84,9 +90,13 @@ def attention_bshd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q8: torch.
     """``attention`` with the output written by the kernel as [B, S, H, D]
     (heads = B * H of q's [heads, S, d]) in fp32, fp16 or bf16 (rounded to
     nearest even from the fp32 result)."""
+    heads, m, n, d = validate_attention_args(q, k, v, q8, k8, q_scales, k_scales, words, key_tiles_per_group)
     q3, k3, v3 = _heads3(q).contiguous(), _heads3(k).contiguous(), _heads3(v).contiguous()
-    heads, m, d = q3.shape
-    n = k3.shape[1]
+    q8, k8, q_scales, k_scales, words = _contiguous(q8, k8, q_scales, k_scales, words)
+    if heads_per_batch < 1 or heads % heads_per_batch:
+        raise ValueError(f"heads_per_batch {heads_per_batch} must divide the {heads} heads")
+    if out_dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        raise ValueError(f"out_dtype must be float32, float16 or bfloat16, got {out_dtype}")
     out = torch.empty((heads // heads_per_batch, m, heads_per_batch, d), dtype=out_dtype, device=q.device)
     routing = TileMixRouting(words, 0 if words is None else words.numel(), key_tiles_per_group)
     quantized = TileMixQuantized(q8, k8, q_scales, k_scales) if q8 is not None else None
