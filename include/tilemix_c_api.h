@@ -127,6 +127,37 @@ int tilemix_attention_from_host(const void* hQ, const void* hK, const void* hV,
                                 int d, float score_scale, int causal, int key_tiles_per_group,
                                 int chunk_heads, void* stream);
 
+/* Routed attention that allocates nothing (no counterpart in the reference;
+ * the reference and tilemix_attention_batched take the INT8 Q/K copies and
+ * their scales from the caller). For callers that cannot allocate device
+ * memory: an operator or plugin interface handed only its inputs and outputs
+ * at launch time, a binding with no access to the process's device allocator,
+ * or a framework whose caching allocator owns the device memory. Q, K, V
+ * (fp16) and O (fp32) are the caller's device buffers, as in
+ * tilemix_attention_batched; the INT8 copies of Q and K and their scales go to
+ * a fixed array of TILEMIX_NOALLOC_SCRATCH_BYTES of device memory inside the
+ * library, which every GPU that loads the library's code holds until the
+ * process exits. The call quantizes Q and K into it and runs the routed
+ * attention on the same stream; it calls no cudaMalloc, cudaFree or other
+ * allocating routine. With routing NULL or routing->words NULL every tile is
+ * FP16 and the scratch is not used.
+ *   - Limit: heads*M*d + heads*N*d bytes of INT8 copies, plus the scales, each
+ *     part rounded up to 256 bytes, must fit in TILEMIX_NOALLOC_SCRATCH_BYTES
+ *     (e.g. 64 heads of S = 4096, d = 128); larger problems return
+ *     cudaErrorMemoryAllocation (2) before anything is queued.
+ *   - Every call on a device shares the one array: calls whose work overlaps
+ *     on the GPU (other streams, other threads) race and corrupt each other's
+ *     intermediates. Order them on one stream or with events.
+ *   - The array keeps the last call's contents; every byte a call reads is
+ *     first written by that call's quantizer, so nothing needs clearing.
+ *   - The first call on each device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture.
+ * Otherwise the error contract of tilemix_attention_batched. */
+#define TILEMIX_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+int tilemix_attention_routed_noalloc(const void* Q, const void* K, const void* V, float* O,
+                                     int heads, int M, int N, int d, float score_scale, int causal,
+                                     const tilemix_routing* routing, void* stream);
+
 /* Sizing helpers (reference include/attention_fused.h:34-45). */
 size_t tilemix_routing_word_count_c(int M, int N, int key_tiles_per_group);
 size_t tilemix_routing_words_per_row_c(int N, int key_tiles_per_group);

@@ -87,6 +87,9 @@ def _load():
     lib.tilemix_attention_from_host.argtypes = [_P, _P, _P, _P, _P, ctypes.POINTER(_DeviceBuffers),
                                                 _I, _I, _I, _I, ctypes.c_float, _I, _I, _I, _P]
     lib.tilemix_attention_from_host.restype = _I
+    lib.tilemix_attention_routed_noalloc.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I,
+                                                     ctypes.POINTER(_Routing), _P]
+    lib.tilemix_attention_routed_noalloc.restype = _I
     lib.tilemix_read_and_clear_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
     lib.tilemix_read_and_clear_status.restype = _I
     return lib
@@ -115,7 +118,7 @@ def __getattr__(name):
 C_ABI_SYMBOLS = (
     "tilemix_abi_version", "tilemix_quantize_qk", "tilemix_fused_attention",
     "tilemix_quantize_qk_batched", "tilemix_attention_batched", "tilemix_attention_batched_out",
-    "tilemix_attention_from_host",
+    "tilemix_attention_from_host", "tilemix_attention_routed_noalloc",
     "tilemix_routing_word_count_c", "tilemix_routing_words_per_row_c",
     "tilemix_reference_shared_bytes", "tilemix_b200_shared_bytes_c",
     "tilemix_read_and_clear_status",
@@ -304,6 +307,27 @@ def tilemix_attention_from_host(hQ, hK, hV, h_words, hO, dev: TileMixDeviceBuffe
                                                  ctypes.byref(b) if b is not None else None,
                                                  heads, M, N, d, float(score_scale), int(bool(causal)),
                                                  key_tiles_per_group, chunk_heads, _stream(stream))
+
+
+# Size of the library's fixed device scratch used by
+# tilemix_attention_routed_noalloc (TILEMIX_NOALLOC_SCRATCH_BYTES).
+NOALLOC_SCRATCH_BYTES = 64 << 20
+cudaErrorMemoryAllocation = 2
+
+
+def tilemix_attention_routed_noalloc(Q, K, V, O, heads: int, M: int, N: int, d: int, score_scale: float,
+                                     causal: bool = False, routing: TileMixRouting | None = None,
+                                     stream=None) -> int:
+    """Quantization and routed attention with the INT8 Q/K copies and their
+    scales in the library's fixed device scratch, for callers that cannot
+    allocate device memory (they pass only Q, K, V, the routing words and O).
+    Problems whose INT8 copies exceed NOALLOC_SCRATCH_BYTES return
+    cudaErrorMemoryAllocation; calls that overlap on the GPU share the scratch
+    and race. Returns a cudaError_t code."""
+    r = (routing or TileMixRouting())._c()
+    return _native().tilemix_attention_routed_noalloc(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
+                                                      float(score_scale), int(bool(causal)), ctypes.byref(r),
+                                                      _stream(stream))
 
 
 def read_and_clear_status() -> tuple[int, int]:
