@@ -170,6 +170,18 @@ size_t tilemix_b200_shared_bytes_c(int d, int quantized);
  * synchronises the device and clears the word. 0 = no timeout seen. */
 int tilemix_read_and_clear_status(unsigned int* status);
 
+/* Watchdog self-test (no counterpart in the reference; for tests only): runs
+ * the unrouted attention kernel in a build in which one softmax warp of each
+ * CTA withholds its first "P ready" arrival, with every wait limited to
+ * wait_limit_us microseconds (1..1000000). The MMA warp's wait for that
+ * arrival runs out, the kernel records the MMA-wait bit (2) in the status word
+ * that tilemix_read_and_clear_status returns, and every role drains its
+ * in-flight copies and MMAs and returns. O is not valid afterwards. Needs
+ * 65 <= d <= 128, d % 16 == 0 and 16-byte aligned Q/K/V/O (the TMA build);
+ * otherwise cudaErrorNotSupported. */
+int tilemix_watchdog_selftest(const void* Q, const void* K, const void* V, float* O, int heads, int M,
+                              int N, int d, float score_scale, unsigned int wait_limit_us, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

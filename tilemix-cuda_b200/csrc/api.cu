@@ -53,7 +53,7 @@ cudaError_t quantize_impl(const __half* Q, const __half* K, std::int8_t* Q8, std
 cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, float* O, int heads,
                            int M, int N, int d, float score_scale, bool causal, cudaStream_t stream,
                            const TileMixRouting& routing, const TileMixQuantized& quantized,
-                           const TileMixOutput* strided = nullptr) {
+                           const TileMixOutput* strided = nullptr, unsigned long long watchdog_test_ns = 0) {
     // Same checks, same order as src/tilemix.cu:242-253.
     if (!Q || !K || !V || (!O && !strided) || heads <= 0 || M <= 0 || N <= 0 || d <= 0 ||
         !std::isfinite(score_scale) || routing.key_tiles_per_group <= 0 ||
@@ -103,6 +103,8 @@ cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, fl
         prob.o_stride_head = strided->stride_head;
         prob.o_stride_row = strided->stride_row;
     }
+    prob.watchdog_test = watchdog_test_ns != 0;
+    prob.watchdog_limit_ns = watchdog_test_ns;
     return tilemix::launch_attention(prob, stream);
 }
 
@@ -404,6 +406,15 @@ size_t tilemix_reference_shared_bytes(int d, int quantized) {
 
 size_t tilemix_b200_shared_bytes_c(int d, int quantized) {
     return tilemix_b200_shared_bytes(d, quantized != 0);
+}
+
+int tilemix_watchdog_selftest(const void* Q, const void* K, const void* V, float* O, int heads, int M, int N,
+                              int d, float score_scale, unsigned int wait_limit_us, void* stream) {
+    if (wait_limit_us == 0 || wait_limit_us > 1000000u) return static_cast<int>(cudaErrorInvalidValue);
+    return static_cast<int>(attention_impl(static_cast<const __half*>(Q), static_cast<const __half*>(K),
+                                           static_cast<const __half*>(V), O, heads, M, N, d, score_scale, false,
+                                           static_cast<cudaStream_t>(stream), TileMixRouting{}, TileMixQuantized{},
+                                           nullptr, 1000ull * wait_limit_us));
 }
 
 int tilemix_read_and_clear_status(unsigned int* status) {

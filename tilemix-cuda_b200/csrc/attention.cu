@@ -101,7 +101,7 @@ static_assert(2 * 128 * kSoftmaxRegs + 128 * kCtrlRegs + 128 * kCorrRegs <= 6553
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;              // S_a at 0, S_b at 128, O_0 at 256, O_1 at 384
 constexpr uint32_t kAtomBytes = 128 * 128;   // 128 rows x 128 bytes
-constexpr uint64_t kWaitLimitNs = 1000000000ull;
+constexpr uint64_t kWaitLimitNs = 1000000000ull;   // default watchdog limit of one wait
 constexpr uint32_t kSuspendNs = 200000;      // per try_wait suspension (wakes early on completion)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 15.0f;        // rescale only when the max grows by > 2^15 (P <= 32768)
@@ -235,6 +235,7 @@ struct Params {
     int f16_ksteps, i8_ksteps, pv_n;
     int o_vec;
     int o_tma;           // fp32 O written by TMA stores from shared memory
+    uint64_t wait_limit_ns;  // watchdog limit of one wait
     int head_group;      // heads scheduled together (their K/V stay L2-resident)
     int prefetch_ahead;  // CTA distance of the Q tile prefetched into L2 (the SM count)
     // strided output (kStrided variants)
@@ -244,30 +245,56 @@ struct Params {
     long long o_sb, o_sh, o_sm;
 };
 
+// Watchdog state of a CTA: the shared-memory abort flag every role polls and
+// the time limit of one wait (1 s; shorter only in the watchdog self-test).
+struct Watchdog {
+    volatile int* flag;
+    uint64_t limit_ns;
+};
+
 // Bounded wait, called by all 32 lanes of a warp; returns a warp-uniform
 // verdict. On timeout it records `code` and raises the CTA abort flag.
 // Slow path of a bounded wait. Kept inline: an out-of-line call from the
 // divergent slow path broke the warp convergence that the warp-wide
 // (.sync.aligned) tcgen05 instructions after the wait rely on.
-__device__ __forceinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+__device__ __forceinline__ bool wait_bar_slow(uint32_t bar, uint32_t parity, const Watchdog& wd,
                                            unsigned int code) {
     const uint64_t start = global_timer_ns();
     while (true) {
         if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
-        if (*abort_flag) return false;
-        if (global_timer_ns() - start > kWaitLimitNs) {
-            *abort_flag = 1;
+        if (*wd.flag) return false;
+        if (global_timer_ns() - start > wd.limit_ns) {
+            *wd.flag = 1;
             atomicOr(&g_tilemix_status, code);
             return false;
         }
     }
 }
 
-__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Watchdog& wd,
                                          unsigned int code) {
     bool ok = mbar_try_wait(bar, parity);
-    if (!ok) ok = wait_bar_slow(bar, parity, abort_flag, code);
+    if (!ok) ok = wait_bar_slow(bar, parity, wd, code);
     return __all_sync(0xffffffffu, ok);
+}
+
+// Drain wait, for asynchronous work this CTA issued itself (TMA loads into
+// its shared memory, MMAs on its TMEM) to finish before that memory is given
+// back. That work completes on its own, so this wait ignores the abort flag
+// (after an abort it is exactly the wait that matters) and gives up, with
+// kStatusDrain recorded, only after the time limit.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, const Watchdog& wd) {
+    if (!mbar_try_wait(bar, parity)) {
+        const uint64_t start = global_timer_ns();
+        while (!mbar_try_wait_suspend(bar, parity, kSuspendNs)) {
+            if (global_timer_ns() - start > wd.limit_ns) {
+                *wd.flag = 1;
+                atomicOr(&g_tilemix_status, kStatusDrain);
+                break;
+            }
+        }
+    }
+    __syncwarp();
 }
 
 // Handshake between the two softmax threads of a query row (threads t and
@@ -277,14 +304,14 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
 // alternate by tag parity: a thread can only reuse a slot after it has read
 // the partner's next word, which the partner writes after reading this one.
 __device__ __forceinline__ bool pair_wait_slow(volatile std::uint64_t* slot, uint32_t tag, std::uint64_t& v,
-                                            volatile int* abort_flag) {
+                                            const Watchdog& wd) {
     const uint64_t start = global_timer_ns();
     while (true) {
         v = *slot;
         if (static_cast<uint32_t>(v >> 32) == tag) return true;
-        if (*abort_flag) return false;
-        if (global_timer_ns() - start > kWaitLimitNs) {
-            *abort_flag = 1;
+        if (*wd.flag) return false;
+        if (global_timer_ns() - start > wd.limit_ns) {
+            *wd.flag = 1;
             atomicOr(&g_tilemix_status, kStatusSoftmax);
             return false;
         }
@@ -292,11 +319,11 @@ __device__ __forceinline__ bool pair_wait_slow(volatile std::uint64_t* slot, uin
 }
 
 __device__ __forceinline__ bool pair_exchange(volatile std::uint64_t* slots, int me, uint32_t tag, float mine,
-                                              float& theirs, volatile int* abort_flag) {
+                                              float& theirs, const Watchdog& wd) {
     slots[me] = (static_cast<std::uint64_t>(tag) << 32) | __float_as_uint(mine);
     std::uint64_t v = slots[me ^ 128];
     bool ok = static_cast<uint32_t>(v >> 32) == tag;
-    if (!ok) ok = pair_wait_slow(slots + (me ^ 128), tag, v, abort_flag);
+    if (!ok) ok = pair_wait_slow(slots + (me ^ 128), tag, v, wd);
     theirs = __uint_as_float(static_cast<uint32_t>(v));
     return __all_sync(0xffffffffu, ok);
 }
@@ -455,7 +482,7 @@ __device__ __forceinline__ void tile_of(const Params& p, int bid, int& head, int
     head = group0 + in_group % group_heads;
 }
 
-template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided>
+template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided, bool kWithholdArrive = false>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
@@ -472,7 +499,8 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     const uint32_t sbase = raw_u32 + pad;
     auto bar = [&](int i) -> uint32_t { return sbase + L::kBars + 8u * static_cast<uint32_t>(i); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+    volatile int* abort_ptr = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+    const Watchdog abort_flag{abort_ptr, p.wait_limit_ns};
 
     const int warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31u;
@@ -494,7 +522,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             const bool p_full = i >= kBarPFull && i < kBarPFull + 4;
             mbar_init(bar(i), p_full ? kSoftmaxWarps / 2 + 4 : stage_empty ? 2 : 1);
         }
-        if (lane == 0) *abort_flag = 0;
+        if (lane == 0) *abort_ptr = 0;
         mbar_init_fence();
         fence_proxy_async_smem();
     }
@@ -634,12 +662,12 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         // Drain: the newest load into each buffer must have landed before the
         // CTA may exit (normally long complete; matters only after an abort).
         if (kUseTma) {
-            wait_bar(bar(kBarQFull), 0, abort_flag, kStatusDrain);
+            drain_wait(bar(kBarQFull), 0, abort_flag);
             for (int j = max(0, k_issued - kKStages); j < k_issued; ++j) {
-                wait_bar(bar(kBarKFull + j % kKStages), (j / kKStages) & 1, abort_flag, kStatusDrain);
+                drain_wait(bar(kBarKFull + j % kKStages), (j / kKStages) & 1, abort_flag);
             }
             for (int j = max(0, v_issued - kVStages); j < v_issued; ++j) {
-                wait_bar(bar(kBarVFull + j % kVStages), (j / kVStages) & 1, abort_flag, kStatusDrain);
+                drain_wait(bar(kBarVFull + j % kVStages), (j / kVStages) & 1, abort_flag);
             }
         }
     } else if (warp == kMmaWarp || warp == kMmaWarp1) {
@@ -786,10 +814,11 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 issue_qk_half(q);
             }
         }
-        // Drain every MMA this thread issued before TMEM can be released.
+        // Drain every MMA this thread issued before TMEM can be released
+        // (after the final barrier, by warp 8).
         if (lane == 0) tc_commit(bar(kBarDrain + mh));
         __syncwarp();
-        wait_bar(bar(kBarDrain + mh), 0, abort_flag, kStatusDrain);
+        drain_wait(bar(kBarDrain + mh), 0, abort_flag);
     }
     } else if (warp < kSoftmaxWarps) {
         reg_alloc<kSoftmaxRegs>();
@@ -1012,7 +1041,10 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarPFull + 2 * b + half));
+            // Watchdog self-test only: softmax warp 0 withholds its first
+            // P-ready arrival, so the MMA warp of key half 0 waits in vain.
+            const bool withheld = kWithholdArrive && j == 0 && warp == 0;
+            if (lane == 0 && !withheld) mbar_arrive(bar(kBarPFull + 2 * b + half));
             if (!__all_sync(0xffffffffu, r_ready)) {
                 if (!wait_bar(bar(kBarRoute + (j + 1) % kRouteSlots), ((j + 1) / kRouteSlots) & 1, abort_flag,
                               kStatusSoftmax)) {
@@ -1210,9 +1242,9 @@ bool encode_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, in
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided = false>
+template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided = false, bool kWithholdArrive = false>
 cudaError_t launch_variant(const CUtensorMap* maps, const Params& p, unsigned grid, cudaStream_t stream) {
-    auto kernel = tilemix_attention_kernel<kAtoms, kUseTma, kTrace, kStrided>;
+    auto kernel = tilemix_attention_kernel<kAtoms, kUseTma, kTrace, kStrided, kWithholdArrive>;
     const int smem = static_cast<int>(SmemLayout<kAtoms>::kBytes);
     // The opt-in attribute is per device; set it the first time a device is seen.
     static int configured[64] = {0};
@@ -1298,6 +1330,7 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
         p.o_vec = (prob.d % unit == 0 && p.o_sb % unit == 0 && p.o_sh % unit == 0 && p.o_sm % unit == 0 &&
                    aligned16(prob.o_data)) ? 1 : 0;
     }
+    p.wait_limit_ns = prob.watchdog_test ? prob.watchdog_limit_ns : kWaitLimitNs;
     p.head_group = std::min(prob.heads, 8);
     const cudaError_t sm_status = sm_count(&p.prefetch_ahead);
     if (sm_status != cudaSuccess) return sm_status;
@@ -1324,6 +1357,12 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     p.o_tma = (!strided && prob.d % 32 == 0 && aligned16(prob.o) &&
                encode_map(&maps[5], prob.o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.heads, p.M, p.d, 32, 32)) ? 1 : 0;
     const unsigned g = static_cast<unsigned>(grid);
+    if (prob.watchdog_test) {
+        // The self-test instantiation exists for d = 65..128 with TMA, fp32
+        // output, no routing trace outputs.
+        if (atoms != 2 || !tma || strided || trace) return cudaErrorNotSupported;
+        return launch_variant<2, true, false, false, true>(maps, p, g, stream);
+    }
     if (strided) {
         // strided outputs carry no trace outputs (checked by the API layer)
         if (atoms == 1) return tma ? launch_variant<1, true, false, true>(maps, p, g, stream)

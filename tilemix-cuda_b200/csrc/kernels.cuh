@@ -43,6 +43,11 @@ struct AttentionProblem {
     int o_dtype;
     int o_heads_per_batch;
     long long o_stride_batch, o_stride_head, o_stride_row;
+    // Watchdog self-test: launch the instantiation in which one softmax warp
+    // withholds its first P-ready arrival, with waits limited to
+    // watchdog_limit_ns (the output is not valid; the status word is).
+    bool watchdog_test;
+    unsigned long long watchdog_limit_ns;
 };
 
 // Shared memory the attention kernel requests for head dim d.

@@ -90,6 +90,8 @@ def _load():
     lib.tilemix_attention_routed_noalloc.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I,
                                                      ctypes.POINTER(_Routing), _P]
     lib.tilemix_attention_routed_noalloc.restype = _I
+    lib.tilemix_watchdog_selftest.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, ctypes.c_uint, _P]
+    lib.tilemix_watchdog_selftest.restype = _I
     lib.tilemix_read_and_clear_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
     lib.tilemix_read_and_clear_status.restype = _I
     return lib
@@ -121,7 +123,7 @@ C_ABI_SYMBOLS = (
     "tilemix_attention_from_host", "tilemix_attention_routed_noalloc",
     "tilemix_routing_word_count_c", "tilemix_routing_words_per_row_c",
     "tilemix_reference_shared_bytes", "tilemix_b200_shared_bytes_c",
-    "tilemix_read_and_clear_status",
+    "tilemix_read_and_clear_status", "tilemix_watchdog_selftest",
 )
 
 
@@ -328,6 +330,19 @@ def tilemix_attention_routed_noalloc(Q, K, V, O, heads: int, M: int, N: int, d: 
     return _native().tilemix_attention_routed_noalloc(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
                                                       float(score_scale), int(bool(causal)), ctypes.byref(r),
                                                       _stream(stream))
+
+
+# watchdog status bits (which kind of wait gave up)
+STATUS_PRODUCER, STATUS_MMA, STATUS_SOFTMAX, STATUS_DRAIN = 1, 2, 4, 8
+
+
+def watchdog_selftest(Q, K, V, O, heads: int, M: int, N: int, d: int, score_scale: float,
+                      wait_limit_us: int, stream=None) -> int:
+    """Run the kernel build that withholds one P-ready arrival per CTA, with
+    waits limited to wait_limit_us; the watchdog must record STATUS_MMA and
+    the kernel return. O is not valid afterwards. Returns a cudaError_t code."""
+    return _native().tilemix_watchdog_selftest(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
+                                               float(score_scale), int(wait_limit_us), _stream(stream))
 
 
 def read_and_clear_status() -> tuple[int, int]:
