@@ -124,6 +124,26 @@ cudaError_t tilemix_attention_batched(const __half* Q, const __half* K, const __
                                       const TileMixRouting& routing = {},
                                       const TileMixQuantized& quantized = {});
 
+// K alone, quantized in 64-row blocks: the same bytes as the K half of
+// quantize_tilemix_qk_batched. The K pre-pass of the fused-Q path below.
+cudaError_t quantize_tilemix_k_batched(const __half* K, std::int8_t* K8, __half* k_scales,
+                                       int heads, int N, int d, cudaStream_t stream = nullptr);
+
+// Routed attention with the Q quantization fused into the attention kernel
+// (no reference counterpart; the reference quantizes Q in a separate kernel,
+// src/tilemix.cu:223-236). Each CTA's 128-row query tile is one Q quantization
+// block (kTileMixQQuantRows), so the CTA quantizes it itself from the fp16 tile
+// it loads anyway: one HBM pass over Q fewer. K8 / k_scales come from
+// quantize_tilemix_k_batched; routing words are required. Q8_out and
+// q_scales_out, when not null, receive exactly the Q8 bytes and fp16 scales
+// quantize_tilemix_qk_batched would produce; O equals, bit for bit, the output
+// of tilemix_attention_batched given those quantized operands.
+cudaError_t tilemix_attention_batched_qfused(const __half* Q, const __half* K, const __half* V, float* O,
+                                             int heads, int M, int N, int d, float score_scale, bool causal,
+                                             cudaStream_t stream, const TileMixRouting& routing,
+                                             const std::int8_t* K8, const __half* k_scales,
+                                             std::int8_t* Q8_out = nullptr, __half* q_scales_out = nullptr);
+
 // Output element types of TileMixOutput.
 enum TileMixOutputType : int { kTileMixOutF32 = 0, kTileMixOutF16 = 1, kTileMixOutBF16 = 2 };
 

@@ -61,6 +61,18 @@ int tilemix_attention_batched(const void* Q, const void* K, const void* V, float
                               void* stream, const tilemix_routing* routing,
                               const tilemix_quantized* quantized);
 
+/* K-only quantizer and routed attention with Q quantized inside the kernel
+ * (no reference counterpart): C forms of quantize_tilemix_k_batched and
+ * tilemix_attention_batched_qfused in attention_fused.h. Routing words, K8 and
+ * k_scales are required; Q8_out / q_scales_out may be NULL, else they receive
+ * the Q8 bytes and fp16 scales tilemix_quantize_qk_batched would produce. */
+int tilemix_quantize_k_batched(const void* K, int8_t* K8, void* k_scales, int heads, int N, int d,
+                               void* stream);
+int tilemix_attention_batched_qfused(const void* Q, const void* K, const void* V, float* O,
+                                     int heads, int M, int N, int d, float score_scale, int causal,
+                                     void* stream, const tilemix_routing* routing, const int8_t* K8,
+                                     const void* k_scales, int8_t* Q8_out, void* q_scales_out);
+
 /* Strided output of tilemix_attention_batched_out (layout-compatible with
  * TileMixOutput in attention_fused.h): head h = b * heads_per_batch + hh,
  * row m, column c goes to data + b * stride_batch + hh * stride_head +

@@ -118,3 +118,27 @@ def test_exhaustive_fp16_values_bit_exact(absmax):
     assert np.array_equal(q8, eq8) and np.array_equal(k8, ek8)
     assert np.array_equal(qs.view(np.uint16), eqs.view(np.uint16))
     assert np.array_equal(ks.view(np.uint16), eks.view(np.uint16))
+
+
+def test_nan_and_inf_blocks_take_the_exact_path():
+    """Blocks holding a NaN or an inf leave the branch-free rounding for the
+    element-wise exact path (the reference GPU kernel's semantics): a NaN input
+    gives 0 and does not enter the absmax; a block whose absmax is inf has an
+    inf scale and all-zero bytes. Neighbouring finite blocks are unaffected."""
+    rng = np.random.default_rng(9)
+    d = 64
+    q = rng.standard_normal((512, d)).astype(np.float16)
+    q[5, 7] = np.nan                  # Q block 0 (and K block 0)
+    q[300, 1] = -np.inf               # Q block 2 (and K block 4)
+    q8, k8, qs, ks = quantize_gpu(q, q)
+    finite = np.where(np.isnan(q), np.float16(0), q)
+    for got8, got_s, rows in ((q8, qs, 128), (k8, ks, 64)):
+        for b in range(512 // rows):
+            blk = slice(b * rows, (b + 1) * rows)
+            if np.isinf(q[blk]).any():
+                assert np.isinf(got_s[b]) and not got8[blk].any()
+                continue
+            e8, es = oracle.quantize(finite[blk], rows)
+            e8 = np.where(np.isnan(q[blk]), np.int8(0), e8)
+            assert np.array_equal(got8[blk], e8), (rows, b)
+            assert got_s[b].view(np.uint16) == es.view(np.uint16)[0], (rows, b)

@@ -108,6 +108,50 @@ cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, fl
     return tilemix::launch_attention(prob, stream);
 }
 
+cudaError_t quantize_k_impl(const __half* K, std::int8_t* K8, __half* k_scales, int heads, int N, int d,
+                            cudaStream_t stream) {
+    if (!K || !K8 || !k_scales || heads <= 0 || N <= 0 || d <= 0) return cudaErrorInvalidValue;
+    if (d > kFusedMaxHeadDim) return cudaErrorNotSupported;
+    if (!fits(heads, N, d)) return cudaErrorInvalidValue;
+    const cudaError_t status = check_device();
+    if (status != cudaSuccess) return status;
+    return tilemix::launch_quantize_k(K, K8, k_scales, heads, N, d, stream);
+}
+
+// Routed attention with Q quantized inside the kernel: the checks of
+// attention_impl, with the quantized inputs reduced to K8 and the K scales
+// (both required, as are the routing words); Q8_out / q_scales_out optional.
+cudaError_t attention_qfused_impl(const __half* Q, const __half* K, const __half* V, float* O, int heads, int M,
+                                  int N, int d, float score_scale, bool causal, cudaStream_t stream,
+                                  const TileMixRouting& routing, const std::int8_t* K8, const __half* k_scales,
+                                  std::int8_t* Q8_out, __half* q_scales_out) {
+    if (!Q || !K || !V || !O || heads <= 0 || M <= 0 || N <= 0 || d <= 0 || !std::isfinite(score_scale) ||
+        routing.key_tiles_per_group <= 0 || !routing.words || !K8 || !k_scales) {
+        return cudaErrorInvalidValue;
+    }
+    if (d > kFusedMaxHeadDim) return cudaErrorNotSupported;
+    const std::size_t per_head = tilemix_routing_word_count(M, N, routing.key_tiles_per_group);
+    if (routing.word_count / static_cast<std::size_t>(heads) < per_head) return cudaErrorInvalidValue;
+    if (!fits(heads, M, d) || !fits(heads, N, d)) return cudaErrorInvalidValue;
+    cudaError_t status = check_device();
+    if (status != cudaSuccess) return status;
+    if (static_cast<long long>((M - 1) / 128 + 1) * heads > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    tilemix::AttentionProblem prob{};
+    prob.q = Q; prob.k = K; prob.v = V; prob.o = O;
+    prob.words = routing.words;
+    prob.decoded_bits = routing.decoded_bits;
+    prob.key_tiles_per_group = routing.key_tiles_per_group;
+    prob.k8 = K8;
+    prob.k_scales = k_scales;
+    prob.heads = heads; prob.M = M; prob.N = N; prob.d = d;
+    prob.score_scale = score_scale;
+    prob.causal = causal;
+    prob.fuse_q = true;
+    prob.q8_out = Q8_out;
+    prob.q_scales_out = q_scales_out;
+    return tilemix::launch_attention(prob, stream);
+}
+
 TileMixRouting to_cpp(const tilemix_routing* r) {
     TileMixRouting out{};
     if (r) {
@@ -326,6 +370,19 @@ cudaError_t tilemix_attention_batched_out(const __half* Q, const __half* K, cons
                           &out);
 }
 
+cudaError_t quantize_tilemix_k_batched(const __half* K, std::int8_t* K8, __half* k_scales, int heads, int N, int d,
+                                       cudaStream_t stream) {
+    return quantize_k_impl(K, K8, k_scales, heads, N, d, stream);
+}
+
+cudaError_t tilemix_attention_batched_qfused(const __half* Q, const __half* K, const __half* V, float* O, int heads,
+                                             int M, int N, int d, float score_scale, bool causal, cudaStream_t stream,
+                                             const TileMixRouting& routing, const std::int8_t* K8,
+                                             const __half* k_scales, std::int8_t* Q8_out, __half* q_scales_out) {
+    return attention_qfused_impl(Q, K, V, O, heads, M, N, d, score_scale, causal, stream, routing, K8, k_scales,
+                                 Q8_out, q_scales_out);
+}
+
 // ---------------------------------------------------------------------- C-ABI
 extern "C" {
 
@@ -390,6 +447,21 @@ int tilemix_attention_from_host(const void* hQ, const void* hK, const void* hV, 
                                            static_cast<const __half*>(hV), h_words, hO, dev, heads, M, N, d,
                                            score_scale, causal != 0, key_tiles_per_group, chunk_heads,
                                            static_cast<cudaStream_t>(stream)));
+}
+
+int tilemix_quantize_k_batched(const void* K, int8_t* K8, void* k_scales, int heads, int N, int d, void* stream) {
+    return static_cast<int>(quantize_k_impl(static_cast<const __half*>(K), K8, static_cast<__half*>(k_scales), heads,
+                                            N, d, static_cast<cudaStream_t>(stream)));
+}
+
+int tilemix_attention_batched_qfused(const void* Q, const void* K, const void* V, float* O, int heads, int M, int N,
+                                     int d, float score_scale, int causal, void* stream,
+                                     const tilemix_routing* routing, const int8_t* K8, const void* k_scales,
+                                     int8_t* Q8_out, void* q_scales_out) {
+    return static_cast<int>(attention_qfused_impl(
+        static_cast<const __half*>(Q), static_cast<const __half*>(K), static_cast<const __half*>(V), O, heads, M, N,
+        d, score_scale, causal != 0, static_cast<cudaStream_t>(stream), to_cpp(routing), K8,
+        static_cast<const __half*>(k_scales), Q8_out, static_cast<__half*>(q_scales_out)));
 }
 
 size_t tilemix_routing_word_count_c(int M, int N, int key_tiles_per_group) {

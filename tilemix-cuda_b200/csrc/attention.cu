@@ -61,6 +61,7 @@
 // before TMEM is freed, so a protocol bug surfaces as an error status instead
 // of a hung GPU.
 #include "kernels.cuh"
+#include "quant_math.cuh"
 #include "sm100.cuh"
 
 #include <cuda.h>
@@ -143,9 +144,10 @@ struct SmemLayout {
     static constexpr uint32_t kRoute = kAlpha + 2 * 2 * kTileRows * 4;  // [kRouteSlots]
     static constexpr uint32_t kXchg = kRoute + kRouteSlots * sizeof(RouteSlot);  // [2][256] u64 pair handshake words
     static constexpr uint32_t kBars = kXchg + 2 * kSoftmaxThreads * 8;
-    static constexpr uint32_t kNumBars = 23 + kRouteSlots + 16;
+    static constexpr uint32_t kNumBars = 23 + kRouteSlots + 16 + 1;
     static constexpr uint32_t kMisc = kBars + kNumBars * 8;            // tmem base, abort flag
-    static constexpr uint32_t kEnd = kMisc + 16;
+    static constexpr uint32_t kQRed = kMisc + 16;                       // [2][8] fused-Q absmax per softmax warp
+    static constexpr uint32_t kEnd = kQRed + 64;
     static constexpr uint32_t kBytes = kEnd + 1024;                     // + alignment slack
     static_assert(kBytes <= 232448, "exceeds the 227 KB of shared memory a CTA can opt into");
     static_assert(kBiasA % 1024 == 0, "128-byte-swizzled operands start on 1024-byte boundaries");
@@ -153,11 +155,12 @@ struct SmemLayout {
 
 // S-full, P-full and PV-done are per (S buffer b, key half h) at base + 2 b + h;
 // the drain barrier per MMA warp; alpha-ready per (b, h, lane quarter q) at
-// base + 4 (2 b + h) + q.
+// base + 4 (2 b + h) + q; Q8-ready (fused Q quantization) takes one arrival per
+// softmax warp.
 enum Bar : int {
     kBarQFull = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7,
     kBarSFull = 9, kBarPFull = 13, kBarPvDone = 17, kBarDrain = 21, kBarRoute = 23,
-    kBarAlpha = 23 + kRouteSlots,
+    kBarAlpha = 23 + kRouteSlots, kBarQ8Ready = 23 + kRouteSlots + 16,
 };
 
 // QK plan of the tile for one key block, packed in 64 bits:
@@ -232,6 +235,10 @@ struct Params {
     float scale_log2;
     int causal;
     int routed;
+    int fuse_q;          // Q quantized inside the CTA (no Q8 / q_scales inputs)
+    std::int8_t* q8_out;      // fused Q: optional Q8 output [heads][M][d]
+    __half* q_scales_out;     // fused Q: optional scale output [heads][q_scale_blocks]
+    int q8_vec;          // q8_out takes 16-byte stores (d % 16 == 0, aligned)
     int f16_ksteps, i8_ksteps, pv_n;
     int o_vec;
     int o_tma;           // fp32 O written by TMA stores from shared memory
@@ -470,6 +477,129 @@ __device__ __forceinline__ void store_strided_row(const Params& p, long long row
     }
 }
 
+// Absmax of the Q tile over the 256 softmax threads: warp shuffles, then one
+// named barrier (id 1) of the eight softmax warps and a read of the eight
+// warp maxima in `red`. NaN-propagating when `nan` is set (the fast-path
+// verdict), NaN-ignoring otherwise; exact either way (fp16 magnitudes).
+__device__ __forceinline__ float block_absmax(float a, float b, float* red, int t, bool nan) {
+    auto mx = [nan](float x, float y) { return nan && (x != x || y != y) ? NAN : fmaxf(x, y); };
+    float local = mx(a, b);
+    #pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) local = mx(local, __shfl_xor_sync(0xffffffffu, local, offset));
+    if ((t & 31) == 0) red[t >> 5] = local;
+    asm volatile("bar.sync 1, %0;" :: "r"(kSoftmaxThreads) : "memory");
+    float total = 0.0f;
+    #pragma unroll
+    for (int w = 0; w < kSoftmaxWarps; ++w) total = mx(total, red[w]);
+    return total;
+}
+
+// Q quantization fused into the attention CTA. The CTA's 128-row query tile
+// is exactly one Q quantization block (reference include/attention_fused.h:13),
+// so the 256 softmax threads quantize it from the fp16 tile the producer has
+// loaded, before their first scores arrive: thread t takes row t / 2 and half
+// t % 2 of the row's 16-byte fp16 chunks, the block absmax is reduced through
+// warp shuffles and a named barrier of the eight softmax warps, and each
+// element is rounded by the standalone quantizer's own functions
+// (quant_math.cuh: branch-free for finite tiles, element-wise exact for tiles
+// holding NaN or inf), so Q8 and the scale are the same bytes
+// quantize_tilemix_qk produces. The INT8 tile goes straight into the
+// 128-byte-swizzled Q8 operand in shared memory; the MMA warps wait for the
+// Q8-ready barrier. Optionally Q8 and the fp16 scale are also written to
+// global memory. Called by all 256 softmax threads; returns false (after the
+// named barrier, which every thread reaches) when the Q wait gave up.
+template <int kAtoms>
+__device__ __forceinline__ bool quantize_q_tile(const Params& p, uint8_t* smem, uint32_t q_full_bar,
+                                                uint32_t q8_ready_bar, int head, int qt, const Watchdog& wd,
+                                                float& q_scale) {
+    using L = SmemLayout<kAtoms>;
+    constexpr int kChunks = 4 * kAtoms;                 // fp16 16-byte chunks per thread
+    const int t = static_cast<int>(threadIdx.x);        // 0..255
+    const int r = t >> 1, part = t & 1;
+    const uint32_t lane = threadIdx.x & 31u;
+    const bool ok = wait_bar(q_full_bar, 0, wd, kStatusSoftmax);
+    uint4 v[kChunks];
+    __half2 m2 = __float2half2_rn(0.0f);
+    #pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+        const int g = part * kChunks + i, atom = g >> 3, c = g & 7;
+        v[i] = ok ? *reinterpret_cast<const uint4*>(smem + L::kQ + atom * kAtomBytes + r * 128 + ((c ^ (r & 7)) << 4))
+                  : make_uint4(0u, 0u, 0u, 0u);
+        const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
+        #pragma unroll
+        for (int e = 0; e < 4; ++e) m2 = __hmax2_nan(m2, __habs2(h[e]));   // exact; a NaN reaches the verdict
+    }
+    float* red = reinterpret_cast<float*>(smem + L::kQRed);
+    float absmax = block_absmax(__low2float(m2), __high2float(m2), red, t, true);
+    uint4 q8[kChunks / 2];
+    float scale;
+    if (fast_block(absmax)) {
+        // every block of finite, not-all-zero inputs: branch-free exact rounding
+        scale = __fdiv_rn(absmax, 127.0f);
+        const float y = __frcp_rn(scale);
+        const float2 neg_s2 = make_float2(-scale, -scale), y2 = make_float2(y, y);
+        #pragma unroll
+        for (int i = 0; i < kChunks; i += 2) {
+            q8[i / 2] = make_uint4(quantize4_fast(v[i].x, v[i].y, neg_s2, y2), quantize4_fast(v[i].z, v[i].w, neg_s2, y2),
+                                   quantize4_fast(v[i + 1].x, v[i + 1].y, neg_s2, y2),
+                                   quantize4_fast(v[i + 1].z, v[i + 1].w, neg_s2, y2));
+        }
+    } else {
+        // NaN, +-inf or an all-zero tile (uniform over the CTA): absmax without
+        // NaN, then the element-wise exact rounding
+        m2 = __float2half2_rn(0.0f);
+        #pragma unroll
+        for (int i = 0; i < kChunks; ++i) {
+            const __half2* h = reinterpret_cast<const __half2*>(&v[i]);
+            #pragma unroll
+            for (int e = 0; e < 4; ++e) m2 = __hmax2(m2, __habs2(h[e]));   // ignores a NaN like fmaxf
+        }
+        absmax = block_absmax(__low2float(m2), __high2float(m2), red + kSoftmaxWarps, t, false);
+        scale = __fdiv_rn(absmax, 127.0f);
+        const float recip = scale > 0.0f ? __frcp_rn(scale) : 0.0f;
+        const float2 recip2 = make_float2(recip, recip);
+        #pragma unroll
+        for (int i = 0; i < kChunks; i += 2) {
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+            #pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const __half2* h = reinterpret_cast<const __half2*>(&v[i + k]);
+                #pragma unroll
+                for (int e = 0; e < 4; ++e) w[2 * k + (e >> 1)] |= quantize_pair(h[e], scale, recip2) << ((e & 1) * 16);
+            }
+            q8[i / 2] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+    const __half scale_h = __float2half_rn(scale);
+    q_scale = __half2float(scale_h);                    // dequantization uses the stored fp16 scale
+    #pragma unroll
+    for (int i = 0; i < kChunks; i += 2) {
+        const int cj = (part * kChunks + i) >> 1;       // int8 16-byte chunk (16 columns)
+        *reinterpret_cast<uint4*>(smem + L::kQ8 + r * 128 + ((cj ^ (r & 7)) << 4)) = q8[i / 2];
+    }
+    fence_proxy_async_smem();                           // generic-proxy writes -> tensor core reads
+    __syncwarp();
+    if (ok && lane == 0) mbar_arrive(q8_ready_bar);
+    if (ok && p.q8_out) {
+        const int row = qt * kTileRows + r;
+        if (row < p.M) {
+            std::int8_t* dst = p.q8_out + (static_cast<std::size_t>(head) * p.M + row) * p.d;
+            #pragma unroll
+            for (int i = 0; i < kChunks / 2; ++i) {
+                const int c0 = (part * kChunks + 2 * i) * 8;
+                if (p.q8_vec) {
+                    if (c0 < p.d) *reinterpret_cast<uint4*>(dst + c0) = q8[i];
+                } else {
+                    const uint8_t* b = reinterpret_cast<const uint8_t*>(&q8[i]);
+                    for (int e = 0; e < 16 && c0 + e < p.d; ++e) dst[c0 + e] = static_cast<std::int8_t>(b[e]);
+                }
+            }
+        }
+    }
+    if (ok && p.q_scales_out && t == 0) p.q_scales_out[static_cast<std::size_t>(head) * p.q_scale_blocks + qt] = scale_h;
+    return ok;
+}
+
 // Work item of CTA `bid`: heads are scheduled in groups (their K/V stay in
 // L2 while the group runs); inside a group the heaviest (last) query tiles go
 // first.
@@ -509,6 +639,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
     tile_of(p, static_cast<int>(blockIdx.x), head, qt);
     const int nblk = p.causal ? min(p.kv_blocks, qt + 1) : p.kv_blocks;
     const int load_i8 = p.routed;
+    const int load_q8 = p.routed && !p.fuse_q;    // fused Q: the CTA quantizes Q itself
 
     if (warp == 0) {
         // One barrier per lane (the set-up barrier waits for the slowest
@@ -520,7 +651,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             const bool stage_empty = (i >= kBarKEmpty && i < kBarKEmpty + kKStages) ||
                                      (i >= kBarVEmpty && i < kBarVEmpty + kVStages);
             const bool p_full = i >= kBarPFull && i < kBarPFull + 4;
-            mbar_init(bar(i), p_full ? kSoftmaxWarps / 2 + 4 : stage_empty ? 2 : 1);
+            mbar_init(bar(i), p_full ? kSoftmaxWarps / 2 + 4 : stage_empty ? 2 : i == kBarQ8Ready ? kSoftmaxWarps : 1);
         }
         if (lane == 0) *abort_ptr = 0;
         mbar_init_fence();
@@ -539,7 +670,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             int head2, qt2;
             tile_of(p, ahead, head2, qt2);
             for (int a = 0; a < kAtoms; ++a) tma_prefetch_l2_3d(&tm_q, a * 64, qt2 * kTileRows, head2);
-            if (load_i8) tma_prefetch_l2_3d(&tm_q8, 0, qt2 * kTileRows, head2);
+            if (load_q8) tma_prefetch_l2_3d(&tm_q8, 0, qt2 * kTileRows, head2);
         }
     }
     for (int i = threadIdx.x; i < 2 * kSoftmaxThreads; i += kAttnThreads) {
@@ -569,21 +700,22 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         // ------------------------------------------------------------ producer
         if (kUseTma && lane == 0) {
             tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_k); tma_prefetch_desc(&tm_v);
-            if (load_i8) { tma_prefetch_desc(&tm_q8); tma_prefetch_desc(&tm_k8); }
+            if (load_q8) tma_prefetch_desc(&tm_q8);
+            if (load_i8) tma_prefetch_desc(&tm_k8);
         }
         const std::size_t q_off = static_cast<std::size_t>(head) * p.M * p.d;
         const std::size_t kv_off = static_cast<std::size_t>(head) * p.N * p.d;
         if (kUseTma) {
             if (elect_one()) {
-                mbar_arrive_expect_tx(bar(kBarQFull), L::kTileF16 + (load_i8 ? kAtomBytes : 0u));
+                mbar_arrive_expect_tx(bar(kBarQFull), L::kTileF16 + (load_q8 ? kAtomBytes : 0u));
                 for (int a = 0; a < kAtoms; ++a) {
                     tma_load_3d(sbase + L::kQ + a * kAtomBytes, &tm_q, bar(kBarQFull), a * 64, qt * kTileRows, head);
                 }
-                if (load_i8) tma_load_3d(sbase + L::kQ8, &tm_q8, bar(kBarQFull), 0, qt * kTileRows, head);
+                if (load_q8) tma_load_3d(sbase + L::kQ8, &tm_q8, bar(kBarQFull), 0, qt * kTileRows, head);
             }
         } else {
             manual_tile_f16(smem + L::kQ, p.q + q_off, qt * kTileRows, p.M, p.d, kAtoms, lane);
-            if (load_i8) manual_tile_i8(smem + L::kQ8, p.q8 + q_off, qt * kTileRows, p.M, p.d, lane);
+            if (load_q8) manual_tile_i8(smem + L::kQ8, p.q8 + q_off, qt * kTileRows, p.M, p.d, lane);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarQFull));
@@ -697,6 +829,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         const bool i8_full = p.i8_ksteps == 4;
         const uint32_t none[4] = {0u, 0u, 0u, 0u};
         bool ok = wait_bar(bar(kBarQFull), 0, abort_flag, kStatusMma);
+        if (ok && p.fuse_q && p.routed) ok = wait_bar(bar(kBarQ8Ready), 0, abort_flag, kStatusMma);
         // One precision over key tiles [kt0, kt0 + nkt) of block j; `off` masks
         // the TMEM lanes (16-row tiles) that keep their previous result.
         // Start addresses advance by byte offset >> 4: 32 B per K step inside
@@ -839,7 +972,15 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         const bool row_valid = q_row < p.M;
         const int q16 = qt * (kTileRows / 16) + row / 16;
         const bool q16_valid = q16 < p.q16_tiles;
-        const float q_scale = p.routed ? __half2float(p.q_scales[head * p.q_scale_blocks + qt]) : 0.0f;
+        float q_scale = 0.0f;
+        bool ok = true;
+        if (p.routed) {
+            if (p.fuse_q) {
+                ok = quantize_q_tile<kAtoms>(p, smem, bar(kBarQFull), bar(kBarQ8Ready), head, qt, abort_flag, q_scale);
+            } else {
+                q_scale = __half2float(p.q_scales[head * p.q_scale_blocks + qt]);
+            }
+        }
         // Scores are kept in "raw" units r with score_log2 = r * c_exp: FP16
         // tiles give r = q.k directly when score_scale > 0 (no multiply); INT8
         // tiles give r = dot * q_scale * k_scale.
@@ -851,7 +992,6 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         const int qlocal = row / 16;
         float m_run = -INFINITY;    // running max (raw units), possibly stale by < 2^15 in p
         float l_run = 0.0f;         // this half's share of the row sum
-        bool ok = true;
         const uint32_t o_addr = tmem + lane_base + kColO + 128u * half;     // O_h
         float* alpha_slots = reinterpret_cast<float*>(smem + L::kAlpha);
         volatile std::uint64_t* xchg = reinterpret_cast<volatile std::uint64_t*>(smem + L::kXchg);
@@ -869,7 +1009,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             const uint32_t sc = half ? sl.scales >> 16 : sl.scales & 0xffffu;
             n_ratio = q_scale * __half2float(__ushort_as_half(static_cast<unsigned short>(sc))) * a_f16;
         };
-        if (nblk > 0) {
+        if (ok && nblk > 0) {
             ok = wait_bar(bar(kBarRoute), 0, abort_flag, kStatusSoftmax);
             if (ok) decode(0);
         }
@@ -1313,6 +1453,10 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     p.scale_log2 = prob.score_scale * kLog2e;
     p.causal = prob.causal ? 1 : 0;
     p.routed = prob.words != nullptr ? 1 : 0;
+    p.fuse_q = prob.fuse_q ? 1 : 0;
+    p.q8_out = prob.q8_out;
+    p.q_scales_out = prob.q_scales_out;
+    p.q8_vec = (prob.d % 16 == 0 && aligned16(prob.q8_out)) ? 1 : 0;
     p.f16_ksteps = (prob.d + 15) / 16;
     p.i8_ksteps = (prob.d + 31) / 32;
     p.pv_n = (prob.d + 15) / 16 * 16;
@@ -1342,15 +1486,18 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
 
     CUtensorMap maps[6];
     std::memset(maps, 0, sizeof(maps));
+    const bool q8_in = p.routed && !p.fuse_q;
     bool tma = prob.d % 16 == 0 && aligned16(prob.q) && aligned16(prob.k) && aligned16(prob.v) &&
-               (!p.routed || (aligned16(prob.q8) && aligned16(prob.k8)));
+               (!p.routed || (aligned16(prob.k8) && (!q8_in || aligned16(prob.q8))));
     if (tma) {
         tma = encode_map(&maps[0], prob.q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.heads, p.M, p.d, 64) &&
               encode_map(&maps[1], prob.k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.heads, p.N, p.d, 64) &&
               encode_map(&maps[2], prob.v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, p.heads, p.N, p.d, 64);
+        if (tma && q8_in) {
+            tma = encode_map(&maps[3], prob.q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.heads, p.M, p.d, 128);
+        }
         if (tma && p.routed) {
-            tma = encode_map(&maps[3], prob.q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.heads, p.M, p.d, 128) &&
-                  encode_map(&maps[4], prob.k8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.heads, p.N, p.d, 128);
+            tma = encode_map(&maps[4], prob.k8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.heads, p.N, p.d, 128);
         }
     }
     // fp32 O by TMA stores of 32 x 32 boxes (128-byte rows, swizzled)

@@ -48,7 +48,17 @@ struct AttentionProblem {
     // watchdog_limit_ns (the output is not valid; the status word is).
     bool watchdog_test;
     unsigned long long watchdog_limit_ns;
+    // Fused Q quantization (routed only): q8 and q_scales are not read; each
+    // CTA quantizes its own query tile, and writes the bytes to q8_out /
+    // q_scales_out when those are set.
+    bool fuse_q;
+    std::int8_t* q8_out;
+    __half* q_scales_out;
 };
+
+// Quantize K [heads, N, d] alone (64-row blocks), for the fused-Q path.
+cudaError_t launch_quantize_k(const __half* K, std::int8_t* K8, __half* k_scales, int heads, int N, int d,
+                              cudaStream_t stream);
 
 // Shared memory the attention kernel requests for head dim d.
 std::size_t attention_smem_bytes(int d);

@@ -12,11 +12,13 @@
 // B200 design: the block is read from HBM once. Each CTA owns one block
 // (<= 128 x 128 fp16 = 32 KB), its 256 threads hold the block in registers
 // (up to 8 x 16-byte loads each), reduce the absmax with warp shuffles, then
-// quantize from registers (a reciprocal multiply, with the exact division kept
-// for near-ties) and write 8-byte stores: 3 bytes of HBM traffic per element,
-// the algorithmic minimum. Unaligned pointers or d % 8 != 0 take a
+// quantize from registers with the branch-free exact rounding of
+// quant_math.cuh (blocks holding NaN or inf keep the element-wise exact
+// path) and write 8-byte stores: 3 bytes of HBM traffic per element, the
+// algorithmic minimum. Unaligned pointers or d % 8 != 0 take a
 // scalar two-pass path (the second pass hits L2).
 #include "kernels.cuh"
+#include "quant_math.cuh"
 
 #include <cstdint>
 
@@ -26,55 +28,24 @@ namespace {
 constexpr int kQuantThreads = 256;
 constexpr int kMaxChunksPerThread = 8;   // 128 rows x 128 d / 8 halves / 256 threads
 
-// Reference rounding: fl(x / scale) by a correctly rounded division, then
-// round half away from zero. Exact shortcut: the answer depends on the
-// quotient only through trunc(fl(|q| + 0.5)), which changes only where |q| + 0.5
-// crosses an integer. With y = fl(|x| * fl(1/scale)), |y - fl(|x| / scale)| <
-// 2^-15 for |q| <= 128 (two roundings of 2^-24 relative each, plus the
-// quotient's own), and fl(v + 0.5) moves v by at most 2^-17 there; so when
-// y + 0.5 is more than 2^-14 away from an integer both give the same integer.
-// Anything closer (ties, near-ties), and NaN / inf / zero scales, takes the
-// exact division.
-__device__ __forceinline__ std::int8_t quantize_exact(float x, float scale) {
-    const float normalized = scale > 0.0f ? __fdiv_rn(x, scale) : 0.0f;
-    const int rounded = __float2int_rz(__fadd_rn(normalized, copysignf(0.5f, normalized)));
-    return static_cast<std::int8_t>(max(-127, min(127, rounded)));
-}
+// NaN-propagating max of two floats (a NaN anywhere in a block must reach
+// the block's verdict, unlike fmaxf).
+__device__ __forceinline__ float max_nan(float a, float b) { return (a != a || b != b) ? NAN : fmaxf(a, b); }
 
-__device__ __forceinline__ std::int8_t quantize_one(float x, float scale, float recip) {
-    const float t = __fadd_rn(__fmul_rn(fabsf(x), recip), 0.5f);
-    const float whole = truncf(t);
-    const float frac = t - whole;                         // exact: t and whole share the exponent range
-    if (frac > 0x1p-14f && frac < 1.0f - 0x1p-14f) {      // false for NaN
-        const int mag = min(127, __float2int_rz(whole));
-        return static_cast<std::int8_t>(x < 0.0f ? -mag : mag);
-    }
-    return quantize_exact(x, scale);
-}
-
-// quantize_one for the two elements of a half2, the multiply and the adds on
-// packed f32x2 (one instruction per pair, same roundings). Returns the two
-// signed bytes in bits [0, 16).
-__device__ __forceinline__ uint32_t quantize_pair(__half2 h, float scale, float2 recip2) {
-    const float2 x = __half22float2(h);
-    const float2 t = __fadd2_rn(__fmul2_rn(make_float2(fabsf(x.x), fabsf(x.y)), recip2), make_float2(0.5f, 0.5f));
-    const float2 whole = make_float2(truncf(t.x), truncf(t.y));
-    const float2 frac = __ffma2_rn(whole, make_float2(-1.0f, -1.0f), t);   // exact
-    uint32_t out = 0u;
+// Block absmax from per-thread maxima, NaN-propagating (values are exact fp16
+// magnitudes, so the float reduction is exact).
+__device__ __forceinline__ float block_max_nan(float value, float* scratch) {
     #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const float f = k ? frac.y : frac.x;
-        const float xv = k ? x.y : x.x;
-        std::int8_t q;
-        if (f > 0x1p-14f && f < 1.0f - 0x1p-14f) {        // false for NaN
-            const int mag = min(127, __float2int_rz(k ? whole.y : whole.x));
-            q = static_cast<std::int8_t>(xv < 0.0f ? -mag : mag);
-        } else {
-            q = quantize_exact(xv, scale);
-        }
-        out |= static_cast<uint32_t>(static_cast<uint8_t>(q)) << (8 * k);
+    for (int offset = 16; offset > 0; offset >>= 1) {
+        value = max_nan(value, __shfl_xor_sync(0xffffffffu, value, offset));
     }
-    return out;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) scratch[warp] = value;
+    __syncthreads();
+    float total = 0.0f;
+    #pragma unroll
+    for (int w = 0; w < kQuantThreads / 32; ++w) total = max_nan(total, scratch[w]);
+    return total;
 }
 
 __device__ __forceinline__ float block_max(float value, float* scratch) {
@@ -101,7 +72,7 @@ struct QuantTensor {
     bool vector_ok;  // 16-byte aligned input, 8-byte aligned output, d % 8 == 0
 };
 
-__global__ void __launch_bounds__(kQuantThreads, 5)
+__global__ void __launch_bounds__(kQuantThreads, 4)
 quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
     __shared__ float scratch[kQuantThreads / 32];
     const int q_ctas = heads * qt.blocks;
@@ -119,8 +90,8 @@ quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
     if (t.vector_ok) {
         uint4 chunk[kMaxChunksPerThread];
         const int chunks = count >> 3;
-        // absmax on packed halves: |x| and max are exact in fp16, and __hmax2
-        // ignores a NaN input like fmaxf
+        // absmax on packed halves (|x| and max are exact in fp16), NaN-
+        // propagating so that a block holding a NaN takes the exact path
         __half2 m2 = __float2half2_rn(0.0f);
         #pragma unroll
         for (int i = 0; i < kMaxChunksPerThread; ++i) {
@@ -129,9 +100,39 @@ quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
                 chunk[i] = __ldg(reinterpret_cast<const uint4*>(src) + c);
                 const __half2* h = reinterpret_cast<const __half2*>(&chunk[i]);
                 #pragma unroll
-                for (int e = 0; e < 4; ++e) m2 = __hmax2(m2, __habs2(h[e]));
+                for (int e = 0; e < 4; ++e) m2 = __hmax2_nan(m2, __habs2(h[e]));
             }
         }
+        const float absmax = block_max_nan(max_nan(__low2float(m2), __high2float(m2)), scratch);
+        if (fast_block(absmax)) {
+            // every block of finite, not-all-zero inputs: branch-free exact rounding
+            const float scale = __fdiv_rn(absmax, 127.0f);
+            const float y = __frcp_rn(scale);
+            const float2 neg_s2 = make_float2(-scale, -scale), y2 = make_float2(y, y);
+            if (threadIdx.x == 0) t.scales[static_cast<std::size_t>(head) * t.blocks + block] = __float2half_rn(scale);
+            #pragma unroll
+            for (int i = 0; i < kMaxChunksPerThread; ++i) {
+                const int c = threadIdx.x + i * kQuantThreads;
+                if (c < chunks) {
+                    reinterpret_cast<uint2*>(dst)[c] = make_uint2(quantize4_fast(chunk[i].x, chunk[i].y, neg_s2, y2),
+                                                                  quantize4_fast(chunk[i].z, chunk[i].w, neg_s2, y2));
+                }
+            }
+            return;
+        }
+        // NaN, +-inf or an all-zero block (uniform over the block): the
+        // absmax without NaN, then the element-wise exact rounding
+        m2 = __float2half2_rn(0.0f);
+        #pragma unroll
+        for (int i = 0; i < kMaxChunksPerThread; ++i) {
+            const int c = threadIdx.x + i * kQuantThreads;
+            if (c < chunks) {
+                const __half2* h = reinterpret_cast<const __half2*>(&chunk[i]);
+                #pragma unroll
+                for (int e = 0; e < 4; ++e) m2 = __hmax2(m2, __habs2(h[e]));   // ignores a NaN like fmaxf
+            }
+        }
+        __syncthreads();   // every thread has read the first reduction's scratch
         const float local = fmaxf(__low2float(m2), __high2float(m2));
         const float scale = __fdiv_rn(block_max(local, scratch), 127.0f);
         const float recip = scale > 0.0f ? __frcp_rn(scale) : 0.0f;
@@ -177,6 +178,17 @@ cudaError_t launch_quantize(const __half* Q, const __half* K, std::int8_t* Q8, s
     const long long ctas = static_cast<long long>(heads) * (qt.blocks + kt.blocks);
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     quantize_blocks_kernel<<<static_cast<unsigned>(ctas), kQuantThreads, 0, stream>>>(qt, kt, heads, d);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_k(const __half* K, std::int8_t* K8, __half* k_scales, int heads, int N, int d,
+                              cudaStream_t stream) {
+    QuantTensor none{nullptr, nullptr, nullptr, 0, kQuantQRows, 0, false};   // no Q blocks
+    QuantTensor kt{K, K8, k_scales, N, kQuantKRows, (N - 1) / kQuantKRows + 1,
+                   d % 8 == 0 && aligned(K, 16) && aligned(K8, 8)};
+    const long long ctas = static_cast<long long>(heads) * kt.blocks;
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    quantize_blocks_kernel<<<static_cast<unsigned>(ctas), kQuantThreads, 0, stream>>>(none, kt, heads, d);
     return cudaGetLastError();
 }
 

@@ -90,6 +90,11 @@ def _load():
     lib.tilemix_attention_routed_noalloc.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I,
                                                      ctypes.POINTER(_Routing), _P]
     lib.tilemix_attention_routed_noalloc.restype = _I
+    lib.tilemix_quantize_k_batched.argtypes = [_P, _P, _P, _I, _I, _I, _P]
+    lib.tilemix_quantize_k_batched.restype = _I
+    lib.tilemix_attention_batched_qfused.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P,
+                                                     ctypes.POINTER(_Routing), _P, _P, _P, _P]
+    lib.tilemix_attention_batched_qfused.restype = _I
     lib.tilemix_watchdog_selftest.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, ctypes.c_uint, _P]
     lib.tilemix_watchdog_selftest.restype = _I
     lib.tilemix_read_and_clear_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
@@ -121,6 +126,7 @@ C_ABI_SYMBOLS = (
     "tilemix_abi_version", "tilemix_quantize_qk", "tilemix_fused_attention",
     "tilemix_quantize_qk_batched", "tilemix_attention_batched", "tilemix_attention_batched_out",
     "tilemix_attention_from_host", "tilemix_attention_routed_noalloc",
+    "tilemix_quantize_k_batched", "tilemix_attention_batched_qfused",
     "tilemix_routing_word_count_c", "tilemix_routing_words_per_row_c",
     "tilemix_reference_shared_bytes", "tilemix_b200_shared_bytes_c",
     "tilemix_read_and_clear_status", "tilemix_watchdog_selftest",
@@ -222,6 +228,24 @@ def tilemix_attention_batched(Q, K, V, O, heads: int, M: int, N: int, d: int,
     return _native().tilemix_attention_batched(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
                                                float(score_scale), int(bool(causal)), _stream(stream),
                                                ctypes.byref(r), ctypes.byref(q))
+
+
+def quantize_tilemix_k_batched(K, K8, k_scales, heads: int, N: int, d: int, stream=None) -> int:
+    """K alone in 64-row blocks (the K half of quantize_tilemix_qk_batched)."""
+    return _native().tilemix_quantize_k_batched(_addr(K), _addr(K8), _addr(k_scales), heads, N, d, _stream(stream))
+
+
+def tilemix_attention_batched_qfused(Q, K, V, O, heads: int, M: int, N: int, d: int, score_scale: float,
+                                     causal: bool = False, stream=None, routing: TileMixRouting | None = None,
+                                     K8=None, k_scales=None, Q8_out=None, q_scales_out=None) -> int:
+    """Routed attention with Q quantized inside the attention kernel (one HBM
+    pass over Q fewer). Routing words, K8 and k_scales are required; Q8_out /
+    q_scales_out optionally receive the bytes the standalone quantizer makes."""
+    r = (routing or TileMixRouting())._c()
+    return _native().tilemix_attention_batched_qfused(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
+                                                      float(score_scale), int(bool(causal)), _stream(stream),
+                                                      ctypes.byref(r), _addr(K8), _addr(k_scales), _addr(Q8_out),
+                                                      _addr(q_scales_out))
 
 
 kTileMixOutF32, kTileMixOutF16, kTileMixOutBF16 = 0, 1, 2
