@@ -50,6 +50,11 @@ def parse_args():
     ap.add_argument("--p", type=float, default=None, help="override the INT8 routing fraction")
     ap.add_argument("--cpu-seconds", type=float, default=6.0,
                     help="target CPU time of one reference-arm sample")
+    ap.add_argument("--routing", default="mask", choices=["mask", "policy"],
+                    help="mask: the config's Bernoulli 64x64 routing mask; policy: routing words chosen on the "
+                         "device from the quantizer's block scales each step (tilemix_routing_policy)")
+    ap.add_argument("--tau", type=float, default=1.0,
+                    help="policy: bound on the INT8 score error (score units) that a tile may incur")
     ap.add_argument("--scaling", default="strong", choices=["weak", "strong"],
                     help="strong (default): the batch's heads are split over ranks; weak: every rank runs a full batch")
     return ap.parse_args()
@@ -220,8 +225,10 @@ def config_block(args, world: int) -> dict:
     """The `config` object of the JSON line; both arms print it identically."""
     from tilemix_b200 import workloads
     cfg = workloads.config(args.config, p=args.p)
+    routing = (f"INT8 routing by the device policy (tau={args.tau})" if args.routing == "policy"
+               else f"INT8 routing p={cfg['p']}")
     label = (f"{args.config}: B{cfg['B']} H{cfg['H']} S{cfg['S']} D{cfg['D']}"
-             f"{' causal' if cfg['causal'] else ''}, INT8 routing p={cfg['p']}"
+             f"{' causal' if cfg['causal'] else ''}, {routing}"
              f"{', x20 outlier channels' if cfg['outliers'] else ''}")
     split = ("heads split into contiguous per-rank shards" if args.scaling == "strong"
              else "every rank runs its own full batch")
@@ -324,8 +331,13 @@ def run_tilemix(args, rank, world, local):
     f_eff = workloads.effective_flops(cfg, H)       # this rank's work per step
     f_real = workloads.realised_int8_fraction(w["mask"], cfg["causal"])
 
+    policy = args.routing == "policy"
+    max_product = tm.tilemix_policy_max_scale_product(args.tau, w["score_scale"], D) if policy else None
+
     def quantize():
         tm.check(tm.quantize_tilemix_qk_batched(q, k, q8, k8, qs, ks, H, S, S, D, stream), "quantize")
+        if policy:   # routing words from this step's block scales, on the device
+            tm.check(tm.tilemix_routing_policy(qs, ks, words, H, S, S, 2, max_product, stream), "routing policy")
 
     def attend():
         tm.check(tm.tilemix_attention_batched(q, k, v, out, H, S, S, D, w["score_scale"], cfg["causal"],
@@ -361,6 +373,8 @@ def run_tilemix(args, rank, world, local):
     tm.check(err, "status")
     if status:
         raise SystemExit(f"kernel watchdog reported status {status:#x}")
+    if policy:
+        f_real = workloads.int8_fraction_from_words(words.cpu().numpy(), H, S, cfg["causal"])
     step_ms = reduce_max(total_ms / n, world)
     attn_avg = reduce_max(sum(attn_ms) / n, world)
     quant_avg = reduce_max(sum(quant_ms) / n, world)
@@ -370,7 +384,7 @@ def run_tilemix(args, rank, world, local):
     # routing words, both kernels, D2H of the fp32 output, pipelined over
     # chunks of heads inside the library).
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    hwords = w["words"].pin_memory()
+    hwords = (words.cpu() if policy else w["words"]).pin_memory()   # the words the timed steps used
     hout = torch.empty((H, S, D), dtype=torch.float32).pin_memory()
     bufs = tm.TileMixDeviceBuffers(q=q, k=k, v=v, q8=q8, k8=k8, q_scales=qs, k_scales=ks, words=words, o=out)
     e2e_steps = max(1, min(n, 5))
@@ -447,7 +461,10 @@ def run_tilemix(args, rank, world, local):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
                 "api": "tilemix_attention_from_host (C-ABI, pinned host buffers, pipelined over head chunks)"},
         "clocks": clk,
-        "gpu_launches": 2 * n,
+        "gpu_launches": (3 if policy else 2) * n,
+        "routing": ({"kind": "policy", "tau": args.tau, "max_scale_product": max_product,
+                     "note": "INT8 iff q_scale * max k_scale <= max_scale_product (tilemix_routing_policy, every step)"}
+                    if policy else {"kind": "mask", "note": "the config's Bernoulli 64x64 INT8 mask"}),
         "repo_native_so": repo_libraries(),
     }
     if cpu is not None:

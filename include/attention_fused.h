@@ -144,6 +144,28 @@ cudaError_t tilemix_attention_batched_qfused(const __half* Q, const __half* K, c
                                              const std::int8_t* K8, const __half* k_scales,
                                              std::int8_t* Q8_out = nullptr, __half* q_scales_out = nullptr);
 
+// Device-side routing policy (no reference counterpart: the reference takes
+// the mask from the caller, src/main.cu:48). Fills `words` (heads *
+// tilemix_routing_word_count(M, N, key_tiles_per_group) words, the reference's
+// mask format) from the quantizer's block scales: a (16-row query tile, key
+// group) pair is INT8 iff q_scale * (max k_scale over the group's 64-row K
+// blocks) <= max_scale_product, as an fp32 product; FP16 otherwise (and for
+// NaN scales). Since every quantized element is within s / 2 of its value and
+// |x| <= 127 s, the INT8 score then differs from the fp32 one by at most
+// |score_scale| * d * 127.25 * q_scale * k_scale: choose max_scale_product =
+// tolerance / (|score_scale| * d * 127.25) (tilemix_policy_max_scale_product)
+// to bound that error by `tolerance`. Outlier blocks (large absmax, coarse
+// INT8 steps) therefore stay FP16.
+cudaError_t tilemix_routing_policy(const __half* q_scales, const __half* k_scales, std::uint64_t* words,
+                                   int heads, int M, int N, int key_tiles_per_group,
+                                   float max_scale_product, cudaStream_t stream = nullptr);
+
+inline float tilemix_policy_max_scale_product(float tolerance, float score_scale, int d) {
+    const double denom = (score_scale < 0 ? -static_cast<double>(score_scale) : static_cast<double>(score_scale)) *
+                         static_cast<double>(d) * 127.25;
+    return denom > 0 ? static_cast<float>(static_cast<double>(tolerance) / denom) : 3.4028234663852886e38f;
+}
+
 // Output element types of TileMixOutput.
 enum TileMixOutputType : int { kTileMixOutF32 = 0, kTileMixOutF16 = 1, kTileMixOutBF16 = 2 };
 

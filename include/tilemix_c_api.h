@@ -170,6 +170,17 @@ int tilemix_attention_routed_noalloc(const void* Q, const void* K, const void* V
                                      int heads, int M, int N, int d, float score_scale, int causal,
                                      const tilemix_routing* routing, void* stream);
 
+/* Device-side routing policy (no reference counterpart; the reference takes
+ * the mask from the caller, src/main.cu:48): C form of tilemix_routing_policy
+ * in attention_fused.h. words: heads * tilemix_routing_word_count_c(M, N, g)
+ * words; bit = 1 (INT8) iff q_scale * max k_scale of the key group <=
+ * max_scale_product. tilemix_policy_max_scale_product_c(tol, score_scale, d)
+ * gives the product that bounds the INT8 score error by tol. */
+int tilemix_routing_policy_c(const void* q_scales, const void* k_scales, uint64_t* words, int heads,
+                             int M, int N, int key_tiles_per_group, float max_scale_product,
+                             void* stream);
+float tilemix_policy_max_scale_product_c(float tolerance, float score_scale, int d);
+
 /* Sizing helpers (reference include/attention_fused.h:34-45). */
 size_t tilemix_routing_word_count_c(int M, int N, int key_tiles_per_group);
 size_t tilemix_routing_words_per_row_c(int N, int key_tiles_per_group);

@@ -91,6 +91,7 @@ def lib():
         _lib.orc_pack_block_mask64.argtypes = [_P, _I, _I, _P]
         _lib.orc_quantize_rows.argtypes = [_P, _I, _I, _I, _P, _P]
         _lib.orc_quantize_batched.argtypes = [_P, _I, _I, _I, _I, _P, _P]
+        _lib.orc_routing_policy.argtypes = [_P, _P, _I, _I, _I, _I, _F, _P]
         _lib.orc_tilemix_batched.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P,
                                              _I, _I, _I, _I, _F, _I, _P]
         _lib.orc_tilemix_sampled.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P,
@@ -289,6 +290,18 @@ def dense_attention(q, k, v) -> np.ndarray:
     m, d = q.shape
     out = np.empty((m, d), np.float64)
     lib().orc_dense_attention(_ptr(q), _ptr(k), _ptr(v), m, k.shape[0], d, _ptr(out))
+    return out
+
+
+def routing_policy(q_scales, k_scales, heads: int, m: int, n: int, key_tiles_per_group: int,
+                   max_product: float) -> np.ndarray:
+    """Routing words of the scale-product policy (orc_routing_policy): bit 1
+    (INT8) iff q_scale(tile) * max k_scale(group) <= max_product in fp32."""
+    qs = _u16(np.asarray(q_scales).reshape(heads, -1))
+    ks = _u16(np.asarray(k_scales).reshape(heads, -1))
+    out = np.empty(heads * routing_word_count(m, n, key_tiles_per_group), np.uint64)
+    lib().orc_routing_policy(_ptr(qs), _ptr(ks), heads, m, n, key_tiles_per_group, ctypes.c_float(max_product),
+                             _ptr(out))
     return out
 
 

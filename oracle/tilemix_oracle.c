@@ -324,3 +324,40 @@ void orc_set_threads(int n) {
     (void)n;
 #endif
 }
+
+/* Routing policy (see tilemix_oracle.h): a plain loop per word and bit. */
+void orc_routing_policy(const uint16_t* q_scales, const uint16_t* k_scales, int heads, int M, int N,
+                        int key_tiles_per_group, float max_product, uint64_t* words) {
+    const int q16_tiles = (M + 15) / 16, k32_tiles = (N + 31) / 32;
+    const long long groups = ((long long)k32_tiles + key_tiles_per_group - 1) / key_tiles_per_group;
+    const long long wpr = (groups + 63) / 64;
+    const int q_blocks = (M + 127) / 128, k_blocks = (N + 63) / 64;
+    for (int h = 0; h < heads; ++h) {
+        for (int t = 0; t < q16_tiles; ++t) {
+            const float sq = orc_half_to_float(q_scales[(size_t)h * q_blocks + t / 8]);
+            for (long long w = 0; w < wpr; ++w) {
+                uint64_t word = 0;
+                for (int b = 0; b < 64; ++b) {
+                    const long long g = w * 64 + b;
+                    if (g >= groups) break;
+                    const long long kt0 = g * key_tiles_per_group;
+                    long long kt1 = kt0 + key_tiles_per_group;
+                    if (kt1 > k32_tiles) kt1 = k32_tiles;
+                    const long long key0 = kt0 * 32;
+                    long long key1 = kt1 * 32;
+                    if (key1 > N) key1 = N;
+                    float skmax = 0.0f;
+                    int nan = 0;
+                    for (long long kb = key0 / 64; kb <= (key1 - 1) / 64; ++kb) {
+                        const float s = orc_half_to_float(k_scales[(size_t)h * k_blocks + kb]);
+                        if (s != s) nan = 1;
+                        else if (s > skmax) skmax = s;
+                    }
+                    const float product = sq * skmax;
+                    if (!nan && product <= max_product) word |= (uint64_t)1 << b;
+                }
+                words[((size_t)h * q16_tiles + t) * wpr + w] = word;
+            }
+        }
+    }
+}

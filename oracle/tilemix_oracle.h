@@ -100,6 +100,16 @@ int orc_max_threads(void);
 /* Thread count of the calling thread's later OpenMP regions (n > 0). */
 void orc_set_threads(int n);
 
+/* Device routing policy restated (the B200 library's tilemix_routing_policy;
+ * the reference has no policy and takes masks from the caller, src/main.cu:48):
+ * for each head, 16-row query tile q16 and group of key_tiles_per_group 32-key
+ * tiles, bit = 1 (INT8) iff fl32(q_scale[q16 / 8] * max k_scale over the
+ * 64-row K blocks the group's keys touch) <= max_product (a NaN scale gives
+ * 0). Words in the reference's mask format (src/tilemix.cu:99-103), bits past
+ * the last group 0; words has heads * ceil(M/16) * words_per_row entries. */
+void orc_routing_policy(const uint16_t* q_scales, const uint16_t* k_scales, int heads, int M, int N,
+                        int key_tiles_per_group, float max_product, uint64_t* words);
+
 #ifdef __cplusplus
 }
 #endif

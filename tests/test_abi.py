@@ -22,7 +22,7 @@ def declared_c_functions():
         if 'extern "C"' not in text:
             continue
         body = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-        names.update(re.findall(r"^\s*(?:int|size_t|void|unsigned int)\s+(tilemix_\w+)\s*\(", body, re.M))
+        names.update(re.findall(r"^\s*(?:int|size_t|void|unsigned int|float)\s+(tilemix_\w+)\s*\(", body, re.M))
     return sorted(names)
 
 

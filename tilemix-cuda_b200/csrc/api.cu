@@ -152,6 +152,21 @@ cudaError_t attention_qfused_impl(const __half* Q, const __half* K, const __half
     return tilemix::launch_attention(prob, stream);
 }
 
+cudaError_t routing_policy_impl(const __half* q_scales, const __half* k_scales, std::uint64_t* words, int heads,
+                                int M, int N, int key_tiles_per_group, float max_scale_product, cudaStream_t stream) {
+    if (!q_scales || !k_scales || !words || heads <= 0 || M <= 0 || N <= 0 || key_tiles_per_group <= 0 ||
+        std::isnan(max_scale_product)) {
+        return cudaErrorInvalidValue;
+    }
+    if (static_cast<long long>(heads) * tilemix_routing_word_count(M, N, key_tiles_per_group) > (1ll << 40)) {
+        return cudaErrorInvalidValue;
+    }
+    const cudaError_t status = check_device();
+    if (status != cudaSuccess) return status;
+    return tilemix::launch_routing_policy(q_scales, k_scales, words, heads, M, N, key_tiles_per_group,
+                                          max_scale_product, stream);
+}
+
 TileMixRouting to_cpp(const tilemix_routing* r) {
     TileMixRouting out{};
     if (r) {
@@ -383,6 +398,13 @@ cudaError_t tilemix_attention_batched_qfused(const __half* Q, const __half* K, c
                                  Q8_out, q_scales_out);
 }
 
+cudaError_t tilemix_routing_policy(const __half* q_scales, const __half* k_scales, std::uint64_t* words, int heads,
+                                   int M, int N, int key_tiles_per_group, float max_scale_product,
+                                   cudaStream_t stream) {
+    return routing_policy_impl(q_scales, k_scales, words, heads, M, N, key_tiles_per_group, max_scale_product,
+                               stream);
+}
+
 // ---------------------------------------------------------------------- C-ABI
 extern "C" {
 
@@ -462,6 +484,18 @@ int tilemix_attention_batched_qfused(const void* Q, const void* K, const void* V
         static_cast<const __half*>(Q), static_cast<const __half*>(K), static_cast<const __half*>(V), O, heads, M, N,
         d, score_scale, causal != 0, static_cast<cudaStream_t>(stream), to_cpp(routing), K8,
         static_cast<const __half*>(k_scales), Q8_out, static_cast<__half*>(q_scales_out)));
+}
+
+int tilemix_routing_policy_c(const void* q_scales, const void* k_scales, uint64_t* words, int heads, int M, int N,
+                             int key_tiles_per_group, float max_scale_product, void* stream) {
+    return static_cast<int>(routing_policy_impl(static_cast<const __half*>(q_scales),
+                                                static_cast<const __half*>(k_scales), words, heads, M, N,
+                                                key_tiles_per_group, max_scale_product,
+                                                static_cast<cudaStream_t>(stream)));
+}
+
+float tilemix_policy_max_scale_product_c(float tolerance, float score_scale, int d) {
+    return tilemix_policy_max_scale_product(tolerance, score_scale, d);
 }
 
 size_t tilemix_routing_word_count_c(int M, int N, int key_tiles_per_group) {

@@ -56,6 +56,12 @@ struct AttentionProblem {
     __half* q_scales_out;
 };
 
+// Routing words from the quantizer's block scales (policy.cu): INT8 iff
+// q_scale(tile) * max k_scale(group) <= max_scale_product.
+cudaError_t launch_routing_policy(const __half* q_scales, const __half* k_scales, std::uint64_t* words, int heads,
+                                  int M, int N, int key_tiles_per_group, float max_scale_product,
+                                  cudaStream_t stream);
+
 // Quantize K [heads, N, d] alone (64-row blocks), for the fused-Q path.
 cudaError_t launch_quantize_k(const __half* K, std::int8_t* K8, __half* k_scales, int heads, int N, int d,
                               cudaStream_t stream);

@@ -95,6 +95,10 @@ def _load():
     lib.tilemix_attention_batched_qfused.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P,
                                                      ctypes.POINTER(_Routing), _P, _P, _P, _P]
     lib.tilemix_attention_batched_qfused.restype = _I
+    lib.tilemix_routing_policy_c.argtypes = [_P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _P]
+    lib.tilemix_routing_policy_c.restype = _I
+    lib.tilemix_policy_max_scale_product_c.argtypes = [ctypes.c_float, ctypes.c_float, _I]
+    lib.tilemix_policy_max_scale_product_c.restype = ctypes.c_float
     lib.tilemix_watchdog_selftest.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, ctypes.c_uint, _P]
     lib.tilemix_watchdog_selftest.restype = _I
     lib.tilemix_read_and_clear_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
@@ -127,6 +131,7 @@ C_ABI_SYMBOLS = (
     "tilemix_quantize_qk_batched", "tilemix_attention_batched", "tilemix_attention_batched_out",
     "tilemix_attention_from_host", "tilemix_attention_routed_noalloc",
     "tilemix_quantize_k_batched", "tilemix_attention_batched_qfused",
+    "tilemix_routing_policy_c", "tilemix_policy_max_scale_product_c",
     "tilemix_routing_word_count_c", "tilemix_routing_words_per_row_c",
     "tilemix_reference_shared_bytes", "tilemix_b200_shared_bytes_c",
     "tilemix_read_and_clear_status", "tilemix_watchdog_selftest",
@@ -246,6 +251,20 @@ def tilemix_attention_batched_qfused(Q, K, V, O, heads: int, M: int, N: int, d: 
                                                       float(score_scale), int(bool(causal)), _stream(stream),
                                                       ctypes.byref(r), _addr(K8), _addr(k_scales), _addr(Q8_out),
                                                       _addr(q_scales_out))
+
+
+def tilemix_routing_policy(q_scales, k_scales, words, heads: int, M: int, N: int, key_tiles_per_group: int,
+                           max_scale_product: float, stream=None) -> int:
+    """Routing words from the quantizer's block scales: INT8 iff q_scale *
+    max k_scale of the key group <= max_scale_product (fp32), else FP16."""
+    return _native().tilemix_routing_policy_c(_addr(q_scales), _addr(k_scales), _addr(words), heads, M, N,
+                                              key_tiles_per_group, float(max_scale_product), _stream(stream))
+
+
+def tilemix_policy_max_scale_product(tolerance: float, score_scale: float, d: int) -> float:
+    """The product threshold that bounds the INT8 score error by `tolerance`:
+    tolerance / (|score_scale| * d * 127.25)."""
+    return float(_native().tilemix_policy_max_scale_product_c(float(tolerance), float(score_scale), int(d)))
 
 
 kTileMixOutF32, kTileMixOutF16, kTileMixOutBF16 = 0, 1, 2

@@ -96,6 +96,23 @@ def realised_int8_fraction(mask: torch.Tensor | np.ndarray, causal: bool) -> flo
     return float(m.mean())
 
 
+def int8_fraction_from_words(words: np.ndarray, heads: int, S: int, causal: bool,
+                             key_tiles_per_group: int = 2) -> float:
+    """INT8 share of the QK work a set of routing words selects: over the
+    (16-row query tile, 32-key tile) pairs the kernel computes (causal: key
+    tiles that start at or before the tile's last row)."""
+    q16, k32 = (S + 15) // 16, (S + 31) // 32
+    groups = (k32 + key_tiles_per_group - 1) // key_tiles_per_group
+    wpr = (groups + 63) // 64
+    w = np.ascontiguousarray(words, dtype=np.uint64).reshape(heads, q16, wpr)
+    bits = np.unpackbits(w.view(np.uint8), axis=-1, bitorder="little").reshape(heads, q16, wpr * 64)
+    tile_bits = np.repeat(bits[:, :, :groups], key_tiles_per_group, axis=-1)[:, :, :k32]
+    if causal:
+        keep = (np.arange(k32)[None, :] * 32) <= (np.arange(q16)[:, None] * 16 + 15)
+        return float(tile_bits[:, keep].mean())
+    return float(tile_bits.mean())
+
+
 def effective_flops(cfg: dict, heads: int | None = None) -> float:
     """F_eff = 4 * B*H * S^2 * D, halved for causal (flash-attention convention)."""
     bh = heads if heads is not None else cfg["B"] * cfg["H"]
