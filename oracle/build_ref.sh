@@ -8,6 +8,9 @@
 #                                        (src/tilemix.cu) for sm_100a, compiled
 #                                        where they lie, behind ref_gpu_shim.cu
 #                                        (bench.py's "reference GPU" column)
+#   oracle/_ref/tilemix_ref_demo       : the reference's OWN driver src/main.cu
+#                                        (with src/tilemix.cu), for comparing
+#                                        its printed output[0] with tilemix_demo
 # Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: $TILEMIX_REFERENCE_ROOT;
 # oracle/__init__.py passes the reference_path of BASELINE.json when unset)
 # The reference build is skipped, not failed, when the reference tree is absent.
@@ -31,6 +34,11 @@ if [[ -n "$ref_root" && -f "$ref_root/src/tests/reference_tilemix.h" ]]; then
             -I"$ref_root/include" "$ref_root/src/tilemix.cu" "$here/ref_gpu_shim.cu" \
             -o "$here/_ref/libtilemix_ref_gpu.so"
         echo "built $here/_ref/libtilemix_ref_gpu.so from $ref_root/src/tilemix.cu"
+        # the reference's own driver (src/main.cu), unmodified, for the
+        # output[0] comparison with tilemix_demo
+        nvcc -gencode arch=compute_100a,code=sm_100a -O2 -std=c++17 -I"$ref_root/include" \
+            "$ref_root/src/main.cu" "$ref_root/src/tilemix.cu" -o "$here/_ref/tilemix_ref_demo"
+        echo "built $here/_ref/tilemix_ref_demo from $ref_root/src/main.cu"
     fi
 else
     echo "reference tree not found at $ref_root; oracle/_ref not rebuilt"

@@ -112,3 +112,38 @@ def test_c5_routing_sweep_sampled(p):
     out, quant, _ = run_config(w)
     quant_host = check_quantized(w, quant)
     sampled_check(w, out, quant_host, np.array([0, 100, 511]), np.array([0, 63, 64, 700, 1500, 2047]))
+
+
+@pytest.mark.parametrize("name,p", [("c3", 0.75), ("c3", 0.5), ("c5", 0.5)])
+def test_benchmark_inputs_from_the_cuda_generator(name, p):
+    """bench.py draws its inputs with the CUDA generator (same distributions,
+    different numbers from the CPU one the other tests use); the same
+    quantize + attention pass on those exact inputs, checked against the
+    oracle: quantization bit-exact on the heads sampled, outputs on sampled
+    rows of those heads."""
+    w = workloads.make_inputs(name, p=p, device="cuda")
+    H, S, D, cfg = w["heads"], w["S"], w["D"], w["cfg"]
+    q8, k8, qs, ks = tm.quantize(w["q"], w["k"])
+    out = tm.attention(w["q"], w["k"], w["v"], q8=q8, k8=k8, q_scales=qs, k_scales=ks, words=w["words"].cuda(),
+                       key_tiles_per_group=2, score_scale=w["score_scale"], causal=cfg["causal"])
+    torch.cuda.synchronize()
+    err, status = tm.read_and_clear_status()
+    assert err == 0 and status == 0
+    heads = [0, H // 3, H - 1]
+    host = {x: w[x][heads].cpu().numpy() for x in ("q", "k", "v")}
+    q8h, k8h, qsh, ksh = (t[heads].cpu().numpy() for t in (q8, k8, qs, ks))
+    for i in range(len(heads)):
+        eq8, eqs = oracle.quantize(host["q"][i], 128)
+        ek8, eks = oracle.quantize(host["k"][i], 64)
+        assert np.array_equal(q8h[i], eq8) and np.array_equal(k8h[i], ek8)
+        assert np.array_equal(qsh[i].view(np.uint16), eqs.view(np.uint16))
+        assert np.array_equal(ksh[i].view(np.uint16), eks.view(np.uint16))
+    wc = w["words"].numel() // H
+    words = w["words"].numpy()
+    bits = np.stack([oracle.decode_routing(words[h * wc:(h + 1) * wc], S, S, 2) for h in heads])
+    rows = np.unique(np.concatenate([np.arange(0, S, 97), [S - 1]])).astype(np.int32)
+    expect = oracle.tilemix_sampled(host["q"], host["k"], host["v"], q8h, k8h, qsh, ksh, bits,
+                                    np.arange(len(heads), dtype=np.int32), rows, w["score_scale"], cfg["causal"])
+    actual = out[heads][:, rows].cpu().numpy()
+    max_abs, rel_l2 = compare_stats(actual, expect)
+    assert max_abs <= MAX_ABS_TOL and rel_l2 <= REL_L2_TOL, (max_abs, rel_l2)
