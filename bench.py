@@ -407,6 +407,24 @@ def run_tilemix(args, rank, world, local):
     h2d = 3 * q.numel() * 2 + words.numel() * 8
     d2h = out.numel() * 4
 
+    # Host-link bandwidth with every rank copying at once (what bounds the
+    # end-to-end leg): one pinned H2D copy of this rank's Q and one D2H copy
+    # of its fp32 O, each timed on the stream; the slowest rank counts.
+    def timed_copy(dst, src):
+        barrier(world)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        dst.copy_(src, non_blocking=True)
+        b.record(stream)
+        torch.cuda.synchronize()
+        return reduce_max(a.elapsed_time(b), world)
+    h2d_ms = timed_copy(q, hq)
+    d2h_ms = timed_copy(hout, out)
+    link = {"h2d_gbs_per_rank": round(q.numel() * 2 / (h2d_ms * 1e-3) / 1e9, 2),
+            "d2h_gbs_per_rank": round(out.numel() * 4 / (d2h_ms * 1e-3) / 1e9, 2),
+            "ranks_copying_at_once": world}
+
     cpu = None
     if rank == 0 and world == 1:
         nh = min(H, 32)
@@ -459,7 +477,8 @@ def run_tilemix(args, rank, world, local):
                      "work": "F_eff = 4*B*H*S^2*D/2 (causal) algorithmic FLOPs per launch"},
         "e2e": {"value": round(job_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
-                "api": "tilemix_attention_from_host (C-ABI, pinned host buffers, pipelined over head chunks)"},
+                "api": "tilemix_attention_from_host (C-ABI, pinned host buffers, pipelined over head chunks)",
+                "host_link": link},
         "clocks": clk,
         "gpu_launches": (3 if policy else 2) * n,
         "routing": ({"kind": "policy", "tau": args.tau, "max_scale_product": max_product,
