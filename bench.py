@@ -55,6 +55,9 @@ def parse_args():
                          "device from the quantizer's block scales each step (tilemix_routing_policy)")
     ap.add_argument("--tau", type=float, default=1.0,
                     help="policy: bound on the INT8 score error (score units) that a tile may incur")
+    ap.add_argument("--v-hint", action="store_true",
+                    help="quantize_tilemix_qkv_batched records max |v| per 64-key block and the attention takes "
+                         "single-term fp16 P where it is <= 3.5 (tilemix_attention_batched_hinted)")
     ap.add_argument("--scaling", default="strong", choices=["weak", "strong"],
                     help="strong (default): the batch's heads are split over ranks; weak: every rank runs a full batch")
     return ap.parse_args()
@@ -227,6 +230,8 @@ def config_block(args, world: int) -> dict:
     cfg = workloads.config(args.config, p=args.p)
     routing = (f"INT8 routing by the device policy (tau={args.tau})" if args.routing == "policy"
                else f"INT8 routing p={cfg['p']}")
+    if args.v_hint:
+        routing += ", single-term P where max|v| <= 3.5"
     label = (f"{args.config}: B{cfg['B']} H{cfg['H']} S{cfg['S']} D{cfg['D']}"
              f"{' causal' if cfg['causal'] else ''}, {routing}"
              f"{', x20 outlier channels' if cfg['outliers'] else ''}")
@@ -334,14 +339,23 @@ def run_tilemix(args, rank, world, local):
     policy = args.routing == "policy"
     max_product = tm.tilemix_policy_max_scale_product(args.tau, w["score_scale"], D) if policy else None
 
+    v_absmax = torch.empty((H, (S - 1) // 64 + 1), dtype=torch.float16, device="cuda") if args.v_hint else None
+
     def quantize():
-        tm.check(tm.quantize_tilemix_qk_batched(q, k, q8, k8, qs, ks, H, S, S, D, stream), "quantize")
+        if args.v_hint:
+            tm.check(tm.quantize_tilemix_qkv_batched(q, k, v, q8, k8, qs, ks, v_absmax, H, S, S, D, stream), "quantize")
+        else:
+            tm.check(tm.quantize_tilemix_qk_batched(q, k, q8, k8, qs, ks, H, S, S, D, stream), "quantize")
         if policy:   # routing words from this step's block scales, on the device
             tm.check(tm.tilemix_routing_policy(qs, ks, words, H, S, S, 2, max_product, stream), "routing policy")
 
     def attend():
-        tm.check(tm.tilemix_attention_batched(q, k, v, out, H, S, S, D, w["score_scale"], cfg["causal"],
-                                              stream, routing, quantized), "attention")
+        if args.v_hint:
+            tm.check(tm.tilemix_attention_batched_hinted(q, k, v, out, H, S, S, D, w["score_scale"], cfg["causal"],
+                                                         stream, routing, quantized, v_absmax), "attention")
+        else:
+            tm.check(tm.tilemix_attention_batched(q, k, v, out, H, S, S, D, w["score_scale"], cfg["causal"],
+                                                  stream, routing, quantized), "attention")
 
     for _ in range(args.warmup):
         quantize(); attend()
@@ -375,6 +389,7 @@ def run_tilemix(args, rank, world, local):
         raise SystemExit(f"kernel watchdog reported status {status:#x}")
     if policy:
         f_real = workloads.int8_fraction_from_words(words.cpu().numpy(), H, S, cfg["causal"])
+    single_share = (float((v_absmax.float() <= 3.5).float().mean()) if args.v_hint else 0.0)
     step_ms = reduce_max(total_ms / n, world)
     attn_avg = reduce_max(sum(attn_ms) / n, world)
     quant_avg = reduce_max(sum(quant_ms) / n, world)
@@ -481,6 +496,7 @@ def run_tilemix(args, rank, world, local):
                 "host_link": link},
         "clocks": clk,
         "gpu_launches": (3 if policy else 2) * n,
+        "pv_single_term_share": round(single_share, 4),
         "routing": ({"kind": "policy", "tau": args.tau, "max_scale_product": max_product,
                      "note": "INT8 iff q_scale * max k_scale <= max_scale_product (tilemix_routing_policy, every step)"}
                     if policy else {"kind": "mask", "note": "the config's Bernoulli 64x64 INT8 mask"}),

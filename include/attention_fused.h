@@ -144,6 +144,30 @@ cudaError_t tilemix_attention_batched_qfused(const __half* Q, const __half* K, c
                                              const std::int8_t* K8, const __half* k_scales,
                                              std::int8_t* Q8_out = nullptr, __half* q_scales_out = nullptr);
 
+// Precision hints for PV (no reference counterpart; the reference keeps P in
+// fp32, src/tilemix.cu:195-210). quantize_tilemix_qkv_batched quantizes Q and
+// K exactly as quantize_tilemix_qk_batched and, in the same launch, records
+// max |v| of every 64-row block of V in v_absmax [heads][ceil(N/64)] (fp16,
+// exact; NaN when the block holds a NaN).
+cudaError_t quantize_tilemix_qkv_batched(const __half* Q, const __half* K, const __half* V,
+                                         std::int8_t* Q8, std::int8_t* K8, __half* q_scales,
+                                         __half* k_scales, __half* v_absmax, int heads, int M, int N,
+                                         int d, cudaStream_t stream = nullptr);
+
+// tilemix_attention_batched using those statistics: the PV product of a
+// 64-key half-block whose max |v| is <= 3.5 uses P rounded once to fp16 (one
+// MMA per K step) instead of the two-term hi + lo split. fp16 rounding moves
+// each p by at most 2^-11 p and O = sum p v / sum p, so such a half adds at
+// most 2^-11 * 3.5 = 1.7e-3 to any output element, within the 2e-3 parity
+// bar; halves with larger |v| keep the two-term P. v_absmax may be null (every
+// half two-term, identical to tilemix_attention_batched).
+cudaError_t tilemix_attention_batched_hinted(const __half* Q, const __half* K, const __half* V,
+                                             float* O, int heads, int M, int N, int d,
+                                             float score_scale, bool causal, cudaStream_t stream,
+                                             const TileMixRouting& routing,
+                                             const TileMixQuantized& quantized,
+                                             const __half* v_absmax);
+
 // Device-side routing policy (no reference counterpart: the reference takes
 // the mask from the caller, src/main.cu:48). Fills `words` (heads *
 // tilemix_routing_word_count(M, N, key_tiles_per_group) words, the reference's

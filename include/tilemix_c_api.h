@@ -170,6 +170,19 @@ int tilemix_attention_routed_noalloc(const void* Q, const void* K, const void* V
                                      int heads, int M, int N, int d, float score_scale, int causal,
                                      const tilemix_routing* routing, void* stream);
 
+/* Precision hints for PV (no reference counterpart): C forms of
+ * quantize_tilemix_qkv_batched (Q/K quantization plus max |v| per 64-row V
+ * block, fp16 [heads][ceil(N/64)]) and tilemix_attention_batched_hinted
+ * (key halves with max |v| <= 3.5 take single-term fp16 P: at most 1.7e-3
+ * added to any output; v_absmax NULL = tilemix_attention_batched). */
+int tilemix_quantize_qkv_batched(const void* Q, const void* K, const void* V, int8_t* Q8, int8_t* K8,
+                                 void* q_scales, void* k_scales, void* v_absmax, int heads, int M, int N,
+                                 int d, void* stream);
+int tilemix_attention_batched_hinted(const void* Q, const void* K, const void* V, float* O, int heads,
+                                     int M, int N, int d, float score_scale, int causal, void* stream,
+                                     const tilemix_routing* routing, const tilemix_quantized* quantized,
+                                     const void* v_absmax);
+
 /* Device-side routing policy (no reference counterpart; the reference takes
  * the mask from the caller, src/main.cu:48): C form of tilemix_routing_policy
  * in attention_fused.h. words: heads * tilemix_routing_word_count_c(M, N, g)

@@ -53,7 +53,8 @@ cudaError_t quantize_impl(const __half* Q, const __half* K, std::int8_t* Q8, std
 cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, float* O, int heads,
                            int M, int N, int d, float score_scale, bool causal, cudaStream_t stream,
                            const TileMixRouting& routing, const TileMixQuantized& quantized,
-                           const TileMixOutput* strided = nullptr, unsigned long long watchdog_test_ns = 0) {
+                           const TileMixOutput* strided = nullptr, unsigned long long watchdog_test_ns = 0,
+                           const __half* v_absmax = nullptr) {
     // Same checks, same order as src/tilemix.cu:242-253.
     if (!Q || !K || !V || (!O && !strided) || heads <= 0 || M <= 0 || N <= 0 || d <= 0 ||
         !std::isfinite(score_scale) || routing.key_tiles_per_group <= 0 ||
@@ -103,9 +104,24 @@ cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, fl
         prob.o_stride_head = strided->stride_head;
         prob.o_stride_row = strided->stride_row;
     }
+    prob.v_absmax = v_absmax;
     prob.watchdog_test = watchdog_test_ns != 0;
     prob.watchdog_limit_ns = watchdog_test_ns;
     return tilemix::launch_attention(prob, stream);
+}
+
+cudaError_t quantize_qkv_impl(const __half* Q, const __half* K, const __half* V, std::int8_t* Q8, std::int8_t* K8,
+                              __half* q_scales, __half* k_scales, __half* v_absmax, int heads, int M, int N, int d,
+                              cudaStream_t stream) {
+    if (!V || !v_absmax) return cudaErrorInvalidValue;
+    if (!Q || !K || !Q8 || !K8 || !q_scales || !k_scales || heads <= 0 || M <= 0 || N <= 0 || d <= 0) {
+        return cudaErrorInvalidValue;
+    }
+    if (d > kFusedMaxHeadDim) return cudaErrorNotSupported;
+    if (!fits(heads, M, d) || !fits(heads, N, d)) return cudaErrorInvalidValue;
+    const cudaError_t status = check_device();
+    if (status != cudaSuccess) return status;
+    return tilemix::launch_quantize_qkv(Q, K, V, Q8, K8, q_scales, k_scales, v_absmax, heads, M, N, d, stream);
 }
 
 cudaError_t quantize_k_impl(const __half* K, std::int8_t* K8, __half* k_scales, int heads, int N, int d,
@@ -398,6 +414,20 @@ cudaError_t tilemix_attention_batched_qfused(const __half* Q, const __half* K, c
                                  Q8_out, q_scales_out);
 }
 
+cudaError_t quantize_tilemix_qkv_batched(const __half* Q, const __half* K, const __half* V, std::int8_t* Q8,
+                                         std::int8_t* K8, __half* q_scales, __half* k_scales, __half* v_absmax,
+                                         int heads, int M, int N, int d, cudaStream_t stream) {
+    return quantize_qkv_impl(Q, K, V, Q8, K8, q_scales, k_scales, v_absmax, heads, M, N, d, stream);
+}
+
+cudaError_t tilemix_attention_batched_hinted(const __half* Q, const __half* K, const __half* V, float* O, int heads,
+                                             int M, int N, int d, float score_scale, bool causal, cudaStream_t stream,
+                                             const TileMixRouting& routing, const TileMixQuantized& quantized,
+                                             const __half* v_absmax) {
+    return attention_impl(Q, K, V, O, heads, M, N, d, score_scale, causal, stream, routing, quantized, nullptr, 0,
+                          v_absmax);
+}
+
 cudaError_t tilemix_routing_policy(const __half* q_scales, const __half* k_scales, std::uint64_t* words, int heads,
                                    int M, int N, int key_tiles_per_group, float max_scale_product,
                                    cudaStream_t stream) {
@@ -484,6 +514,24 @@ int tilemix_attention_batched_qfused(const void* Q, const void* K, const void* V
         static_cast<const __half*>(Q), static_cast<const __half*>(K), static_cast<const __half*>(V), O, heads, M, N,
         d, score_scale, causal != 0, static_cast<cudaStream_t>(stream), to_cpp(routing), K8,
         static_cast<const __half*>(k_scales), Q8_out, static_cast<__half*>(q_scales_out)));
+}
+
+int tilemix_quantize_qkv_batched(const void* Q, const void* K, const void* V, int8_t* Q8, int8_t* K8, void* q_scales,
+                                  void* k_scales, void* v_absmax, int heads, int M, int N, int d, void* stream) {
+    return static_cast<int>(quantize_qkv_impl(static_cast<const __half*>(Q), static_cast<const __half*>(K),
+                                              static_cast<const __half*>(V), Q8, K8, static_cast<__half*>(q_scales),
+                                              static_cast<__half*>(k_scales), static_cast<__half*>(v_absmax), heads,
+                                              M, N, d, static_cast<cudaStream_t>(stream)));
+}
+
+int tilemix_attention_batched_hinted(const void* Q, const void* K, const void* V, float* O, int heads, int M, int N,
+                                     int d, float score_scale, int causal, void* stream,
+                                     const tilemix_routing* routing, const tilemix_quantized* quantized,
+                                     const void* v_absmax) {
+    return static_cast<int>(attention_impl(static_cast<const __half*>(Q), static_cast<const __half*>(K),
+                                           static_cast<const __half*>(V), O, heads, M, N, d, score_scale,
+                                           causal != 0, static_cast<cudaStream_t>(stream), to_cpp(routing),
+                                           to_cpp(quantized), nullptr, 0, static_cast<const __half*>(v_absmax)));
 }
 
 int tilemix_routing_policy_c(const void* q_scales, const void* k_scales, uint64_t* words, int heads, int M, int N,

@@ -106,6 +106,12 @@ constexpr uint64_t kWaitLimitNs = 1000000000ull;   // default watchdog limit of 
 constexpr uint32_t kSuspendNs = 200000;      // per try_wait suspension (wakes early on completion)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 15.0f;        // rescale only when the max grows by > 2^15 (P <= 32768)
+// Single-term P: rounding p to fp16 changes each p by at most 2^-11 p, so a
+// key half-block whose |v| are all <= 3.5 adds at most 2^-11 * 3.5 = 1.7e-3 to
+// any output element (O = sum p v / sum p, with the sum over the unrounded p):
+// inside the 2e-3 parity bar. Such halves skip the P_lo term (decided from the
+// per-64-key-block max |v| the caller passes, v_absmax).
+constexpr float kSingleTermVMax = 3.5f;
 
 __device__ __forceinline__ uint32_t col_s(int b) { return static_cast<uint32_t>(b) * 128u; }
 
@@ -124,10 +130,14 @@ enum : unsigned int {
 //   scales the block's two 64-key K scales (fp16, 0 when unrouted)
 //   plan   the block's QK MMA plan per 64-key half (see make_plan; key
 //          tiles counted from the half's first)
+//   single bit h set: every |v| of the half's 64 keys is <= kSingleTermVMax, so
+//          P of that half is stored as one fp16 term and PV runs once
 struct RouteSlot {
     uint32_t pats;
     uint32_t scales;
     std::uint64_t plan[2];
+    uint32_t single;    // bit h: key half h of the block takes single-term P (see kSingleTermVMax)
+    uint32_t pad;
 };
 
 template <int kAtoms>
@@ -236,6 +246,7 @@ struct Params {
     int causal;
     int routed;
     int fuse_q;          // Q quantized inside the CTA (no Q8 / q_scales inputs)
+    const __half* v_absmax;   // optional [heads][k_scale_blocks] max |v| per 64-key block
     std::int8_t* q8_out;      // fused Q: optional Q8 output [heads][M][d]
     __half* q_scales_out;     // fused Q: optional scale output [heads][q_scale_blocks]
     int q8_vec;          // q8_out takes 16-byte stores (d % 16 == 0, aligned)
@@ -348,6 +359,7 @@ struct RouteFetch {
     std::uint64_t word;         // prefetched word
     uint32_t bit;               // bit of the prefetched word
     uint32_t scale;             // lanes 0, 1: prefetched K scale (fp16 bits) of the block's 64-key halves
+    uint32_t vmax;              // lanes 2, 3: prefetched max |v| (fp16 bits) of the block's 64-key halves
 
     __device__ __forceinline__ void init(const Params& p, int head, int qt, uint32_t lane) {
         const int q16 = qt * (kTileRows / 16) + static_cast<int>(lane & 7u);
@@ -364,15 +376,21 @@ struct RouteFetch {
         const int sb = 2 * j + static_cast<int>(lane);
         scale = p.routed && lane < 2 && j < nblk && sb < p.k_scale_blocks
                     ? __half_as_ushort(p.k_scales[static_cast<std::size_t>(head) * p.k_scale_blocks + sb]) : 0u;
+        const int vb = 2 * j + static_cast<int>(lane) - 2;
+        vmax = p.v_absmax && (lane == 2 || lane == 3) && j < nblk && vb < p.k_scale_blocks
+                   ? __half_as_ushort(p.v_absmax[static_cast<std::size_t>(head) * p.k_scale_blocks + vb]) : 0x7E00u;
     }
 
     // pats: INT8 bits; valid: bits of existing (query tile, key tile) pairs.
     __device__ __forceinline__ void decode(const Params& p, int j, uint32_t& pats, uint32_t& valid,
-                                           uint32_t& scales) const {
+                                           uint32_t& scales, uint32_t& single) const {
         const bool ok = q_ok && 4 * j + static_cast<int>(kt) < p.k32_tiles;
         valid = __ballot_sync(0xffffffffu, ok);
         pats = __ballot_sync(0xffffffffu, ok && ((word >> bit) & 1ull) != 0);
         scales = __shfl_sync(0xffffffffu, scale, 0) | (__shfl_sync(0xffffffffu, scale, 1) << 16);
+        // NaN (0x7E00, also "no statistics") compares false
+        const bool small = __half2float(__ushort_as_half(static_cast<unsigned short>(vmax))) <= kSingleTermVMax;
+        single = (__ballot_sync(0xffffffffu, small) >> 2) & 3u;
     }
 };
 
@@ -728,8 +746,8 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int i = 0; i <= nblk; ++i) {
             if (i < nblk) {
                 const int j = i;
-                uint32_t pats, valid, scales;
-                route.decode(p, j, pats, valid, scales);
+                uint32_t pats, valid, scales, single;
+                route.decode(p, j, pats, valid, scales, single);
                 route.fetch(p, head, j + 1, nblk, lane);
                 const bool need_i8 = pats != 0;
                 const bool need_f16 = (valid & ~pats) != 0;
@@ -737,6 +755,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                     RouteSlot slot;
                     slot.pats = pats;
                     slot.scales = scales;
+                    slot.single = single;
                     const int kt_here = min(4, p.k32_tiles - 4 * j);
                     slot.plan[0] = make_plan(pats & 0xffffu, (valid & ~pats) & 0xffffu, min(2, kt_here));
                     slot.plan[1] = make_plan(pats >> 16, (valid & ~pats) >> 16, min(2, kt_here - 2));
@@ -905,18 +924,26 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         // P_lo of a 16-key step share the V operand.
         auto issue_pv_half = [&](int j) {
             const int vs = j % kVStages;
+            const bool single = (ring[j % kRouteSlots].single >> mh) & 1u;
             if (elect_one()) {
                 const uint32_t v_lo = v_lo0 + static_cast<uint32_t>(vs) * (L::kTileF16 >> 4);
                 const uint32_t o_tmem = tmem + kColO + 128u * mh;
                 const uint32_t a0 = tmem + col_s(j & 1) + 64u * mh;
                 const uint32_t b0 = v_lo + 512u * mh;
                 mma_f16_ts_w(o_tmem, a0, b0, dhi, pv_idesc, j > 0 ? 1u : 0u);
-                mma_f16_ts_w(o_tmem, a0 + 16, b0, dhi, pv_idesc, 1u);
-                #pragma unroll
-                for (int t = 1; t < 4; ++t) {
-                    const uint32_t a_hi = a0 + 32 * (t >> 1) + 8 * (t & 1);
-                    mma_f16_ts_w(o_tmem, a_hi, b0 + 128 * t, dhi, pv_idesc, 1u);
-                    mma_f16_ts_w(o_tmem, a_hi + 16, b0 + 128 * t, dhi, pv_idesc, 1u);
+                if (single) {
+                    #pragma unroll
+                    for (int t = 1; t < 4; ++t) {
+                        mma_f16_ts_w(o_tmem, a0 + 32 * (t >> 1) + 8 * (t & 1), b0 + 128 * t, dhi, pv_idesc, 1u);
+                    }
+                } else {
+                    mma_f16_ts_w(o_tmem, a0 + 16, b0, dhi, pv_idesc, 1u);
+                    #pragma unroll
+                    for (int t = 1; t < 4; ++t) {
+                        const uint32_t a_hi = a0 + 32 * (t >> 1) + 8 * (t & 1);
+                        mma_f16_ts_w(o_tmem, a_hi, b0 + 128 * t, dhi, pv_idesc, 1u);
+                        mma_f16_ts_w(o_tmem, a_hi + 16, b0 + 128 * t, dhi, pv_idesc, 1u);
+                    }
                 }
                 tc_commit(bar(kBarPvDone + 2 * (j & 1) + mh));
                 tc_commit(bar(kBarVEmpty + vs));
@@ -1002,8 +1029,10 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         // exponentiated, so the loop top only waits for S.
         uint32_t n_types = 0;
         float n_ratio = 0.0f;
+        bool n_single = false;
         auto decode = [&](int jb) {
             const RouteSlot sl = ring[jb % kRouteSlots];
+            n_single = (sl.single >> half) & 1u;
             n_types = q16_valid ? (((sl.pats >> (16 * half + qlocal)) & 1u) |
                                    (((sl.pats >> (16 * half + 8 + qlocal)) & 1u) << 1)) : 0u;
             const uint32_t sc = half ? sl.scales >> 16 : sl.scales & 0xffffu;
@@ -1020,6 +1049,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             const uint32_t s_own = s_row + 64u * half;
             uint32_t types = n_types;          // bit c: chunk c of this half is INT8
             const float ratio = n_ratio;
+            const bool single = n_single;      // this half's P as one fp16 term
             const int key0 = j * kTileKeys;
             const int limit = p.causal ? min(p.N, q_row + 1) : p.N;
             // fast: no key of the block is masked for any row of the warp and
@@ -1144,37 +1174,65 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             float2 s01 = make_float2(0.0f, 0.0f), s23 = make_float2(0.0f, 0.0f);
             const float2 nm2 = make_float2(neg_m, neg_m);
             const float2 minus1 = make_float2(-1.0f, -1.0f);
-            #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                const uint32_t (&x)[32] = c ? xb : xa;
-                const float mul = c ? mul1 : mul0;
-                const float2 mul2 = make_float2(mul, mul);
-                float2 arg[16];
+            if (single) {
+                // every |v| of this half is small: P rounded once to fp16
+                // (P_hi columns only; PV runs one MMA per K step)
                 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    arg[i] = __ffma2_rn(make_float2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])),
-                                        mul2, nm2);
+                for (int c = 0; c < 2; ++c) {
+                    const uint32_t (&x)[32] = c ? xb : xa;
+                    const float mul = c ? mul1 : mul0;
+                    const float2 mul2 = make_float2(mul, mul);
+                    float2 arg[16];
+                    #pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        arg[i] = __ffma2_rn(make_float2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])),
+                                            mul2, nm2);
+                    }
+                    uint32_t hi[16];
+                    #pragma unroll
+                    for (int i = 0; i < 16; i += 2) {
+                        const float2 p01 = make_float2(ex2(arg[i].x), ex2(arg[i].y));
+                        const float2 p23 = make_float2(ex2(arg[i + 1].x), ex2(arg[i + 1].y));
+                        s01 = __fadd2_rn(s01, p01);
+                        s23 = __fadd2_rn(s23, p23);
+                        hi[i] = pack_half2(p01.x, p01.y);
+                        hi[i + 1] = pack_half2(p23.x, p23.y);
+                    }
+                    tmem_st16(s_own + 32 * c, hi);
                 }
-                uint32_t hi[16], lo[16];
+            } else {
                 #pragma unroll
-                for (int i = 0; i < 16; i += 2) {
-                    const float2 p01 = make_float2(ex2(arg[i].x), ex2(arg[i].y));
-                    const float2 p23 = make_float2(ex2(arg[i + 1].x), ex2(arg[i + 1].y));
-                    s01 = __fadd2_rn(s01, p01);
-                    s23 = __fadd2_rn(s23, p23);
-                    const float2 h01 = make_float2(__uint_as_float(__float_as_uint(p01.x) & 0xFFFFE000u),
-                                                   __uint_as_float(__float_as_uint(p01.y) & 0xFFFFE000u));
-                    const float2 h23 = make_float2(__uint_as_float(__float_as_uint(p23.x) & 0xFFFFE000u),
-                                                   __uint_as_float(__float_as_uint(p23.y) & 0xFFFFE000u));
-                    hi[i] = pack_half2(h01.x, h01.y);
-                    hi[i + 1] = pack_half2(h23.x, h23.y);
-                    const float2 l01 = __ffma2_rn(h01, minus1, p01);      // p - P_hi, exact
-                    const float2 l23 = __ffma2_rn(h23, minus1, p23);
-                    lo[i] = pack_half2(l01.x, l01.y);
-                    lo[i + 1] = pack_half2(l23.x, l23.y);
+                for (int c = 0; c < 2; ++c) {
+                    const uint32_t (&x)[32] = c ? xb : xa;
+                    const float mul = c ? mul1 : mul0;
+                    const float2 mul2 = make_float2(mul, mul);
+                    float2 arg[16];
+                    #pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        arg[i] = __ffma2_rn(make_float2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])),
+                                            mul2, nm2);
+                    }
+                    uint32_t hi[16], lo[16];
+                    #pragma unroll
+                    for (int i = 0; i < 16; i += 2) {
+                        const float2 p01 = make_float2(ex2(arg[i].x), ex2(arg[i].y));
+                        const float2 p23 = make_float2(ex2(arg[i + 1].x), ex2(arg[i + 1].y));
+                        s01 = __fadd2_rn(s01, p01);
+                        s23 = __fadd2_rn(s23, p23);
+                        const float2 h01 = make_float2(__uint_as_float(__float_as_uint(p01.x) & 0xFFFFE000u),
+                                                       __uint_as_float(__float_as_uint(p01.y) & 0xFFFFE000u));
+                        const float2 h23 = make_float2(__uint_as_float(__float_as_uint(p23.x) & 0xFFFFE000u),
+                                                       __uint_as_float(__float_as_uint(p23.y) & 0xFFFFE000u));
+                        hi[i] = pack_half2(h01.x, h01.y);
+                        hi[i + 1] = pack_half2(h23.x, h23.y);
+                        const float2 l01 = __ffma2_rn(h01, minus1, p01);      // p - P_hi, exact
+                        const float2 l23 = __ffma2_rn(h23, minus1, p23);
+                        lo[i] = pack_half2(l01.x, l01.y);
+                        lo[i + 1] = pack_half2(l23.x, l23.y);
+                    }
+                    tmem_st16(s_own + 32 * c, hi);
+                    tmem_st16(s_own + 32 * c + 16, lo);
                 }
-                tmem_st16(s_own + 32 * c, hi);
-                tmem_st16(s_own + 32 * c + 16, lo);
             }
             l_run += (s01.x + s01.y) + (s23.x + s23.y);
             s_ready = j + 1 < nblk && mbar_test_wait(bar(kBarSFull + 2 * (b ^ 1) + half), ((j + 1) >> 1) & 1);
@@ -1454,6 +1512,7 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     p.causal = prob.causal ? 1 : 0;
     p.routed = prob.words != nullptr ? 1 : 0;
     p.fuse_q = prob.fuse_q ? 1 : 0;
+    p.v_absmax = prob.v_absmax;
     p.q8_out = prob.q8_out;
     p.q_scales_out = prob.q_scales_out;
     p.q8_vec = (prob.d % 16 == 0 && aligned16(prob.q8_out)) ? 1 : 0;

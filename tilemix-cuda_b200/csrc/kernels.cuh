@@ -54,6 +54,9 @@ struct AttentionProblem {
     bool fuse_q;
     std::int8_t* q8_out;
     __half* q_scales_out;
+    // Optional max |v| per 64-key block [heads][ceil(N/64)]: key halves whose
+    // max is <= 3.5 take single-term P (null: two-term everywhere).
+    const __half* v_absmax;
 };
 
 // Routing words from the quantizer's block scales (policy.cu): INT8 iff
@@ -61,6 +64,13 @@ struct AttentionProblem {
 cudaError_t launch_routing_policy(const __half* q_scales, const __half* k_scales, std::uint64_t* words, int heads,
                                   int M, int N, int key_tiles_per_group, float max_scale_product,
                                   cudaStream_t stream);
+
+// quantize Q and K as launch_quantize, and record max |V| of every 64-row V
+// block (fp16, NaN when the block holds one) in v_absmax [heads][ceil(N/64)],
+// all in one launch.
+cudaError_t launch_quantize_qkv(const __half* Q, const __half* K, const __half* V, std::int8_t* Q8, std::int8_t* K8,
+                                __half* q_scales, __half* k_scales, __half* v_absmax, int heads, int M, int N,
+                                int d, cudaStream_t stream);
 
 // Quantize K [heads, N, d] alone (64-row blocks), for the fused-Q path.
 cudaError_t launch_quantize_k(const __half* K, std::int8_t* K8, __half* k_scales, int heads, int N, int d,

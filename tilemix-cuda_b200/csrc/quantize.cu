@@ -73,12 +73,15 @@ struct QuantTensor {
 };
 
 __global__ void __launch_bounds__(kQuantThreads, 4)
-quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
+quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, QuantTensor vt, int heads, int d) {
     __shared__ float scratch[kQuantThreads / 32];
-    const int q_ctas = heads * qt.blocks;
-    const bool is_q = static_cast<int>(blockIdx.x) < q_ctas;
-    const QuantTensor& t = is_q ? qt : kt;
-    const int cta = is_q ? static_cast<int>(blockIdx.x) : static_cast<int>(blockIdx.x) - q_ctas;
+    // CTAs [0, q) quantize Q blocks, [q, q + k) K blocks, the rest record the
+    // absmax of V blocks (vt.values == nullptr: statistics only)
+    const int q_ctas = heads * qt.blocks, k_ctas = heads * kt.blocks;
+    const int bid = static_cast<int>(blockIdx.x);
+    const bool is_q = bid < q_ctas, is_k = !is_q && bid < q_ctas + k_ctas;
+    const QuantTensor& t = is_q ? qt : is_k ? kt : vt;
+    const int cta = is_q ? bid : is_k ? bid - q_ctas : bid - q_ctas - k_ctas;
     const int head = cta / t.blocks, block = cta % t.blocks;
     const int first_row = block * t.block_rows;
     const int rows_here = min(t.block_rows, t.rows - first_row);
@@ -104,6 +107,10 @@ quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
             }
         }
         const float absmax = block_max_nan(max_nan(__low2float(m2), __high2float(m2)), scratch);
+        if (!t.values) {   // V statistics: the block's max |v| (exact in fp16; NaN if the block holds one)
+            if (threadIdx.x == 0) t.scales[static_cast<std::size_t>(head) * t.blocks + block] = __float2half_rn(absmax);
+            return;
+        }
         if (fast_block(absmax)) {
             // every block of finite, not-all-zero inputs: branch-free exact rounding
             const float scale = __fdiv_rn(absmax, 127.0f);
@@ -150,6 +157,13 @@ quantize_blocks_kernel(QuantTensor qt, QuantTensor kt, int heads, int d) {
             }
         }
     } else {
+        if (!t.values) {   // V statistics (NaN-propagating, as on the vector path)
+            float vmax = 0.0f;
+            for (int i = threadIdx.x; i < count; i += kQuantThreads) vmax = max_nan(vmax, fabsf(__half2float(src[i])));
+            const float absmax = block_max_nan(vmax, scratch);
+            if (threadIdx.x == 0) t.scales[static_cast<std::size_t>(head) * t.blocks + block] = __float2half_rn(absmax);
+            return;
+        }
         float local = 0.0f;
         for (int i = threadIdx.x; i < count; i += kQuantThreads) {
             local = fmaxf(local, fabsf(__half2float(src[i])));
@@ -177,7 +191,8 @@ cudaError_t launch_quantize(const __half* Q, const __half* K, std::int8_t* Q8, s
                    d % 8 == 0 && aligned(K, 16) && aligned(K8, 8)};
     const long long ctas = static_cast<long long>(heads) * (qt.blocks + kt.blocks);
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-    quantize_blocks_kernel<<<static_cast<unsigned>(ctas), kQuantThreads, 0, stream>>>(qt, kt, heads, d);
+    const QuantTensor none{nullptr, nullptr, nullptr, 0, kQuantKRows, 0, false};   // no V statistics
+    quantize_blocks_kernel<<<static_cast<unsigned>(ctas), kQuantThreads, 0, stream>>>(qt, kt, none, heads, d);
     return cudaGetLastError();
 }
 
@@ -188,7 +203,21 @@ cudaError_t launch_quantize_k(const __half* K, std::int8_t* K8, __half* k_scales
                    d % 8 == 0 && aligned(K, 16) && aligned(K8, 8)};
     const long long ctas = static_cast<long long>(heads) * kt.blocks;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-    quantize_blocks_kernel<<<static_cast<unsigned>(ctas), kQuantThreads, 0, stream>>>(none, kt, heads, d);
+    quantize_blocks_kernel<<<static_cast<unsigned>(ctas), kQuantThreads, 0, stream>>>(none, kt, none, heads, d);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_qkv(const __half* Q, const __half* K, const __half* V, std::int8_t* Q8, std::int8_t* K8,
+                                __half* q_scales, __half* k_scales, __half* v_absmax, int heads, int M, int N,
+                                int d, cudaStream_t stream) {
+    QuantTensor qt{Q, Q8, q_scales, M, kQuantQRows, (M - 1) / kQuantQRows + 1,
+                   d % 8 == 0 && aligned(Q, 16) && aligned(Q8, 8)};
+    QuantTensor kt{K, K8, k_scales, N, kQuantKRows, (N - 1) / kQuantKRows + 1,
+                   d % 8 == 0 && aligned(K, 16) && aligned(K8, 8)};
+    QuantTensor vt{V, nullptr, v_absmax, N, kQuantKRows, (N - 1) / kQuantKRows + 1, d % 8 == 0 && aligned(V, 16)};
+    const long long ctas = static_cast<long long>(heads) * (qt.blocks + kt.blocks + vt.blocks);
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    quantize_blocks_kernel<<<static_cast<unsigned>(ctas), kQuantThreads, 0, stream>>>(qt, kt, vt, heads, d);
     return cudaGetLastError();
 }
 

@@ -95,6 +95,11 @@ def _load():
     lib.tilemix_attention_batched_qfused.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P,
                                                      ctypes.POINTER(_Routing), _P, _P, _P, _P]
     lib.tilemix_attention_batched_qfused.restype = _I
+    lib.tilemix_quantize_qkv_batched.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P]
+    lib.tilemix_quantize_qkv_batched.restype = _I
+    lib.tilemix_attention_batched_hinted.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P,
+                                                     ctypes.POINTER(_Routing), ctypes.POINTER(_Quantized), _P]
+    lib.tilemix_attention_batched_hinted.restype = _I
     lib.tilemix_routing_policy_c.argtypes = [_P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _P]
     lib.tilemix_routing_policy_c.restype = _I
     lib.tilemix_policy_max_scale_product_c.argtypes = [ctypes.c_float, ctypes.c_float, _I]
@@ -132,6 +137,7 @@ C_ABI_SYMBOLS = (
     "tilemix_attention_from_host", "tilemix_attention_routed_noalloc",
     "tilemix_quantize_k_batched", "tilemix_attention_batched_qfused",
     "tilemix_routing_policy_c", "tilemix_policy_max_scale_product_c",
+    "tilemix_quantize_qkv_batched", "tilemix_attention_batched_hinted",
     "tilemix_routing_word_count_c", "tilemix_routing_words_per_row_c",
     "tilemix_reference_shared_bytes", "tilemix_b200_shared_bytes_c",
     "tilemix_read_and_clear_status", "tilemix_watchdog_selftest",
@@ -251,6 +257,27 @@ def tilemix_attention_batched_qfused(Q, K, V, O, heads: int, M: int, N: int, d: 
                                                       float(score_scale), int(bool(causal)), _stream(stream),
                                                       ctypes.byref(r), _addr(K8), _addr(k_scales), _addr(Q8_out),
                                                       _addr(q_scales_out))
+
+
+def quantize_tilemix_qkv_batched(Q, K, V, Q8, K8, q_scales, k_scales, v_absmax, heads: int, M: int, N: int,
+                                 d: int, stream=None) -> int:
+    """quantize_tilemix_qk_batched plus max |v| per 64-row V block (fp16
+    [heads, ceil(N/64)]) in the same launch."""
+    return _native().tilemix_quantize_qkv_batched(_addr(Q), _addr(K), _addr(V), _addr(Q8), _addr(K8),
+                                                  _addr(q_scales), _addr(k_scales), _addr(v_absmax), heads, M, N,
+                                                  d, _stream(stream))
+
+
+def tilemix_attention_batched_hinted(Q, K, V, O, heads: int, M: int, N: int, d: int, score_scale: float,
+                                     causal: bool = False, stream=None, routing: TileMixRouting | None = None,
+                                     quantized: TileMixQuantized | None = None, v_absmax=None) -> int:
+    """tilemix_attention_batched with single-term fp16 P for the 64-key halves
+    whose max |v| (v_absmax) is <= 3.5 (at most 1.7e-3 added to any output)."""
+    r = (routing or TileMixRouting())._c()
+    q = (quantized or TileMixQuantized())._c()
+    return _native().tilemix_attention_batched_hinted(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
+                                                      float(score_scale), int(bool(causal)), _stream(stream),
+                                                      ctypes.byref(r), ctypes.byref(q), _addr(v_absmax))
 
 
 def tilemix_routing_policy(q_scales, k_scales, words, heads: int, M: int, N: int, key_tiles_per_group: int,
