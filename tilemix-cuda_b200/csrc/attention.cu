@@ -382,15 +382,19 @@ struct RouteFetch {
     }
 
     // pats: INT8 bits; valid: bits of existing (query tile, key tile) pairs.
+    template <bool kPvHint>
     __device__ __forceinline__ void decode(const Params& p, int j, uint32_t& pats, uint32_t& valid,
                                            uint32_t& scales, uint32_t& single) const {
         const bool ok = q_ok && 4 * j + static_cast<int>(kt) < p.k32_tiles;
         valid = __ballot_sync(0xffffffffu, ok);
         pats = __ballot_sync(0xffffffffu, ok && ((word >> bit) & 1ull) != 0);
         scales = __shfl_sync(0xffffffffu, scale, 0) | (__shfl_sync(0xffffffffu, scale, 1) << 16);
-        // NaN (0x7E00, also "no statistics") compares false
-        const bool small = __half2float(__ushort_as_half(static_cast<unsigned short>(vmax))) <= kSingleTermVMax;
-        single = (__ballot_sync(0xffffffffu, small) >> 2) & 3u;
+        single = 0u;
+        if (kPvHint) {
+            // NaN (0x7E00, also "no statistics") compares false
+            const bool small = __half2float(__ushort_as_half(static_cast<unsigned short>(vmax))) <= kSingleTermVMax;
+            single = (__ballot_sync(0xffffffffu, small) >> 2) & 3u;
+        }
     }
 };
 
@@ -630,7 +634,7 @@ __device__ __forceinline__ void tile_of(const Params& p, int bid, int& head, int
     head = group0 + in_group % group_heads;
 }
 
-template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided, bool kWithholdArrive = false>
+template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided, bool kWithholdArrive = false, bool kPvHint = false>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
@@ -747,7 +751,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             if (i < nblk) {
                 const int j = i;
                 uint32_t pats, valid, scales, single;
-                route.decode(p, j, pats, valid, scales, single);
+                route.decode<kPvHint>(p, j, pats, valid, scales, single);
                 route.fetch(p, head, j + 1, nblk, lane);
                 const bool need_i8 = pats != 0;
                 const bool need_f16 = (valid & ~pats) != 0;
@@ -924,7 +928,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         // P_lo of a 16-key step share the V operand.
         auto issue_pv_half = [&](int j) {
             const int vs = j % kVStages;
-            const bool single = (ring[j % kRouteSlots].single >> mh) & 1u;
+            const bool single = kPvHint && ((ring[j % kRouteSlots].single >> mh) & 1u);
             if (elect_one()) {
                 const uint32_t v_lo = v_lo0 + static_cast<uint32_t>(vs) * (L::kTileF16 >> 4);
                 const uint32_t o_tmem = tmem + kColO + 128u * mh;
@@ -1032,7 +1036,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
         bool n_single = false;
         auto decode = [&](int jb) {
             const RouteSlot sl = ring[jb % kRouteSlots];
-            n_single = (sl.single >> half) & 1u;
+            if (kPvHint) n_single = (sl.single >> half) & 1u;
             n_types = q16_valid ? (((sl.pats >> (16 * half + qlocal)) & 1u) |
                                    (((sl.pats >> (16 * half + 8 + qlocal)) & 1u) << 1)) : 0u;
             const uint32_t sc = half ? sl.scales >> 16 : sl.scales & 0xffffu;
@@ -1049,7 +1053,7 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
             const uint32_t s_own = s_row + 64u * half;
             uint32_t types = n_types;          // bit c: chunk c of this half is INT8
             const float ratio = n_ratio;
-            const bool single = n_single;      // this half's P as one fp16 term
+            const bool single = kPvHint && n_single;      // this half's P as one fp16 term
             const int key0 = j * kTileKeys;
             const int limit = p.causal ? min(p.N, q_row + 1) : p.N;
             // fast: no key of the block is masked for any row of the warp and
@@ -1440,9 +1444,10 @@ bool encode_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, in
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided = false, bool kWithholdArrive = false>
+template <int kAtoms, bool kUseTma, bool kTrace, bool kStrided = false, bool kWithholdArrive = false,
+          bool kPvHint = false>
 cudaError_t launch_variant(const CUtensorMap* maps, const Params& p, unsigned grid, cudaStream_t stream) {
-    auto kernel = tilemix_attention_kernel<kAtoms, kUseTma, kTrace, kStrided, kWithholdArrive>;
+    auto kernel = tilemix_attention_kernel<kAtoms, kUseTma, kTrace, kStrided, kWithholdArrive, kPvHint>;
     const int smem = static_cast<int>(SmemLayout<kAtoms>::kBytes);
     // The opt-in attribute is per device; set it the first time a device is seen.
     static int configured[64] = {0};
@@ -1563,6 +1568,12 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     p.o_tma = (!strided && prob.d % 32 == 0 && aligned16(prob.o) &&
                encode_map(&maps[5], prob.o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.heads, p.M, p.d, 32, 32)) ? 1 : 0;
     const unsigned g = static_cast<unsigned>(grid);
+    if (prob.v_absmax && tma && !strided && !trace && !prob.watchdog_test) {
+        // precision hints: the instantiation with per-half single-term P
+        return atoms == 1 ? launch_variant<1, true, false, false, false, true>(maps, p, g, stream)
+                          : launch_variant<2, true, false, false, false, true>(maps, p, g, stream);
+    }
+    p.v_absmax = nullptr;   // the other builds keep two-term P everywhere
     if (prob.watchdog_test) {
         // The self-test instantiation exists for d = 65..128 with TMA, fp32
         // output, no routing trace outputs.
