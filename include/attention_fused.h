@@ -160,7 +160,9 @@ cudaError_t quantize_tilemix_qkv_batched(const __half* Q, const __half* K, const
 // each p by at most 2^-11 p and O = sum p v / sum p, so such a half adds at
 // most 2^-11 * 3.5 = 1.7e-3 to any output element, within the 2e-3 parity
 // bar; halves with larger |v| keep the two-term P. v_absmax may be null (every
-// half two-term, identical to tilemix_attention_batched).
+// half two-term, identical to tilemix_attention_batched); layouts the TMA
+// build does not take (d % 16 != 0, unaligned bases) and routing trace
+// outputs also run two-term everywhere.
 cudaError_t tilemix_attention_batched_hinted(const __half* Q, const __half* K, const __half* V,
                                              float* O, int heads, int M, int N, int d,
                                              float score_scale, bool causal, cudaStream_t stream,
