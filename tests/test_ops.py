@@ -128,3 +128,50 @@ def test_validate_rejects_host_tensors():
         tm.validate_quantize_args(q, q)
     with pytest.raises(ValueError):
         torch.ops.tilemix.attention(q, q, q, None, None, None, None, None, 2, 0.125, False)
+
+
+def test_fake_shapes_of_the_newer_operators():
+    with FakeTensorMode():
+        q = torch.empty((3, 300, 128), dtype=torch.float16)
+        k = torch.empty((3, 257, 128), dtype=torch.float16)
+        v = torch.empty((3, 257, 128), dtype=torch.float16)
+        q8, k8, qs, ks, va = torch.ops.tilemix.quantize_qkv(q, k, v)
+        assert va.shape == ks.shape == (3, 5) and va.dtype == torch.float16
+        k8b, ks2 = torch.ops.tilemix.quantize_k(k)
+        assert k8b.shape == k.shape and ks2.shape == (3, 5)
+        words = torch.empty((3 * 19,), dtype=torch.int64)
+        o = torch.ops.tilemix.attention_hinted(q, k, v, q8, k8, qs, ks, words, 2, 0.088, True, va)
+        assert o.shape == q.shape and o.dtype == torch.float32
+        o2, q8f, qsf = torch.ops.tilemix.attention_qfused(q, k, v, k8b, ks2, words, 2, 0.088, True)
+        assert o2.shape == q.shape and q8f.shape == q.shape and qsf.shape == (3, 3)
+        w = torch.ops.tilemix.routing_policy(qs, ks, 300, 257, 2, 0.5)
+        assert w.shape == (3 * 19,) and w.dtype == torch.int64
+
+
+@pytest.mark.gpu
+def test_newer_operators_match_the_c_abi():
+    import tilemix_b200 as tm
+    from tilemix_b200 import workloads
+    w = workloads.make_inputs("c3", batch=1, heads=2, seq=384)
+    q, k, v = (w[x].cuda() for x in ("q", "k", "v"))
+    H, S, D = 2, 384, 128
+    q8, k8, qs, ks, va = torch.ops.tilemix.quantize_qkv(q, k, v)
+    e8, f8, es, fs = tm.quantize(q, k)
+    torch.cuda.synchronize()
+    assert torch.equal(q8, e8) and torch.equal(k8, f8) and torch.equal(qs, es) and torch.equal(ks, fs)
+    words = torch.ops.tilemix.routing_policy(qs, ks, S, S, 2, float(qs.float().median() * ks.float().median()))
+    ref_words = torch.empty_like(words)
+    assert tm.tilemix_routing_policy(qs, ks, ref_words, H, S, S, 2, float(qs.float().median() * ks.float().median())) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(words, ref_words)
+    expect = tm.attention(q, k, v, q8=q8, k8=k8, q_scales=qs, k_scales=ks, words=words, key_tiles_per_group=2,
+                          score_scale=w["score_scale"], causal=True)
+    o = torch.ops.tilemix.attention_hinted(q, k, v, q8, k8, qs, ks, words, 2, w["score_scale"], True, va)
+    k8b, ksb = torch.ops.tilemix.quantize_k(k)
+    o2, q8f, qsf = torch.ops.tilemix.attention_qfused(q, k, v, k8b, ksb, words, 2, w["score_scale"], True)
+    torch.cuda.synchronize()
+    assert torch.equal(k8b, k8) and torch.equal(ksb, ks) and torch.equal(q8f, q8) and torch.equal(qsf, qs)
+    assert torch.equal(o2, expect)
+    assert (o - expect).abs().max().item() <= 2e-3      # outlier data: every half two-term, so equal in practice
+    err, status = tm.read_and_clear_status()
+    assert err == 0 and status == 0

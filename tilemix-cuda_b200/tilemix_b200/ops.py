@@ -1,5 +1,8 @@
 """PyTorch operators over the C-ABI: ``torch.ops.tilemix.quantize_qk``,
-``torch.ops.tilemix.attention`` and ``torch.ops.tilemix.attention_bshd``.
+``.attention``, ``.attention_bshd``, ``.quantize_qkv`` + ``.attention_hinted``
+(single-term P from V statistics), ``.quantize_k`` + ``.attention_qfused`` (Q
+quantized inside the kernel) and ``.routing_policy`` (routing words chosen on
+the device).
 
 They call the same extern "C" entry points as the ctypes functions in
 ``tilemix_b200`` (``tilemix_quantize_qk_batched``, ``tilemix_attention_batched``)
@@ -18,9 +21,10 @@ import math
 
 import torch
 
-from . import (TileMixOutput, TileMixQuantized, TileMixRouting, check, quantize_tilemix_qk_batched,
-               tilemix_attention_batched, tilemix_attention_batched_out, validate_attention_args,
-               validate_quantize_args)
+from . import (TileMixOutput, TileMixQuantized, TileMixRouting, check, quantize_tilemix_k_batched,
+               quantize_tilemix_qk_batched, quantize_tilemix_qkv_batched, tilemix_attention_batched,
+               tilemix_attention_batched_hinted, tilemix_attention_batched_out, tilemix_attention_batched_qfused,
+               tilemix_routing_policy, tilemix_routing_word_count, validate_attention_args, validate_quantize_args)
 
 _Q_ROWS, _K_ROWS = 128, 64   # quantization block rows (include/attention_fused.h:13-14)
 
@@ -111,6 +115,136 @@ def _(q, k, v, q8, k8, q_scales, k_scales, words, key_tiles_per_group, score_sca
       out_dtype):
     heads = 1 if q.dim() == 2 else q.shape[0]
     return q.new_empty((heads // heads_per_batch, q.shape[-2], heads_per_batch, q.shape[-1]), dtype=out_dtype)
+
+
+@torch.library.custom_op("tilemix::quantize_qkv", mutates_args=())
+def quantize_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor,
+                                                                          torch.Tensor, torch.Tensor]:
+    """quantize_qk plus max |v| per 64-row block of V (fp16 [heads, ceil(N/64)]),
+    the statistics attention_hinted uses for single-term P."""
+    heads, m, n, d = validate_attention_args(q, k, v)
+    q3, k3, v3 = _heads3(q).contiguous(), _heads3(k).contiguous(), _heads3(v).contiguous()
+    q8 = torch.empty(q.shape, dtype=torch.int8, device=q.device)
+    k8 = torch.empty(k.shape, dtype=torch.int8, device=k.device)
+    qs = torch.empty((heads, (m - 1) // _Q_ROWS + 1), dtype=torch.float16, device=q.device)
+    ks = torch.empty((heads, (n - 1) // _K_ROWS + 1), dtype=torch.float16, device=q.device)
+    va = torch.empty((heads, (n - 1) // _K_ROWS + 1), dtype=torch.float16, device=q.device)
+    check(quantize_tilemix_qkv_batched(q3, k3, v3, q8, k8, qs, ks, va, heads, m, n, d,
+                                       torch.cuda.current_stream(q.device)), "tilemix::quantize_qkv")
+    return q8, k8, qs, ks, va
+
+
+@quantize_qkv.register_fake
+def _(q, k, v):
+    heads = 1 if q.dim() == 2 else q.shape[0]
+    m, n = q.shape[-2], k.shape[-2]
+    kb = (n - 1) // _K_ROWS + 1
+    return (q.new_empty(q.shape, dtype=torch.int8), k.new_empty(k.shape, dtype=torch.int8),
+            q.new_empty((heads, (m - 1) // _Q_ROWS + 1), dtype=torch.float16),
+            q.new_empty((heads, kb), dtype=torch.float16), q.new_empty((heads, kb), dtype=torch.float16))
+
+
+@torch.library.custom_op("tilemix::attention_hinted", mutates_args=())
+def attention_hinted(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q8: torch.Tensor | None,
+                     k8: torch.Tensor | None, q_scales: torch.Tensor | None, k_scales: torch.Tensor | None,
+                     words: torch.Tensor | None, key_tiles_per_group: int, score_scale: float, causal: bool,
+                     v_absmax: torch.Tensor) -> torch.Tensor:
+    """``attention`` with single-term fp16 P for the 64-key halves whose max |v|
+    (``v_absmax`` from quantize_qkv) is <= 3.5 (at most 1.7e-3 added to any output)."""
+    heads, m, n, d = validate_attention_args(q, k, v, q8, k8, q_scales, k_scales, words, key_tiles_per_group)
+    if v_absmax.dtype != torch.float16 or v_absmax.numel() != heads * ((n - 1) // _K_ROWS + 1) or \
+            v_absmax.device != q.device:
+        raise ValueError("v_absmax must be fp16 [heads, ceil(N/64)] on q's device")
+    q3, k3, v3 = _heads3(q).contiguous(), _heads3(k).contiguous(), _heads3(v).contiguous()
+    q8, k8, q_scales, k_scales, words, v_absmax = _contiguous(q8, k8, q_scales, k_scales, words, v_absmax)
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    routing = TileMixRouting(words, 0 if words is None else words.numel(), key_tiles_per_group)
+    quantized = TileMixQuantized(q8, k8, q_scales, k_scales) if q8 is not None else None
+    check(tilemix_attention_batched_hinted(q3, k3, v3, out, heads, m, n, d, score_scale, causal,
+                                           torch.cuda.current_stream(q.device), routing, quantized, v_absmax),
+          "tilemix::attention_hinted")
+    return out
+
+
+@attention_hinted.register_fake
+def _(q, k, v, q8, k8, q_scales, k_scales, words, key_tiles_per_group, score_scale, causal, v_absmax):
+    return q.new_empty(q.shape, dtype=torch.float32)
+
+
+@torch.library.custom_op("tilemix::quantize_k", mutates_args=())
+def quantize_k(k: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """K alone in 64-row blocks (the pre-pass of attention_qfused)."""
+    heads, _, n, d = validate_quantize_args(k, k)
+    k3 = _heads3(k).contiguous()
+    k8 = torch.empty(k.shape, dtype=torch.int8, device=k.device)
+    ks = torch.empty((heads, (n - 1) // _K_ROWS + 1), dtype=torch.float16, device=k.device)
+    check(quantize_tilemix_k_batched(k3, k8, ks, heads, n, d, torch.cuda.current_stream(k.device)),
+          "tilemix::quantize_k")
+    return k8, ks
+
+
+@quantize_k.register_fake
+def _(k):
+    heads = 1 if k.dim() == 2 else k.shape[0]
+    return (k.new_empty(k.shape, dtype=torch.int8),
+            k.new_empty((heads, (k.shape[-2] - 1) // _K_ROWS + 1), dtype=torch.float16))
+
+
+@torch.library.custom_op("tilemix::attention_qfused", mutates_args=())
+def attention_qfused(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k8: torch.Tensor, k_scales: torch.Tensor,
+                     words: torch.Tensor, key_tiles_per_group: int, score_scale: float,
+                     causal: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Routed attention that quantizes each 128-row Q tile inside the kernel;
+    returns (out, q8, q_scales), q8 / q_scales the bytes quantize_qk makes."""
+    heads, m, n, d = validate_attention_args(q, k, v, words=None)
+    if k8.dtype != torch.int8 or tuple(k8.shape) != tuple(k.shape) or k_scales.dtype != torch.float16 or \
+            k_scales.numel() != heads * ((n - 1) // _K_ROWS + 1):
+        raise ValueError("k8 / k_scales must come from quantize_k on this k")
+    if words.dtype not in (torch.int64, torch.uint64) or \
+            words.numel() < heads * tilemix_routing_word_count(m, n, key_tiles_per_group):
+        raise ValueError("words must be 64-bit and hold heads * tilemix_routing_word_count words")
+    q3, k3, v3 = _heads3(q).contiguous(), _heads3(k).contiguous(), _heads3(v).contiguous()
+    k8, k_scales, words = _contiguous(k8, k_scales, words)
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    q8 = torch.empty(q.shape, dtype=torch.int8, device=q.device)
+    qs = torch.empty((heads, (m - 1) // _Q_ROWS + 1), dtype=torch.float16, device=q.device)
+    check(tilemix_attention_batched_qfused(q3, k3, v3, out, heads, m, n, d, score_scale, causal,
+                                           torch.cuda.current_stream(q.device),
+                                           TileMixRouting(words, words.numel(), key_tiles_per_group), k8, k_scales,
+                                           q8, qs), "tilemix::attention_qfused")
+    return out, q8, qs
+
+
+@attention_qfused.register_fake
+def _(q, k, v, k8, k_scales, words, key_tiles_per_group, score_scale, causal):
+    heads = 1 if q.dim() == 2 else q.shape[0]
+    return (q.new_empty(q.shape, dtype=torch.float32), q.new_empty(q.shape, dtype=torch.int8),
+            q.new_empty((heads, (q.shape[-2] - 1) // _Q_ROWS + 1), dtype=torch.float16))
+
+
+@torch.library.custom_op("tilemix::routing_policy", mutates_args=())
+def routing_policy(q_scales: torch.Tensor, k_scales: torch.Tensor, m: int, n: int, key_tiles_per_group: int,
+                   max_scale_product: float) -> torch.Tensor:
+    """Routing words (int64 view of the reference's uint64 mask words) chosen on
+    the device: INT8 iff q_scale * max k_scale of the key group <= max_scale_product."""
+    heads = q_scales.shape[0] if q_scales.dim() == 2 else 1
+    if q_scales.dtype != torch.float16 or k_scales.dtype != torch.float16 or \
+            q_scales.numel() != heads * ((m - 1) // _Q_ROWS + 1) or k_scales.numel() != heads * ((n - 1) // _K_ROWS + 1):
+        raise ValueError("q_scales / k_scales must be fp16 [heads, ceil(M/128)] / [heads, ceil(N/64)]")
+    words = torch.empty(heads * tilemix_routing_word_count(m, n, key_tiles_per_group), dtype=torch.int64,
+                        device=q_scales.device)
+    check(tilemix_routing_policy(q_scales.contiguous(), k_scales.contiguous(), words, heads, m, n,
+                                 key_tiles_per_group, max_scale_product, torch.cuda.current_stream(q_scales.device)),
+          "tilemix::routing_policy")
+    return words
+
+
+@routing_policy.register_fake
+def _(q_scales, k_scales, m, n, key_tiles_per_group, max_scale_product):
+    heads = q_scales.shape[0] if q_scales.dim() == 2 else 1
+    q16, k32 = (m + 15) // 16, (n + 31) // 32
+    groups = (k32 + key_tiles_per_group - 1) // key_tiles_per_group
+    return q_scales.new_empty((heads * q16 * ((groups + 63) // 64),), dtype=torch.int64)
 
 
 def tilemix_attention(q, k, v, words=None, *, key_tiles_per_group: int = 2, score_scale: float | None = None,
