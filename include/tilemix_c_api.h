@@ -200,6 +200,18 @@ size_t tilemix_routing_words_per_row_c(int N, int key_tiles_per_group);
 size_t tilemix_reference_shared_bytes(int d, int quantized);
 size_t tilemix_b200_shared_bytes_c(int d, int quantized);
 
+/* Backward of the unrouted attention (no reference counterpart; the reference
+ * is forward only): C form of tilemix_attention_backward in attention_fused.h.
+ * Q, K, V, dO fp16; O fp32 (the forward's output on the same inputs, unrouted);
+ * dQ [heads, M, d], dK and dV [heads, N, d] fp32 outputs; lse and dsum
+ * [heads, M] fp32 workspaces (base-2 log-sum-exp of score_scale * Q K^T rows,
+ * rowsum(dO * O)). d % 16 == 0, d <= 128, 16-byte aligned pointers. Its waits
+ * are bounded like the forward's and report through
+ * tilemix_read_and_clear_status (bits 16 and 32). */
+int tilemix_attention_backward_c(const void* Q, const void* K, const void* V, const float* O, const void* dO,
+                                 float* dQ, float* dK, float* dV, float* lse, float* dsum, int heads, int M,
+                                 int N, int d, float score_scale, int causal, void* stream);
+
 /* Device-side watchdog status of the attention kernel on the current device:
  * every pipeline wait in the kernel is bounded; a wait that runs out records a
  * nonzero code here and the kernel returns early instead of hanging. Reading

@@ -1,6 +1,7 @@
 // Drop-in API layer: argument validation with the reference's error contract
 // (src/tilemix.cu:223-278), device checks, and the extern "C" ABI of
-// include/tilemix_c_api.h. Kernels live in quantize.cu and attention.cu.
+// include/tilemix_c_api.h. Kernels live in quantize.cu, attention.cu, policy.cu
+// and backward.cu.
 #include "attention_fused.h"
 #include "kernels.cuh"
 #include "tilemix_c_api.h"
@@ -435,6 +436,27 @@ cudaError_t tilemix_routing_policy(const __half* q_scales, const __half* k_scale
                                stream);
 }
 
+cudaError_t tilemix_attention_backward(const __half* Q, const __half* K, const __half* V, const float* O,
+                                       const __half* dO, float* dQ, float* dK, float* dV, float* lse,
+                                       float* dsum, int heads, int M, int N, int d, float score_scale,
+                                       bool causal, cudaStream_t stream) {
+    if (!Q || !K || !V || !O || !dO || !dQ || !dK || !dV || !lse || !dsum || heads <= 0 || M <= 0 || N <= 0 ||
+        d <= 0 || !std::isfinite(score_scale)) {
+        return cudaErrorInvalidValue;
+    }
+    if (d > tilemix::kBackwardMaxHeadDim || d % 16 != 0) return cudaErrorNotSupported;
+    if (!fits(heads, M, d) || !fits(heads, N, d)) return cudaErrorInvalidValue;
+    const cudaError_t status = check_device();
+    if (status != cudaSuccess) return status;
+    tilemix::AttentionBackwardProblem prob{};
+    prob.q = Q; prob.k = K; prob.v = V; prob.o = O; prob.dout = dO;
+    prob.dq = dQ; prob.dk = dK; prob.dv = dV; prob.lse = lse; prob.dsum = dsum;
+    prob.heads = heads; prob.M = M; prob.N = N; prob.d = d;
+    prob.score_scale = score_scale;
+    prob.causal = causal;
+    return tilemix::launch_attention_backward(prob, stream);
+}
+
 // ---------------------------------------------------------------------- C-ABI
 extern "C" {
 
@@ -569,6 +591,15 @@ int tilemix_watchdog_selftest(const void* Q, const void* K, const void* V, float
                                            static_cast<const __half*>(V), O, heads, M, N, d, score_scale, false,
                                            static_cast<cudaStream_t>(stream), TileMixRouting{}, TileMixQuantized{},
                                            nullptr, 1000ull * wait_limit_us));
+}
+
+int tilemix_attention_backward_c(const void* Q, const void* K, const void* V, const float* O, const void* dO,
+                                 float* dQ, float* dK, float* dV, float* lse, float* dsum, int heads, int M, int N,
+                                 int d, float score_scale, int causal, void* stream) {
+    return static_cast<int>(tilemix_attention_backward(
+        static_cast<const __half*>(Q), static_cast<const __half*>(K), static_cast<const __half*>(V), O,
+        static_cast<const __half*>(dO), dQ, dK, dV, lse, dsum, heads, M, N, d, score_scale, causal != 0,
+        static_cast<cudaStream_t>(stream)));
 }
 
 int tilemix_read_and_clear_status(unsigned int* status) {

@@ -1605,7 +1605,12 @@ cudaError_t read_and_clear_status(unsigned int* status) {
     if (err != cudaSuccess) return err;
     err = cudaMemcpyFromSymbol(status, g_tilemix_status, sizeof(unsigned int));
     if (err != cudaSuccess) return err;
-    return cudaMemcpyToSymbol(g_tilemix_status, &zero, sizeof(unsigned int));
+    err = cudaMemcpyToSymbol(g_tilemix_status, &zero, sizeof(unsigned int));
+    if (err != cudaSuccess) return err;
+    unsigned int backward = 0;
+    err = read_and_clear_backward_status(&backward);
+    *status |= backward;
+    return err;
 }
 
 }  // namespace tilemix

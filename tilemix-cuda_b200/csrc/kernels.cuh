@@ -82,7 +82,32 @@ std::size_t attention_smem_bytes(int d);
 // Launch the fused attention kernel (arguments assumed validated, d <= 128).
 cudaError_t launch_attention(const AttentionProblem& problem, cudaStream_t stream);
 
-// Read and clear the device watchdog word of the current device.
+// Read and clear the device watchdog word of the current device (forward and
+// backward kernels' bits together).
 cudaError_t read_and_clear_status(unsigned int* status);
+
+// Backward of the unrouted attention (backward.cu): fp16 Q, K, V, dO; fp32 O
+// (the forward's output) and fp32 dQ, dK, dV; lse and dsum are [heads][M]
+// fp32 row statistics the launch writes and reads (log2-unit log-sum-exp of
+// score_scale * S, and rowsum(dO * O)). d % 16 == 0, d <= 128, every pointer
+// 16-byte aligned; arguments otherwise assumed validated.
+constexpr int kBackwardMaxHeadDim = 128;
+struct AttentionBackwardProblem {
+    const __half* q;
+    const __half* k;
+    const __half* v;
+    const float* o;
+    const __half* dout;
+    float* dq;
+    float* dk;
+    float* dv;
+    float* lse;
+    float* dsum;
+    int heads, M, N, d;
+    float score_scale;
+    bool causal;
+};
+cudaError_t launch_attention_backward(const AttentionBackwardProblem& problem, cudaStream_t stream);
+cudaError_t read_and_clear_backward_status(unsigned int* status);
 
 }  // namespace tilemix

@@ -108,6 +108,9 @@ def _load():
     lib.tilemix_watchdog_selftest.restype = _I
     lib.tilemix_read_and_clear_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
     lib.tilemix_read_and_clear_status.restype = _I
+    lib.tilemix_attention_backward_c.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I,
+                                                 ctypes.c_float, _I, _P]
+    lib.tilemix_attention_backward_c.restype = _I
     return lib
 
 
@@ -140,7 +143,7 @@ C_ABI_SYMBOLS = (
     "tilemix_quantize_qkv_batched", "tilemix_attention_batched_hinted",
     "tilemix_routing_word_count_c", "tilemix_routing_words_per_row_c",
     "tilemix_reference_shared_bytes", "tilemix_b200_shared_bytes_c",
-    "tilemix_read_and_clear_status", "tilemix_watchdog_selftest",
+    "tilemix_read_and_clear_status", "tilemix_watchdog_selftest", "tilemix_attention_backward_c",
 )
 
 
@@ -402,8 +405,10 @@ def tilemix_attention_routed_noalloc(Q, K, V, O, heads: int, M: int, N: int, d: 
                                                       _stream(stream))
 
 
-# watchdog status bits (which kind of wait gave up)
+# watchdog status bits (which kind of wait gave up): forward kernel roles,
+# then the backward kernels' pipeline waits and drains
 STATUS_PRODUCER, STATUS_MMA, STATUS_SOFTMAX, STATUS_DRAIN = 1, 2, 4, 8
+STATUS_BACKWARD_WAIT, STATUS_BACKWARD_DRAIN = 16, 32
 
 
 def watchdog_selftest(Q, K, V, O, heads: int, M: int, N: int, d: int, score_scale: float,
@@ -413,6 +418,16 @@ def watchdog_selftest(Q, K, V, O, heads: int, M: int, N: int, d: int, score_scal
     the kernel return. O is not valid afterwards. Returns a cudaError_t code."""
     return _native().tilemix_watchdog_selftest(_addr(Q), _addr(K), _addr(V), _addr(O), heads, M, N, d,
                                                float(score_scale), int(wait_limit_us), _stream(stream))
+
+
+def tilemix_attention_backward(Q, K, V, O, dO, dQ, dK, dV, lse, dsum, heads: int, M: int, N: int, d: int,
+                               score_scale: float, causal: bool = False, stream=None) -> int:
+    """Backward of the unrouted attention through the C-ABI: fp16 Q, K, V, dO,
+    fp32 O (the forward's output), fp32 dQ, dK, dV outputs, fp32 [heads, M]
+    lse / dsum workspaces. Returns a cudaError_t code."""
+    return _native().tilemix_attention_backward_c(_addr(Q), _addr(K), _addr(V), _addr(O), _addr(dO), _addr(dQ),
+                                                  _addr(dK), _addr(dV), _addr(lse), _addr(dsum), heads, M, N, d,
+                                                  float(score_scale), int(bool(causal)), _stream(stream))
 
 
 def read_and_clear_status() -> tuple[int, int]:

@@ -19,7 +19,7 @@ LIB = PKG / "libtilemix_b200.so"
 DEMO = PROJECT / "src" / "main.cu"
 DEMO_BIN = PKG / "tilemix_demo"
 
-SOURCES = ["quantize.cu", "attention.cu", "api.cu", "noalloc.cu", "policy.cu"]
+SOURCES = ["quantize.cu", "attention.cu", "api.cu", "noalloc.cu", "policy.cu", "backward.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

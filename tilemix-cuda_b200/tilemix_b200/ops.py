@@ -1,8 +1,9 @@
 """PyTorch operators over the C-ABI: ``torch.ops.tilemix.quantize_qk``,
 ``.attention``, ``.attention_bshd``, ``.quantize_qkv`` + ``.attention_hinted``
 (single-term P from V statistics), ``.quantize_k`` + ``.attention_qfused`` (Q
-quantized inside the kernel) and ``.routing_policy`` (routing words chosen on
-the device).
+quantized inside the kernel), ``.routing_policy`` (routing words chosen on
+the device) and ``.attention_backward`` (gradients of the unrouted attention,
+registered as the autograd formula of ``.attention``).
 
 They call the same extern "C" entry points as the ctypes functions in
 ``tilemix_b200`` (``tilemix_quantize_qk_batched``, ``tilemix_attention_batched``)
@@ -21,9 +22,10 @@ import math
 
 import torch
 
-from . import (TileMixOutput, TileMixQuantized, TileMixRouting, check, quantize_tilemix_k_batched,
+from . import (TileMixOutput, TileMixQuantized, TileMixRouting, _require, check, quantize_tilemix_k_batched,
                quantize_tilemix_qk_batched, quantize_tilemix_qkv_batched, tilemix_attention_batched,
-               tilemix_attention_batched_hinted, tilemix_attention_batched_out, tilemix_attention_batched_qfused,
+               tilemix_attention_backward, tilemix_attention_batched_hinted, tilemix_attention_batched_out,
+               tilemix_attention_batched_qfused,
                tilemix_routing_policy, tilemix_routing_word_count, validate_attention_args, validate_quantize_args)
 
 _Q_ROWS, _K_ROWS = 128, 64   # quantization block rows (include/attention_fused.h:13-14)
@@ -245,6 +247,54 @@ def _(q_scales, k_scales, m, n, key_tiles_per_group, max_scale_product):
     q16, k32 = (m + 15) // 16, (n + 31) // 32
     groups = (k32 + key_tiles_per_group - 1) // key_tiles_per_group
     return q_scales.new_empty((heads * q16 * ((groups + 63) // 64),), dtype=torch.int64)
+
+
+@torch.library.custom_op("tilemix::attention_backward", mutates_args=())
+def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, do: torch.Tensor,
+                       score_scale: float, causal: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients (dq, dk, dv), fp32 of q's / k's / v's shapes, of the unrouted
+    attention o = softmax(score_scale * q k^T [causal]) v, from fp16 q, k, v,
+    the fp32 forward output o and the output gradient do (fp16)."""
+    heads, m, n, d = validate_attention_args(q, k, v)
+    _require(o.shape == q.shape and o.dtype == torch.float32 and o.device == q.device,
+             "o must be a float32 tensor of q's shape on q's device")
+    _require(do.shape == q.shape and do.dtype == torch.float16 and do.device == q.device,
+             "do must be a float16 tensor of q's shape on q's device")
+    q3, k3, v3 = _heads3(q).contiguous(), _heads3(k).contiguous(), _heads3(v).contiguous()
+    o3, do3 = _heads3(o).contiguous(), _heads3(do).contiguous()
+    dq = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    dk = torch.empty(k.shape, dtype=torch.float32, device=q.device)
+    dv = torch.empty(v.shape, dtype=torch.float32, device=q.device)
+    stats = torch.empty((2, heads, m), dtype=torch.float32, device=q.device)
+    check(tilemix_attention_backward(q3, k3, v3, o3, do3, dq, dk, dv, stats[0], stats[1], heads, m, n, d,
+                                     score_scale, causal, torch.cuda.current_stream(q.device)),
+          "tilemix::attention_backward")
+    return dq, dk, dv
+
+
+@attention_backward.register_fake
+def _(q, k, v, o, do, score_scale, causal):
+    return (q.new_empty(q.shape, dtype=torch.float32), k.new_empty(k.shape, dtype=torch.float32),
+            v.new_empty(v.shape, dtype=torch.float32))
+
+
+def _attention_setup_context(ctx, inputs, output):
+    q, k, v, q8, k8, q_scales, k_scales, words, key_tiles_per_group, score_scale, causal = inputs
+    ctx.routed = words is not None
+    ctx.score_scale = score_scale
+    ctx.causal = causal
+    ctx.save_for_backward(q, k, v, output)
+
+
+def _attention_backward(ctx, grad):
+    if ctx.routed:
+        raise NotImplementedError("tilemix::attention has a gradient for the unrouted (all-FP16) call only")
+    q, k, v, o = ctx.saved_tensors
+    dq, dk, dv = attention_backward(q, k, v, o, grad.to(torch.float16), ctx.score_scale, ctx.causal)
+    return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None, None, None, None, None, None
+
+
+attention.register_autograd(_attention_backward, setup_context=_attention_setup_context)
 
 
 def tilemix_attention(q, k, v, words=None, *, key_tiles_per_group: int = 2, score_scale: float | None = None,
