@@ -220,20 +220,29 @@ cudaError_t tilemix_attention_batched_out(const __half* Q, const __half* K, cons
                                           const TileMixRouting& routing = {},
                                           const TileMixQuantized& quantized = {});
 
+// tilemix_attention_batched (unrouted) that also writes lse [heads, M] fp32:
+// log2 of each row's sum of 2^(score_scale * log2(e) * q.k), the statistic
+// tilemix_attention_backward recomputes P from (no reference counterpart).
+cudaError_t tilemix_attention_batched_lse(const __half* Q, const __half* K, const __half* V, float* O, float* lse,
+                                          int heads, int M, int N, int d, float score_scale, bool causal,
+                                          cudaStream_t stream = nullptr);
+
 // Backward of the unrouted attention (no reference counterpart: the reference
 // is forward only). Given fp16 Q, K, V [heads, M|N, d], the fp32 output O of
 // tilemix_attention_batched on them (unrouted, same score_scale and causal)
 // and the fp16 output gradient dO [heads, M, d], writes fp32 dQ [heads, M, d],
 // dK and dV [heads, N, d] of
 //   O = softmax(score_scale * Q K^T [causal: keys <= query]) V.
-// lse and dsum are caller-provided [heads, M] fp32 workspaces that hold, on
-// return, each row's log-sum-exp of score_scale * log2(e) * Q K^T (base 2)
-// and rowsum(dO * O). S, dP and the accumulations are fp32 on the tensor
-// cores; P and dS enter the second products rounded to fp16. Needs
-// d % 16 == 0, d <= 128 and 16-byte aligned pointers (cudaErrorNotSupported /
+// lse and dsum are caller-provided [heads, M] fp32 buffers. With
+// lse_from_forward, lse holds what tilemix_attention_batched_lse wrote for
+// this O and is only read; otherwise the call recomputes each row's
+// log-sum-exp (one more Q K^T pass) and writes it there. dsum receives
+// rowsum(dO * O). S, dP and the accumulations are fp32 on the tensor cores; P
+// and dS enter the second products rounded to fp16. Needs d % 16 == 0,
+// d <= 128 and 16-byte aligned pointers (cudaErrorNotSupported /
 // cudaErrorMisalignedAddress otherwise); other argument errors as
 // tilemix_attention_batched. Two kernel launches, no atomics, deterministic.
 cudaError_t tilemix_attention_backward(const __half* Q, const __half* K, const __half* V, const float* O,
                                        const __half* dO, float* dQ, float* dK, float* dV, float* lse,
                                        float* dsum, int heads, int M, int N, int d, float score_scale,
-                                       bool causal, cudaStream_t stream = nullptr);
+                                       bool causal, bool lse_from_forward = false, cudaStream_t stream = nullptr);

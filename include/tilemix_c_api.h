@@ -200,17 +200,27 @@ size_t tilemix_routing_words_per_row_c(int N, int key_tiles_per_group);
 size_t tilemix_reference_shared_bytes(int d, int quantized);
 size_t tilemix_b200_shared_bytes_c(int d, int quantized);
 
+/* Training forward (no reference counterpart): C form of
+ * tilemix_attention_batched_lse in attention_fused.h, the unrouted
+ * tilemix_attention_batched that also writes lse [heads, M] fp32 (log2 of each
+ * row's sum of 2^(score_scale * log2(e) * q.k)). */
+int tilemix_attention_batched_lse_c(const void* Q, const void* K, const void* V, float* O, float* lse,
+                                    int heads, int M, int N, int d, float score_scale, int causal,
+                                    void* stream);
+
 /* Backward of the unrouted attention (no reference counterpart; the reference
  * is forward only): C form of tilemix_attention_backward in attention_fused.h.
  * Q, K, V, dO fp16; O fp32 (the forward's output on the same inputs, unrouted);
  * dQ [heads, M, d], dK and dV [heads, N, d] fp32 outputs; lse and dsum
- * [heads, M] fp32 workspaces (base-2 log-sum-exp of score_scale * Q K^T rows,
- * rowsum(dO * O)). d % 16 == 0, d <= 128, 16-byte aligned pointers. Its waits
- * are bounded like the forward's and report through
- * tilemix_read_and_clear_status (bits 16 and 32). */
+ * [heads, M] fp32: with lse_from_forward != 0 lse holds what
+ * tilemix_attention_batched_lse_c wrote and is read, otherwise it is computed
+ * and written; dsum receives rowsum(dO * O). d % 16 == 0, d <= 128, 16-byte
+ * aligned pointers. Its waits are bounded like the forward's and report
+ * through tilemix_read_and_clear_status (bits 16 and 32). */
 int tilemix_attention_backward_c(const void* Q, const void* K, const void* V, const float* O, const void* dO,
                                  float* dQ, float* dK, float* dV, float* lse, float* dsum, int heads, int M,
-                                 int N, int d, float score_scale, int causal, void* stream);
+                                 int N, int d, float score_scale, int causal, int lse_from_forward,
+                                 void* stream);
 
 /* Device-side watchdog status of the attention kernel on the current device:
  * every pipeline wait in the kernel is bounded; a wait that runs out records a

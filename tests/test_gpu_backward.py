@@ -52,13 +52,25 @@ def forward(q, k, v, scale, causal):
     return o
 
 
-def backward(q, k, v, o, do, scale, causal):
+def forward_lse(q, k, v, scale, causal):
+    heads, m, d = q.shape
+    o = torch.empty((heads, m, d), dtype=torch.float32, device=DEV)
+    buf, lse = guarded((heads, m))
+    tm.check(tm.tilemix_attention_batched_lse(q, k, v, o, lse, heads, m, k.shape[1], d, scale, causal), "forward")
+    torch.cuda.synchronize()
+    assert torch.all(buf[:4] == GUARD) and torch.all(buf[-4:] == GUARD), "guard overwritten"
+    return o, lse
+
+
+def backward(q, k, v, o, do, scale, causal, lse_in=None):
     heads, m, d = q.shape
     n = k.shape[1]
     bufs = [guarded(s) for s in ((heads, m, d), (heads, n, d), (heads, n, d), (heads, m), (heads, m))]
     dq, dk, dv, lse, dsum = (b[1] for b in bufs)
-    tm.check(tm.tilemix_attention_backward(q, k, v, o, do, dq, dk, dv, lse, dsum, heads, m, n, d, scale, causal),
-             "backward")
+    if lse_in is not None:
+        lse.copy_(lse_in)
+    tm.check(tm.tilemix_attention_backward(q, k, v, o, do, dq, dk, dv, lse, dsum, heads, m, n, d, scale, causal,
+                                           lse_from_forward=lse_in is not None), "backward")
     torch.cuda.synchronize()
     for buf, _ in bufs:
         assert torch.all(buf[:4] == GUARD) and torch.all(buf[-4:] == GUARD), "guard overwritten"
@@ -157,6 +169,7 @@ def test_backward_argument_errors():
     q, k, v, do = inputs(1, 128, 128, 64, seed=1)
     o = forward(q, k, v, 0.125, False)
     dq, dk, dv = (torch.empty((1, 128, 64), dtype=torch.float32, device=DEV) for _ in range(3))
+    assert tm.tilemix_attention_batched_lse(q, k, v, dq, None, 1, 128, 128, 64, 0.125) == 1
     stats = torch.empty((2, 1, 128), dtype=torch.float32, device=DEV)
     call = tm.tilemix_attention_backward
     assert call(q, k, v, o, None, dq, dk, dv, stats[0], stats[1], 1, 128, 128, 64, 0.125) == 1
@@ -178,6 +191,43 @@ def test_autograd_through_the_attention_operator():
     out = torch.ops.tilemix.attention(qg, kg, vg, None, None, None, None, None, 2, scale, True)
     out.backward(do.float())
     _, dq_ref, dk_ref, dv_ref = reference_grads(q, k, v, do, scale, True)
+    for got, ref, name in ((qg.grad, dq_ref, "dQ"), (kg.grad, dk_ref, "dK"), (vg.grad, dv_ref, "dV")):
+        assert got.dtype == torch.float16
+        assert_close(got.float(), ref, name)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("heads,m,n,d,causal", [CASES[2], CASES[3], CASES[6], CASES[7], CASES[8]])
+def test_backward_from_the_forward_lse(heads, m, n, d, causal):
+    q, k, v, do = inputs(heads, m, n, d, seed=heads * 1000 + m + n + d + causal + 7)
+    scale = 1.0 / math.sqrt(d)
+    o, lse_fwd = forward_lse(q, k, v, scale, causal)
+    # the training forward's O is the plain forward's, bit for bit
+    assert torch.equal(o.view(torch.int32), forward(q, k, v, scale, causal).view(torch.int32))
+    s = scale * q.double() @ k.double().transpose(-1, -2)
+    if causal:
+        above = torch.arange(n, device=DEV)[None, :] > torch.arange(m, device=DEV)[:, None]
+        s = s.masked_fill(above, float("-inf"))
+    lse_ref = torch.logsumexp(s, -1) / math.log(2.0)
+    assert (lse_fwd.double() - lse_ref).abs().max().item() <= 1e-4 * max(1.0, lse_ref.abs().max().item())
+    _, dq_ref, dk_ref, dv_ref = reference_grads(q, k, v, do, scale, causal)
+    dq, dk, dv, lse_after, _ = backward(q, k, v, o, do, scale, causal, lse_in=lse_fwd)
+    assert torch.equal(lse_after, lse_fwd)        # read, not rewritten
+    assert_close(dq, dq_ref, "dQ")
+    assert_close(dk, dk_ref, "dK")
+    assert_close(dv, dv_ref, "dV")
+    assert tm.read_and_clear_status() == (0, 0)
+
+
+@pytest.mark.gpu
+def test_autograd_through_the_training_operator():
+    heads, m, n, d = 2, 384, 256, 64
+    q, k, v, do = inputs(heads, m, n, d, seed=33)
+    scale = 0.2
+    qg, kg, vg = (t.clone().requires_grad_() for t in (q, k, v))
+    out, lse = torch.ops.tilemix.attention_lse(qg, kg, vg, scale, False)
+    out.backward(do.float())
+    _, dq_ref, dk_ref, dv_ref = reference_grads(q, k, v, do, scale, False)
     for got, ref, name in ((qg.grad, dq_ref, "dQ"), (kg.grad, dk_ref, "dK"), (vg.grad, dv_ref, "dV")):
         assert got.dtype == torch.float16
         assert_close(got.float(), ref, name)

@@ -55,7 +55,7 @@ cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, fl
                            int M, int N, int d, float score_scale, bool causal, cudaStream_t stream,
                            const TileMixRouting& routing, const TileMixQuantized& quantized,
                            const TileMixOutput* strided = nullptr, unsigned long long watchdog_test_ns = 0,
-                           const __half* v_absmax = nullptr) {
+                           const __half* v_absmax = nullptr, float* lse_out = nullptr) {
     // Same checks, same order as src/tilemix.cu:242-253.
     if (!Q || !K || !V || (!O && !strided) || heads <= 0 || M <= 0 || N <= 0 || d <= 0 ||
         !std::isfinite(score_scale) || routing.key_tiles_per_group <= 0 ||
@@ -106,6 +106,7 @@ cudaError_t attention_impl(const __half* Q, const __half* K, const __half* V, fl
         prob.o_stride_row = strided->stride_row;
     }
     prob.v_absmax = v_absmax;
+    prob.lse_out = lse_out;
     prob.watchdog_test = watchdog_test_ns != 0;
     prob.watchdog_limit_ns = watchdog_test_ns;
     return tilemix::launch_attention(prob, stream);
@@ -436,10 +437,18 @@ cudaError_t tilemix_routing_policy(const __half* q_scales, const __half* k_scale
                                stream);
 }
 
+cudaError_t tilemix_attention_batched_lse(const __half* Q, const __half* K, const __half* V, float* O, float* lse,
+                                          int heads, int M, int N, int d, float score_scale, bool causal,
+                                          cudaStream_t stream) {
+    if (!lse) return cudaErrorInvalidValue;
+    return attention_impl(Q, K, V, O, heads, M, N, d, score_scale, causal, stream, TileMixRouting{},
+                          TileMixQuantized{}, nullptr, 0, nullptr, lse);
+}
+
 cudaError_t tilemix_attention_backward(const __half* Q, const __half* K, const __half* V, const float* O,
                                        const __half* dO, float* dQ, float* dK, float* dV, float* lse,
                                        float* dsum, int heads, int M, int N, int d, float score_scale,
-                                       bool causal, cudaStream_t stream) {
+                                       bool causal, bool lse_from_forward, cudaStream_t stream) {
     if (!Q || !K || !V || !O || !dO || !dQ || !dK || !dV || !lse || !dsum || heads <= 0 || M <= 0 || N <= 0 ||
         d <= 0 || !std::isfinite(score_scale)) {
         return cudaErrorInvalidValue;
@@ -454,6 +463,7 @@ cudaError_t tilemix_attention_backward(const __half* Q, const __half* K, const _
     prob.heads = heads; prob.M = M; prob.N = N; prob.d = d;
     prob.score_scale = score_scale;
     prob.causal = causal;
+    prob.lse_ready = lse_from_forward;
     return tilemix::launch_attention_backward(prob, stream);
 }
 
@@ -593,13 +603,21 @@ int tilemix_watchdog_selftest(const void* Q, const void* K, const void* V, float
                                            nullptr, 1000ull * wait_limit_us));
 }
 
+int tilemix_attention_batched_lse_c(const void* Q, const void* K, const void* V, float* O, float* lse, int heads,
+                                    int M, int N, int d, float score_scale, int causal, void* stream) {
+    return static_cast<int>(tilemix_attention_batched_lse(static_cast<const __half*>(Q), static_cast<const __half*>(K),
+                                                          static_cast<const __half*>(V), O, lse, heads, M, N, d,
+                                                          score_scale, causal != 0,
+                                                          static_cast<cudaStream_t>(stream)));
+}
+
 int tilemix_attention_backward_c(const void* Q, const void* K, const void* V, const float* O, const void* dO,
                                  float* dQ, float* dK, float* dV, float* lse, float* dsum, int heads, int M, int N,
-                                 int d, float score_scale, int causal, void* stream) {
+                                 int d, float score_scale, int causal, int lse_from_forward, void* stream) {
     return static_cast<int>(tilemix_attention_backward(
         static_cast<const __half*>(Q), static_cast<const __half*>(K), static_cast<const __half*>(V), O,
         static_cast<const __half*>(dO), dQ, dK, dV, lse, dsum, heads, M, N, d, score_scale, causal != 0,
-        static_cast<cudaStream_t>(stream)));
+        lse_from_forward != 0, static_cast<cudaStream_t>(stream)));
 }
 
 int tilemix_read_and_clear_status(unsigned int* status) {

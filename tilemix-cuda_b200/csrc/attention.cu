@@ -249,6 +249,7 @@ struct Params {
     const __half* v_absmax;   // optional [heads][k_scale_blocks] max |v| per 64-key block
     std::int8_t* q8_out;      // fused Q: optional Q8 output [heads][M][d]
     __half* q_scales_out;     // fused Q: optional scale output [heads][q_scale_blocks]
+    float* lse_out;           // optional [heads][M] base-2 log-sum-exp of each row's scores
     int q8_vec;          // q8_out takes 16-byte stores (d % 16 == 0, aligned)
     int f16_ksteps, i8_ksteps, pv_n;
     int o_vec;
@@ -1271,7 +1272,13 @@ tilemix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const float m = fmaxf(m_run, m_oth);
                 const float a_me = m_run == -INFINITY ? 0.0f : ex2((m_run - m) * c_exp);
                 const float a_oth = m_oth == -INFINITY ? 0.0f : ex2((m_oth - m) * c_exp);
-                const float inv_l = 1.0f / (l_run * a_me + l_oth * a_oth);
+                const float l_row = l_run * a_me + l_oth * a_oth;
+                const float inv_l = 1.0f / l_row;
+                // log2 of the row's sum of 2^(score_scale log2(e) q.k): the
+                // statistic the backward pass recomputes P from
+                if (p.lse_out && half == 0 && row_valid) {
+                    p.lse_out[static_cast<std::size_t>(head) * p.M + q_row] = m * c_exp + log2f(l_row);
+                }
                 const float w_me = a_me * inv_l, w_oth = a_oth * inv_l;
                 const uint32_t o_oth = tmem + lane_base + kColO + 128u * (half ^ 1);
                 // fp32 O in [heads][M][d], or the strided output's row
@@ -1520,6 +1527,7 @@ cudaError_t launch_attention(const AttentionProblem& prob, cudaStream_t stream) 
     p.v_absmax = prob.v_absmax;
     p.q8_out = prob.q8_out;
     p.q_scales_out = prob.q_scales_out;
+    p.lse_out = prob.lse_out;
     p.q8_vec = (prob.d % 16 == 0 && aligned16(prob.q8_out)) ? 1 : 0;
     p.f16_ksteps = (prob.d + 15) / 16;
     p.i8_ksteps = (prob.d + 31) / 32;

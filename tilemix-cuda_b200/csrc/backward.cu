@@ -4,25 +4,33 @@
 // given dO, for the fp16 Q, K, V the forward takes. Two kernels, no atomics:
 //
 //   row kernel (one CTA per 128-row query tile): pass 1 recomputes S = Q K^T
-//     block by block for the row log-sum-exp (log2 units), D = rowsum(dO * O)
-//     comes from the fp32 O; pass 2 recomputes S and dP = dO V^T, forms
+//     for the row log-sum-exp (log2 units), D = rowsum(dO * O) comes from the
+//     fp32 O; pass 2 recomputes S and dP = dO V^T, forms
 //     dS = P * (dP - D) * score_scale and accumulates dQ += dS K. It writes
 //     dQ and the per-row statistics (LSE, D) the column kernel reads.
 //   column kernel (one CTA per 128-key tile): for every query block that can
 //     see the tile, S^T = K Q^T and dP^T = V dO^T, P^T and dS^T from the row
 //     statistics, then dV += P^T dO and dK += dS^T Q.
 //
-// Both kernels follow the forward's tcgen05 conventions: operand tiles loaded
-// by TMA 128-byte swizzled, S-like products as SS MMAs (kind::f16, fp32 in
-// TMEM, K-major operands), the P/dS products as TS MMAs with the fp16 tile in
-// TMEM (two values per 32-bit column) and an MN-major shared-memory B
-// operand, exactly like the forward's PV. Warps 0-3 own TMEM lanes 0-127 (one
-// thread per row of the CTA's tile) and do the elementwise work, warp 4 issues
-// the TMA loads, warp 5 allocates TMEM and issues every MMA from one elected
-// lane (so the in-order tensor pipe orders an MMA that overwrites a TMEM tile
-// after the MMAs that read it). Every wait is bounded (1 s); a wait that runs
-// out records a status bit (read with tilemix_read_and_clear_status), all
-// roles stop, drain their own in-flight copies and MMAs, and return.
+// Both kernels work in sub-blocks of 64 columns (keys for the row kernel,
+// queries for the column kernel) so that the products of two sub-blocks fit in
+// TMEM next to the accumulators: while the elementwise warps turn sub-block u
+// into P / dS, the tensor core already computes the S and dP of sub-block u + 1
+// into the other buffer, then the accumulation products of u.
+//
+// Conventions follow the forward: operand tiles loaded by TMA 128-byte
+// swizzled; S-like products as SS MMAs (kind::f16, fp32 in TMEM, K-major
+// operands); the P / dS products as TS MMAs with the fp16 tile in TMEM (two
+// values per 32-bit column; the 16 values of a K step in 8 consecutive
+// columns) and an MN-major shared-memory B operand, exactly like the forward's
+// PV. Warps 0-7 do the elementwise work (warp w owns TMEM lanes 32 (w % 4) ..,
+// one thread per row of the CTA's tile, and column half w / 4 of every
+// sub-block), warp 8 issues the TMA loads, warp 9 allocates TMEM and issues
+// every MMA from one elected lane (the in-order tensor pipe then orders an MMA
+// that overwrites a TMEM tile after the MMAs that read it). Every wait is
+// bounded (1 s); a wait that runs out records a status bit (read with
+// tilemix_read_and_clear_status), all roles stop, drain their own in-flight
+// copies and MMAs, and return.
 #include "kernels.cuh"
 #include "sm100.cuh"
 
@@ -42,10 +50,13 @@ namespace {
 using namespace sm100;
 
 constexpr int kRows = 128;                    // tile rows of either kernel (tcgen05 M)
-constexpr int kBwdThreads = 192;              // warps 0-3 elementwise, 4 producer, 5 MMA
-constexpr int kProducer = 4;
-constexpr int kMma = 5;
+constexpr int kSub = 64;                      // sub-block columns
+constexpr int kElemWarps = 8;                 // two per TMEM lane quadrant
+constexpr int kProducer = 8;
+constexpr int kMma = 9;
+constexpr int kBwdThreads = 320;
 constexpr uint32_t kAtom = 128 * 128;         // one 64-column fp16 atom of a 128-row tile
+constexpr uint32_t kHalfRows16 = kSub * 128 / 16;   // 64 tile rows, in 16-byte descriptor units
 constexpr uint64_t kLimitNs = 1000000000ull;
 constexpr uint32_t kSuspend = 200000;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -86,6 +97,9 @@ __device__ __forceinline__ void bw_drain(uint32_t bar, uint32_t parity) {
     __syncwarp();
 }
 
+// Named barrier of the eight elementwise warps.
+__device__ __forceinline__ void elem_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
 struct BwdParams {
     const float* o;            // [heads][M][d] fp32 forward output
     float* dq;                 // [heads][M][d]
@@ -102,7 +116,8 @@ struct BwdParams {
 
 // Shared memory of both kernels: one resident 128-row tile pair (A0, A1) and
 // two stages of a streamed pair (B0, B1), each tile kAtoms atoms of 16 KB,
-// 1024-byte aligned for the 128-byte swizzle; then barriers and small arrays.
+// 1024-byte aligned for the 128-byte swizzle; then row statistics, barriers
+// and the TMEM base / abort flag.
 template <int kAtoms>
 struct BwdSmem {
     static constexpr uint32_t kTile = kAtoms * kAtom;
@@ -110,23 +125,23 @@ struct BwdSmem {
     static constexpr uint32_t kA1 = kA0 + kTile;             // row kernel: dO; column kernel: V
     static constexpr uint32_t kB0 = kA1 + kTile;             // [2] row kernel: K;  column kernel: Q
     static constexpr uint32_t kB1 = kB0 + 2 * kTile;         // [2] row kernel: V;  column kernel: dO
-    static constexpr uint32_t kStats = kB1 + 2 * kTile;      // column kernel: [2][2][128] LSE, D
-    static constexpr uint32_t kBars = kStats + 2 * 2 * kRows * 4;
-    static constexpr uint32_t kNumBars = 16;
+    static constexpr uint32_t kStats = kB1 + 2 * kTile;      // 1024 floats
+    static constexpr uint32_t kBars = kStats + 1024 * 4;
+    static constexpr uint32_t kNumBars = 24;
     static constexpr uint32_t kMisc = kBars + kNumBars * 8;  // TMEM base, abort flag
     static constexpr uint32_t kBytes = kMisc + 16 + 1024;    // + alignment slack
     static_assert(kBytes <= 232448, "shared memory");
 };
 
 // Barriers (same indices in both kernels):
-//   0 A-full (resident pair), 1-2 B-full[stage], 3-4 B-empty[stage],
-//   5 S-full (S and dP of the current block in TMEM), 6 P-ready (the
-//   elementwise warps have written P / dS), 7-8 S-free[buffer] (row kernel,
-//   pass 1: S consumed), 9 done (last accumulation MMA complete), 10 drain
-//   (the MMA warp's own drain), 11-12 S-full[buffer] of pass 1.
-enum : int { kBarA = 0, kBarBFull = 1, kBarBEmpty = 3, kBarS = 5, kBarP = 6, kBarSFree = 7, kBarDone = 9,
-             kBarDrain = 10, kBarS1 = 11 };
-constexpr int kElemWarps = 4;               // arrivals on P-ready and S-free
+//   A-full (resident pair); B-full / B-empty [stage]; S-full [buffer] (S and
+//   dP of a sub-block in TMEM); P-ready [buffer] (the elementwise warps have
+//   written P / dS of it); done (last accumulation MMA complete); drain (the
+//   MMA warp's own drain); row kernel pass 1: S1-full / S1-free [ring slot],
+//   stats (LSE and D of every row known).
+enum : int { kBarA = 0, kBarBFull = 1, kBarBEmpty = 3, kBarS = 5, kBarP = 7, kBarDone = 9, kBarDrain = 10,
+             kBarS1 = 11, kBarS1Free = 15, kBarStats = 19 };
+constexpr int kRing = 4;                      // pass-1 S slots (64 columns each)
 
 // Common prologue: barriers (one per lane of warp 0), abort flag, TMEM (512
 // columns: 1 CTA per SM by shared memory). Returns the TMEM base.
@@ -137,7 +152,9 @@ __device__ __forceinline__ uint32_t bwd_setup(uint8_t* smem, uint32_t sbase) {
     const uint32_t lane = threadIdx.x & 31u;
     if (warp == 0) {
         if (lane < L::kNumBars) {
-            const bool many = lane == kBarP || lane == kBarSFree || lane == kBarSFree + 1;
+            const int i = static_cast<int>(lane);
+            const bool many = (i >= kBarP && i < kBarP + 2) || (i >= kBarS1Free && i < kBarS1Free + kRing) ||
+                              i == kBarStats;
             mbar_init(sbase + L::kBars + 8u * lane, many ? kElemWarps : 1);
         }
         if (lane == 0) *reinterpret_cast<volatile int*>(smem + L::kMisc + 4) = 0;
@@ -154,10 +171,11 @@ __device__ __forceinline__ uint32_t bwd_setup(uint8_t* smem, uint32_t sbase) {
     return *reinterpret_cast<volatile uint32_t*>(smem + L::kMisc);
 }
 
-// D (128 x 128, fp32 in TMEM) = A B^T over d: A and B 128-row K-major tiles.
-__device__ __forceinline__ void mma_abt(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t dhi, uint32_t idesc,
-                                        int ksteps) {
+// D (128 x 64, fp32 in TMEM) = A B^T over d: A a 128-row K-major tile, B 64
+// rows of one (b_lo already offset to the half).
+__device__ __forceinline__ void mma_sub(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t dhi, int ksteps) {
     const uint32_t none[4] = {0u, 0u, 0u, 0u};
+    const uint32_t idesc = idesc_f16_f32(kRows, kSub, false);
     mma_f16_ss_w<0>(d_tmem, a_lo, b_lo, dhi, idesc, none);
     for (int ks = 1; ks < ksteps; ++ks) {
         const uint32_t ko = static_cast<uint32_t>((ks >> 2) * (kAtom >> 4) + (ks & 3) * 2);
@@ -165,18 +183,23 @@ __device__ __forceinline__ void mma_abt(uint32_t d_tmem, uint32_t a_lo, uint32_t
     }
 }
 
-// D (128 x d) (+)= T B: T a 128 x 128 fp16 tile in TMEM (two values per
-// column, 16 rows of B per 8 columns), B a 128-row tile read MN-major.
-__device__ __forceinline__ void mma_tb(uint32_t d_tmem, uint32_t t_tmem, uint32_t b_lo, uint32_t dhi,
-                                       uint32_t idesc, bool accumulate) {
-    for (int t = 0; t < kRows / 16; ++t) {
-        mma_f16_ts_w(d_tmem, t_tmem + 8u * static_cast<uint32_t>(t), b_lo + 128u * static_cast<uint32_t>(t), dhi,
-                     idesc, (accumulate || t > 0) ? 1u : 0u);
+// D (128 x d) (+)= T B over a 64-column sub-block: T fp16 in TMEM as the
+// elementwise warps write it (column half ch at +32 ch, 16 values per 8
+// columns), B 64 rows of a tile read MN-major (b_lo offset to the half).
+__device__ __forceinline__ void mma_acc(uint32_t d_tmem, uint32_t t_tmem, uint32_t b_lo, uint32_t dhi,
+                                        uint32_t idesc, bool accumulate) {
+    #pragma unroll
+    for (int t = 0; t < kSub / 16; ++t) {
+        mma_f16_ts_w(d_tmem, t_tmem + 32u * static_cast<uint32_t>(t >> 1) + 8u * static_cast<uint32_t>(t & 1),
+                     b_lo + 128u * static_cast<uint32_t>(t), dhi, idesc, (accumulate || t > 0) ? 1u : 0u);
     }
 }
 
-// Row kernel: one CTA per (head, 128-row query tile); heaviest tiles first.
-template <int kAtoms>
+// Row kernel: one CTA per (head, 128-row query tile); heaviest causal tiles
+// first. TMEM: pass 1 S slots at 64 s (s < 4); pass 2 buffers at 0 and 128
+// (S in the first 64 columns, dS written over it; dP in the next 64); dQ at
+// 256.
+template <int kAtoms, bool kHaveLse>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -195,10 +218,13 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     const int qt = p.q_tiles - 1 - bid / p.heads;
     const int head = bid % p.heads;
     const int nblk = p.causal ? min(p.k_tiles, qt + 1) : p.k_tiles;
+    const int nsub = 2 * nblk;                    // 64-key sub-blocks
+    const int npass1 = kHaveLse ? 0 : nblk;       // K blocks loaded for pass 1
     const uint32_t tmem = bwd_setup<kAtoms>(smem, sbase);
 
     if (warp == kProducer) {
-        // Q and dO once; K (pass 1), then K and V (pass 2) through two stages.
+        // Q and dO once; K (pass 1, unless the forward's LSE is given), then
+        // K and V (pass 2) through two stages.
         if (elect_one()) {
             mbar_arrive_expect_tx(bar(kBarA), 2 * L::kTile);
             for (int a = 0; a < kAtoms; ++a) {
@@ -208,10 +234,10 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
         __syncwarp();
         int issued = 0;
-        for (int l = 0; l < 2 * nblk; ++l) {
+        for (int l = 0; l < npass1 + nblk; ++l) {
             const int s = l & 1;
-            const bool pass2 = l >= nblk;
-            const int j = pass2 ? l - nblk : l;
+            const bool pass2 = l >= npass1;
+            const int j = pass2 ? l - npass1 : l;
             if (!bw_wait(bar(kBarBEmpty + s), ((l >> 1) & 1) ^ 1, abort_flag)) break;
             if (elect_one()) {
                 mbar_arrive_expect_tx(bar(kBarBFull + s), (pass2 ? 2u : 1u) * L::kTile);
@@ -231,76 +257,85 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         for (int l = max(0, issued - 2); l < issued; ++l) bw_drain(bar(kBarBFull + (l & 1)), (l >> 1) & 1);
     } else if (warp == kMma) {
         const uint32_t dhi = smem_desc_sw128_hi(1024);
-        const uint32_t idesc_s = idesc_f16_f32(kRows, kRows, false);
         const uint32_t idesc_o = idesc_f16_f32(kRows, p.d, true);
         const int ksteps = p.d / 16;
         const uint32_t q_lo = smem_desc_sw128_lo(sbase + L::kA0, 16);
         const uint32_t do_lo = smem_desc_sw128_lo(sbase + L::kA1, 16);
+        auto k_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, lbo); };
+        auto v_lo = [&](int s) { return smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, 16); };
         bool ok = bw_wait(bar(kBarA), 0, abort_flag);
-        // pass 1: S(j) = Q K(j)^T into TMEM buffer j & 1
-        for (int j = 0; ok && j < nblk; ++j) {
-            const int s = j & 1;
-            ok = bw_wait(bar(kBarBFull + s), (j >> 1) & 1, abort_flag);
-            if (ok && j >= 2) ok = bw_wait(bar(kBarSFree + (j & 1)), ((j - 2) >> 1) & 1, abort_flag);
+        // pass 1: S of sub-block v (keys 64 v ..) into ring slot v % kRing
+        for (int v = 0; ok && v < 2 * npass1; ++v) {
+            const int j = v >> 1, h = v & 1, s = j & 1;
+            if (h == 0) ok = bw_wait(bar(kBarBFull + s), (j >> 1) & 1, abort_flag);
+            if (ok && v >= kRing) ok = bw_wait(bar(kBarS1Free + v % kRing), ((v - kRing) / kRing) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
             if (elect_one()) {
-                mma_abt(tmem + 128u * static_cast<uint32_t>(j & 1), q_lo,
-                        smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, 16), dhi, idesc_s, ksteps);
-                tc_commit(bar(kBarS1 + (j & 1)));
-                tc_commit(bar(kBarBEmpty + s));
-            }
-            __syncwarp();
-        }
-        // pass 2 reuses both buffers: wait until the last pass-1 blocks are read
-        for (int b = 0; ok && b < 2; ++b) {
-            const int jb = nblk - 1 - b;
-            if (jb >= 0) ok = bw_wait(bar(kBarSFree + (jb & 1)), (jb >> 1) & 1, abort_flag);
-        }
-        // pass 2: S = Q K^T (columns 0-127), dP = dO V^T (128-255); then, once
-        // the elementwise warps have written dS over S, dQ += dS K (256-...)
-        for (int j = 0; ok && j < nblk; ++j) {
-            const int l = nblk + j, s = l & 1;
-            ok = bw_wait(bar(kBarBFull + s), (l >> 1) & 1, abort_flag);
-            if (!ok) break;
-            tc_fence_after();
-            if (elect_one()) {
-                mma_abt(tmem, q_lo, smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, 16), dhi, idesc_s, ksteps);
-                mma_abt(tmem + 128u, do_lo, smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, 16), dhi, idesc_s,
+                mma_sub(tmem + 64u * static_cast<uint32_t>(v % kRing), q_lo, k_lo(s, 16) + kHalfRows16 * h, dhi,
                         ksteps);
-                tc_commit(bar(kBarS));
+                tc_commit(bar(kBarS1 + v % kRing));
+                if (h == 1) tc_commit(bar(kBarBEmpty + s));
             }
             __syncwarp();
-            ok = bw_wait(bar(kBarP), j & 1, abort_flag);
-            if (!ok) break;
-            tc_fence_after();
-            if (elect_one()) {
-                mma_tb(tmem + 256u, tmem, smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, kAtom), dhi, idesc_o,
-                       j > 0);
-                tc_commit(bar(kBarBEmpty + s));
-                if (j == nblk - 1) tc_commit(bar(kBarDone));
+        }
+        // pass 2 starts once every row's LSE is known (the pass-1 slots have
+        // then been read). S(v + 1) and dP(v + 1) go into the other buffer
+        // before dQ += dS(v) K, so the tensor core works while the
+        // elementwise warps form dS(v + 1).
+        if (!kHaveLse && ok) ok = bw_wait(bar(kBarStats), 0, abort_flag);
+        for (int v = -1; ok && v < nsub; ++v) {
+            const int nv = v + 1;
+            if (nv < nsub) {
+                const int l = npass1 + (nv >> 1), s = l & 1, h = nv & 1;
+                if (h == 0) ok = bw_wait(bar(kBarBFull + s), (l >> 1) & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                if (elect_one()) {
+                    const uint32_t buf = tmem + 128u * static_cast<uint32_t>(nv & 1);
+                    mma_sub(buf, q_lo, k_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
+                    mma_sub(buf + 64u, do_lo, v_lo(s) + kHalfRows16 * h, dhi, ksteps);
+                    tc_commit(bar(kBarS + (nv & 1)));
+                }
+                __syncwarp();
             }
-            __syncwarp();
+            if (v >= 0) {
+                const int l = npass1 + (v >> 1), s = l & 1, h = v & 1;
+                ok = bw_wait(bar(kBarP + (v & 1)), (v >> 1) & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                if (elect_one()) {
+                    mma_acc(tmem + 256u, tmem + 128u * static_cast<uint32_t>(v & 1),
+                            k_lo(s, kAtom) + kHalfRows16 * h, dhi, idesc_o, v > 0);
+                    if (h == 1) tc_commit(bar(kBarBEmpty + s));
+                    if (v == nsub - 1) tc_commit(bar(kBarDone));
+                }
+                __syncwarp();
+            }
         }
         if (lane == 0) tc_commit(bar(kBarDrain));
         __syncwarp();
         bw_drain(bar(kBarDrain), 0);
     } else {
-        // elementwise: thread = query row = TMEM lane
-        const int r = static_cast<int>(threadIdx.x);
+        // elementwise: thread = (query row = TMEM lane, column half ch)
+        const int quad = warp & 3, ch = warp >> 2;
+        const int r = quad * 32 + static_cast<int>(lane);
         const int row = qt * kRows + r;
         const bool row_ok = row < p.M;
-        const uint32_t lb = static_cast<uint32_t>(warp * 32) << 16;
+        const uint32_t lb = static_cast<uint32_t>(quad * 32) << 16;
+        float* stats = reinterpret_cast<float*>(smem + L::kStats);   // [ch][max, sum, D][128]
         bool ok = bw_wait(bar(kBarA), 0, abort_flag);
-        // D = rowsum(dO * O): dO from the swizzled tile, O (fp32) from global
+        // D = rowsum(dO * O) over this half's columns: dO from the swizzled
+        // tile, O (fp32) from global
         float dsum = 0.0f;
         if (ok && row_ok) {
             const float* orow = p.o + (static_cast<std::size_t>(head) * p.M + row) * p.d;
-            for (int c8 = 0; c8 < p.d / 8; ++c8) {
+            const int h8 = p.d / 16;   // 8-column chunks per half (d % 16 == 0)
+            for (int c8 = ch * h8; c8 < (ch + 1) * h8; ++c8) {
                 const int atom = c8 >> 3, c = c8 & 7;
-                const uint4 h = *reinterpret_cast<const uint4*>(smem + L::kA1 + atom * kAtom + r * 128 +
-                                                                ((c ^ (r & 7)) << 4));
-                const __half2* hh = reinterpret_cast<const __half2*>(&h);
+                const uint4 hv = *reinterpret_cast<const uint4*>(smem + L::kA1 + atom * kAtom + r * 128 +
+                                                                 ((c ^ (r & 7)) << 4));
+                const __half2* hh = reinterpret_cast<const __half2*>(&hv);
                 const float4 o0 = *reinterpret_cast<const float4*>(orow + 8 * c8);
                 const float4 o1 = *reinterpret_cast<const float4*>(orow + 8 * c8 + 4);
                 const float2 f0 = __half22float2(hh[0]), f1 = __half22float2(hh[1]);
@@ -311,87 +346,127 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 dsum = fmaf(f3.x, o1.z, dsum); dsum = fmaf(f3.y, o1.w, dsum);
             }
         }
-        // pass 1: running max and sum of 2^(c S) over the row's visible keys
-        float m = -INFINITY, l = 0.0f;
-        for (int j = 0; ok && j < nblk; ++j) {
-            ok = bw_wait(bar(kBarS1 + (j & 1)), (j >> 1) & 1, abort_flag);
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t sb = tmem + lb + 128u * static_cast<uint32_t>(j & 1);
-            #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+        // A sub-block needs no mask when all its keys exist and (causal) lie
+        // at or before the tile's first row.
+        auto full_sub = [&](int v) {
+            const int key_end = (v + 1) * kSub;
+            return key_end <= p.N && (!p.causal || key_end - 1 <= qt * kRows);
+        };
+        float lse = 0.0f;
+        if constexpr (!kHaveLse) {
+            // pass 1: running max and sum of 2^(c S) over this half's visible keys
+            float m = -INFINITY, l = 0.0f;
+            for (int v = 0; ok && v < nsub; ++v) {
+                ok = bw_wait(bar(kBarS1 + v % kRing), (v / kRing) & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
                 uint32_t x[32];
-                tmem_ld32(sb + 32u * c, x);
+                tmem_ld32(tmem + lb + 64u * static_cast<uint32_t>(v % kRing) + 32u * ch, x);
                 tc_wait_ld();
-                const int key0 = j * kRows + 32 * c;
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kBarS1Free + v % kRing));
+                const int key0 = v * kSub + 32 * ch;
+                const bool full = full_sub(v);
                 float s2[32];
                 float cm = -INFINITY;
                 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int key = key0 + i;
-                    const bool valid = key < p.N && (!p.causal || key <= row);
-                    s2[i] = valid ? __uint_as_float(x[i]) * p.c : -INFINITY;
-                    cm = fmaxf(cm, s2[i]);
+                for (int i = 0; i < 32; i += 2) {
+                    const float2 t = __fmul2_rn(make_float2(__uint_as_float(x[i]), __uint_as_float(x[i + 1])),
+                                                make_float2(p.c, p.c));
+                    s2[i] = t.x;
+                    s2[i + 1] = t.y;
                 }
+                if (!full) {
+                    #pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int key = key0 + i;
+                        if (!(key < p.N && (!p.causal || key <= row))) s2[i] = -INFINITY;
+                    }
+                }
+                #pragma unroll
+                for (int i = 0; i < 32; i += 4) cm = fmaxf(cm, max3f(s2[i], s2[i + 1], fmaxf(s2[i + 2], s2[i + 3])));
                 const float mn = fmaxf(m, cm);
                 if (mn > -INFINITY) {
-                    float sum = 0.0f;
+                    float sum0 = 0.0f, sum1 = 0.0f;
                     #pragma unroll
-                    for (int i = 0; i < 32; ++i) sum += ex2(s2[i] - mn);
-                    l = l * ex2(m - mn) + sum;
+                    for (int i = 0; i < 32; i += 2) {
+                        sum0 += ex2(s2[i] - mn);
+                        sum1 += ex2(s2[i + 1] - mn);
+                    }
+                    l = (m > -INFINITY ? l * ex2(m - mn) : 0.0f) + (sum0 + sum1);
                     m = mn;
                 }
             }
-            tc_fence_before();
+            // combine the two halves of each row; every elementwise warp
+            // reaches this barrier exactly once, aborted or not
+            stats[(ch * 3 + 0) * kRows + r] = m;
+            stats[(ch * 3 + 1) * kRows + r] = l;
+            stats[(ch * 3 + 2) * kRows + r] = dsum;
+            elem_sync();
+            const int other = 1 - ch;
+            const float m2 = stats[(other * 3 + 0) * kRows + r];
+            const float l2 = stats[(other * 3 + 1) * kRows + r];
+            const float mm = fmaxf(m, m2);
+            const float lsum =
+                (m > -INFINITY ? l * ex2(m - mm) : 0.0f) + (m2 > -INFINITY ? l2 * ex2(m2 - mm) : 0.0f);
+            lse = mm + log2f(lsum);
+            dsum += stats[(other * 3 + 2) * kRows + r];
+            if (ok && row_ok && ch == 0) p.lse[static_cast<std::size_t>(head) * p.M + row] = lse;
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarSFree + (j & 1)));
+            if (lane == 0) mbar_arrive(bar(kBarStats));
+        } else {
+            // the forward's LSE; D's two halves combined
+            stats[(ch * 3 + 2) * kRows + r] = dsum;
+            elem_sync();
+            dsum += stats[((1 - ch) * 3 + 2) * kRows + r];
+            if (row_ok) lse = p.lse[static_cast<std::size_t>(head) * p.M + row];
         }
-        const float lse = m + log2f(l);
-        if (ok && row_ok) {
-            p.lse[static_cast<std::size_t>(head) * p.M + row] = lse;
-            p.dsum[static_cast<std::size_t>(head) * p.M + row] = dsum;
-        }
-        // pass 2: dS = P (dP - D) * score_scale, fp16, over S's columns
-        for (int j = 0; ok && j < nblk; ++j) {
-            ok = bw_wait(bar(kBarS), j & 1, abort_flag);
+        if (ok && row_ok && ch == 0) p.dsum[static_cast<std::size_t>(head) * p.M + row] = dsum;
+        // pass 2: dS = P (dP - D) * score_scale, fp16, over this half's S
+        // columns; P = 2^(c S - LSE)
+        const float2 c2 = make_float2(p.c, p.c), nl2 = make_float2(-lse, -lse);
+        const float2 sc2 = make_float2(p.scale, p.scale);
+        const float2 nd2 = make_float2(-dsum * p.scale, -dsum * p.scale);
+        for (int v = 0; ok && v < nsub; ++v) {
+            ok = bw_wait(bar(kBarS + (v & 1)), (v >> 1) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t sb = tmem + lb;
-            #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                uint32_t x[32], y[32];
-                tmem_ld32(sb + 32u * c, x);
-                tmem_ld32(sb + 128u + 32u * c, y);
-                tc_wait_ld();
-                const int key0 = j * kRows + 32 * c;
-                uint32_t ds[16];
-                #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    float v[2];
-                    #pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int key = key0 + 2 * i + e;
-                        const bool valid = key < p.N && (!p.causal || key <= row);
-                        const float pr = valid ? ex2(__uint_as_float(x[2 * i + e]) * p.c - lse) : 0.0f;
-                        v[e] = pr * (__uint_as_float(y[2 * i + e]) - dsum) * p.scale;
-                    }
-                    ds[i] = pack_half2(v[0], v[1]);
+            const uint32_t buf = tmem + lb + 128u * static_cast<uint32_t>(v & 1) + 32u * ch;
+            uint32_t x[32], y[32];
+            tmem_ld32(buf, x);
+            tmem_ld32(buf + 64u, y);
+            tc_wait_ld();
+            const int key0 = v * kSub + 32 * ch;
+            const bool full = full_sub(v);
+            uint32_t ds[16];
+            #pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                float2 t = __ffma2_rn(make_float2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])), c2, nl2);
+                if (!full) {
+                    const int key = key0 + 2 * i;
+                    if (!(key < p.N && (!p.causal || key <= row))) t.x = -INFINITY;
+                    if (!(key + 1 < p.N && (!p.causal || key + 1 <= row))) t.y = -INFINITY;
                 }
-                // columns [16c, 16c + 16) were read by this or the previous chunk
-                tmem_st16(sb + 16u * c, ds);
+                const float2 pr = make_float2(ex2(t.x), ex2(t.y));
+                const float2 g =
+                    __ffma2_rn(make_float2(__uint_as_float(y[2 * i]), __uint_as_float(y[2 * i + 1])), sc2, nd2);
+                const float2 dv = __fmul2_rn(pr, g);
+                ds[i] = pack_half2(dv.x, dv.y);
             }
+            tmem_st16(buf, ds);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarP));
+            if (lane == 0) mbar_arrive(bar(kBarP + (v & 1)));
         }
-        // dQ out
+        // dQ out: 32-column chunks alternate between the two halves
         if (ok) ok = bw_wait(bar(kBarDone), 0, abort_flag);
         if (ok) {
             tc_fence_after();
             float* out = p.dq + (static_cast<std::size_t>(head) * p.M + row) * p.d;
             #pragma unroll 1
-            for (int c = 0; c < p.d; c += 32) {
+            for (int c = 32 * ch; c < p.d; c += 64) {
                 uint32_t x[32];
                 tmem_ld32(tmem + lb + 256u + static_cast<uint32_t>(c), x);
                 tc_wait_ld();
@@ -417,9 +492,10 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 }
 
 // Column kernel: one CTA per (head, 128-key tile); K and V stay resident, the
-// query blocks that see the tile stream through (Q, dO) stages. TMEM: S^T in
-// columns 0-127 (P^T written over it), dP^T in 128-255 (dS^T over it), dV in
-// 256-383, dK in 384-511.
+// query blocks that see the tile stream through (Q, dO) stages, each as two
+// 64-query sub-blocks. TMEM: buffers at 0 and 128 (S^T in the first 64
+// columns with P^T written over it, dP^T in the next 64 with dS^T over it), dV
+// at 256, dK at 384.
 template <int kAtoms>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
@@ -441,6 +517,7 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     const int head = bid % p.heads;
     const int i0 = p.causal ? kt : 0;             // first query block that sees the tile
     const int nq = p.q_tiles - i0;                // may be <= 0 (causal, keys past the last query)
+    const int nsub = nq > 0 ? 2 * nq : 0;         // 64-query sub-blocks
     const uint32_t tmem = bwd_setup<kAtoms>(smem, sbase);
 
     if (warp == kProducer) {
@@ -475,103 +552,128 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     } else if (warp == kMma) {
         if (nq > 0) {
             const uint32_t dhi = smem_desc_sw128_hi(1024);
-            const uint32_t idesc_s = idesc_f16_f32(kRows, kRows, false);
             const uint32_t idesc_o = idesc_f16_f32(kRows, p.d, true);
             const int ksteps = p.d / 16;
             const uint32_t k_lo = smem_desc_sw128_lo(sbase + L::kA0, 16);
             const uint32_t v_lo = smem_desc_sw128_lo(sbase + L::kA1, 16);
+            auto q_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, lbo); };
+            auto do_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, lbo); };
             bool ok = bw_wait(bar(kBarA), 0, abort_flag);
-            for (int b = 0; ok && b < nq; ++b) {
-                const int s = b & 1;
-                ok = bw_wait(bar(kBarBFull + s), (b >> 1) & 1, abort_flag);
-                if (!ok) break;
-                tc_fence_after();
-                if (elect_one()) {
-                    // S^T = K Q^T, dP^T = V dO^T (over d)
-                    mma_abt(tmem, k_lo, smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, 16), dhi, idesc_s, ksteps);
-                    mma_abt(tmem + 128u, v_lo, smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, 16), dhi, idesc_s,
-                            ksteps);
-                    tc_commit(bar(kBarS));
+            // S^T(u + 1), dP^T(u + 1) into the other buffer, then dV, dK
+            // from sub-block u once its P^T / dS^T are written
+            for (int u = -1; ok && u < nsub; ++u) {
+                const int nu = u + 1;
+                if (nu < nsub) {
+                    const int b = nu >> 1, s = b & 1, h = nu & 1;
+                    if (h == 0) ok = bw_wait(bar(kBarBFull + s), (b >> 1) & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    if (elect_one()) {
+                        const uint32_t buf = tmem + 128u * static_cast<uint32_t>(nu & 1);
+                        mma_sub(buf, k_lo, q_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
+                        mma_sub(buf + 64u, v_lo, do_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
+                        tc_commit(bar(kBarS + (nu & 1)));
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
-                ok = bw_wait(bar(kBarP), b & 1, abort_flag);
-                if (!ok) break;
-                tc_fence_after();
-                if (elect_one()) {
-                    // dV += P^T dO, dK += dS^T Q (over the block's queries)
-                    mma_tb(tmem + 256u, tmem, smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, kAtom), dhi, idesc_o,
-                           b > 0);
-                    mma_tb(tmem + 384u, tmem + 128u, smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, kAtom), dhi,
-                           idesc_o, b > 0);
-                    tc_commit(bar(kBarBEmpty + s));
-                    if (b == nq - 1) tc_commit(bar(kBarDone));
+                if (u >= 0) {
+                    const int b = u >> 1, s = b & 1, h = u & 1;
+                    ok = bw_wait(bar(kBarP + (u & 1)), (u >> 1) & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    if (elect_one()) {
+                        const uint32_t buf = tmem + 128u * static_cast<uint32_t>(u & 1);
+                        mma_acc(tmem + 256u, buf, do_lo(s, kAtom) + kHalfRows16 * h, dhi, idesc_o, u > 0);
+                        mma_acc(tmem + 384u, buf + 64u, q_lo(s, kAtom) + kHalfRows16 * h, dhi, idesc_o, u > 0);
+                        if (h == 1) tc_commit(bar(kBarBEmpty + s));
+                        if (u == nsub - 1) tc_commit(bar(kBarDone));
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
             if (lane == 0) tc_commit(bar(kBarDrain));
             __syncwarp();
             bw_drain(bar(kBarDrain), 0);
         }
     } else {
-        // elementwise: thread = key row = TMEM lane
-        const int r = static_cast<int>(threadIdx.x);
+        // elementwise: thread = (key row = TMEM lane, query half ch)
+        const int quad = warp & 3, ch = warp >> 2;
+        const int r = quad * 32 + static_cast<int>(lane);
         const int key = kt * kRows + r;
-        const uint32_t lb = static_cast<uint32_t>(warp * 32) << 16;
-        float* stats = reinterpret_cast<float*>(smem + L::kStats);
+        const uint32_t lb = static_cast<uint32_t>(quad * 32) << 16;
+        float* stats = reinterpret_cast<float*>(smem + L::kStats);   // [block & 1][-LSE, -D scale][128]
+        const float2 c2 = make_float2(p.c, p.c), sc2 = make_float2(p.scale, p.scale);
         bool ok = true;
-        // Every elementwise warp runs all nq iterations (the named barrier
-        // needs all four); after an abort they only pass the barrier.
-        for (int b = 0; b < nq; ++b) {
-            const int i = i0 + b;
-            // the block's row statistics, staged once for all 128 threads
-            float* lse_s = stats + (b & 1) * 2 * kRows;
-            float* d_s = lse_s + kRows;
-            const int q = i * kRows + r;
-            lse_s[r] = q < p.M ? p.lse[static_cast<std::size_t>(head) * p.M + q] : 0.0f;
-            d_s[r] = q < p.M ? p.dsum[static_cast<std::size_t>(head) * p.M + q] : 0.0f;
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (ok) ok = bw_wait(bar(kBarS), b & 1, abort_flag);
+        // Every elementwise warp runs all iterations (the named barrier needs
+        // all eight); after an abort they only pass the barrier.
+        for (int u = 0; u < nsub; ++u) {
+            const int b = u >> 1, h = u & 1, i = i0 + b;
+            const float* nl_s = stats + (b & 1) * 2 * kRows;
+            const float* nd_s = nl_s + kRows;
+            if (h == 0) {
+                // the block's row statistics, staged once: thread t < 128
+                // stores -LSE of query t, thread 128 + t its -D * scale
+                const int t = static_cast<int>(threadIdx.x);
+                const int q = i * kRows + (t & (kRows - 1));
+                float val = 0.0f;
+                if (q < p.M) {
+                    const std::size_t at = static_cast<std::size_t>(head) * p.M + q;
+                    val = t < kRows ? -p.lse[at] : -p.dsum[at] * p.scale;
+                }
+                stats[(b & 1) * 2 * kRows + t] = val;
+                elem_sync();
+            }
+            if (ok) ok = bw_wait(bar(kBarS + (u & 1)), (u >> 1) & 1, abort_flag);
             if (!ok) continue;
             tc_fence_after();
-            const uint32_t sb = tmem + lb;
-            #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                uint32_t x[32], y[32];
-                tmem_ld32(sb + 32u * c, x);
-                tmem_ld32(sb + 128u + 32u * c, y);
-                tc_wait_ld();
-                const int q0 = i * kRows + 32 * c;
-                uint32_t pt[16], dst[16];
+            const uint32_t buf = tmem + lb + 128u * static_cast<uint32_t>(u & 1) + 32u * ch;
+            uint32_t x[32], y[32];
+            tmem_ld32(buf, x);
+            tmem_ld32(buf + 64u, y);
+            tc_wait_ld();
+            const int col0 = kSub * h + 32 * ch;          // query within the block
+            const int q0 = i * kRows + col0;
+            // no mask when every query of the sub-block exists and (causal)
+            // sees every key of the tile
+            const bool full = i * kRows + kSub * (h + 1) <= p.M && (!p.causal || kt * kRows + kRows - 1 <= i * kRows + kSub * h);
+            uint32_t pt[16], dst[16];
+            #pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+                const float4 nl = *reinterpret_cast<const float4*>(nl_s + col0 + 2 * e);
+                const float4 nd = *reinterpret_cast<const float4*>(nd_s + col0 + 2 * e);
                 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    float pv[2], dv[2];
-                    #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int col = 32 * c + 2 * e + h;
-                        const int qq = q0 + 2 * e + h;
-                        const bool valid = qq < p.M && (!p.causal || key <= qq);
-                        const float pr = valid ? ex2(__uint_as_float(x[2 * e + h]) * p.c - lse_s[col]) : 0.0f;
-                        pv[h] = pr;
-                        dv[h] = pr * (__uint_as_float(y[2 * e + h]) - d_s[col]) * p.scale;
+                for (int f = 0; f < 2; ++f) {
+                    const int c = 2 * (e + f);
+                    float2 t = __ffma2_rn(make_float2(__uint_as_float(x[c]), __uint_as_float(x[c + 1])), c2,
+                                          f == 0 ? make_float2(nl.x, nl.y) : make_float2(nl.z, nl.w));
+                    if (!full) {
+                        if (!(q0 + c < p.M && (!p.causal || key <= q0 + c))) t.x = -INFINITY;
+                        if (!(q0 + c + 1 < p.M && (!p.causal || key <= q0 + c + 1))) t.y = -INFINITY;
                     }
-                    pt[e] = pack_half2(pv[0], pv[1]);
-                    dst[e] = pack_half2(dv[0], dv[1]);
+                    const float2 pr = make_float2(ex2(t.x), ex2(t.y));
+                    const float2 g = __ffma2_rn(make_float2(__uint_as_float(y[c]), __uint_as_float(y[c + 1])), sc2,
+                                                f == 0 ? make_float2(nd.x, nd.y) : make_float2(nd.z, nd.w));
+                    const float2 dv = __fmul2_rn(pr, g);
+                    pt[e + f] = pack_half2(pr.x, pr.y);
+                    dst[e + f] = pack_half2(dv.x, dv.y);
                 }
-                tmem_st16(sb + 16u * c, pt);
-                tmem_st16(sb + 128u + 16u * c, dst);
             }
+            tmem_st16(buf, pt);
+            tmem_st16(buf + 64u, dst);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarP));
+            if (lane == 0) mbar_arrive(bar(kBarP + (u & 1)));
         }
-        if (ok && key < p.N) {
+        if (key < p.N) {
             float* dv_out = p.dv + (static_cast<std::size_t>(head) * p.N + key) * p.d;
             float* dk_out = p.dk + (static_cast<std::size_t>(head) * p.N + key) * p.d;
             if (nq <= 0) {
-                for (int c = 0; c < p.d; c += 4) {
-                    *reinterpret_cast<float4*>(dv_out + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-                    *reinterpret_cast<float4*>(dk_out + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int c = 32 * ch; c < p.d; c += 64) {
+                    for (int e = 0; e < 32 && c + e < p.d; e += 4) {
+                        *reinterpret_cast<float4*>(dv_out + c + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+                        *reinterpret_cast<float4*>(dk_out + c + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
                 }
             }
         }
@@ -582,7 +684,7 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             for (int part = 0; part < 2; ++part) {
                 float* out = (part == 0 ? p.dv : p.dk) + (static_cast<std::size_t>(head) * p.N + key) * p.d;
                 #pragma unroll 1
-                for (int c = 0; c < p.d; c += 32) {
+                for (int c = 32 * ch; c < p.d; c += 64) {
                     uint32_t x[32];
                     tmem_ld32(tmem + lb + 256u + 128u * part + static_cast<uint32_t>(c), x);
                     tc_wait_ld();
@@ -637,9 +739,9 @@ bool encode_tile_map(CUtensorMap* map, const __half* base, int heads, int rows, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int kAtoms>
+template <int kAtoms, bool kHaveLse>
 cudaError_t launch_backward_atoms(const CUtensorMap* maps, const BwdParams& p, cudaStream_t stream) {
-    auto rows = backward_rows_kernel<kAtoms>;
+    auto rows = backward_rows_kernel<kAtoms, kHaveLse>;
     auto cols = backward_cols_kernel<kAtoms>;
     // at least half the SM's shared memory: one CTA per SM, since each CTA
     // takes all 512 TMEM columns (a second one would only wait in its alloc)
@@ -698,7 +800,10 @@ cudaError_t launch_attention_backward(const AttentionBackwardProblem& prob, cuda
         !encode_tile_map(&maps[2], prob.k, p.heads, p.N, p.d) || !encode_tile_map(&maps[3], prob.v, p.heads, p.N, p.d)) {
         return cudaErrorInvalidValue;
     }
-    return p.d <= 64 ? launch_backward_atoms<1>(maps, p, stream) : launch_backward_atoms<2>(maps, p, stream);
+    if (prob.lse_ready) {
+        return p.d <= 64 ? launch_backward_atoms<1, true>(maps, p, stream) : launch_backward_atoms<2, true>(maps, p, stream);
+    }
+    return p.d <= 64 ? launch_backward_atoms<1, false>(maps, p, stream) : launch_backward_atoms<2, false>(maps, p, stream);
 }
 
 cudaError_t read_and_clear_backward_status(unsigned int* status) {

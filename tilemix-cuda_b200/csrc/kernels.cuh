@@ -57,6 +57,9 @@ struct AttentionProblem {
     // Optional max |v| per 64-key block [heads][ceil(N/64)]: key halves whose
     // max is <= 3.5 take single-term P (null: two-term everywhere).
     const __half* v_absmax;
+    // Optional [heads][M] fp32 output: log2 of each row's sum of
+    // 2^(score_scale * log2(e) * score) (null: not written).
+    float* lse_out;
 };
 
 // Routing words from the quantizer's block scales (policy.cu): INT8 iff
@@ -88,9 +91,11 @@ cudaError_t read_and_clear_status(unsigned int* status);
 
 // Backward of the unrouted attention (backward.cu): fp16 Q, K, V, dO; fp32 O
 // (the forward's output) and fp32 dQ, dK, dV; lse and dsum are [heads][M]
-// fp32 row statistics the launch writes and reads (log2-unit log-sum-exp of
-// score_scale * S, and rowsum(dO * O)). d % 16 == 0, d <= 128, every pointer
-// 16-byte aligned; arguments otherwise assumed validated.
+// fp32 row statistics (log2-unit log-sum-exp of score_scale * S, and
+// rowsum(dO * O)): the launch writes dsum, and writes lse too unless
+// lse_ready (lse then holds the forward's lse_out and is only read).
+// d % 16 == 0, d <= 128, every pointer 16-byte aligned; arguments otherwise
+// assumed validated.
 constexpr int kBackwardMaxHeadDim = 128;
 struct AttentionBackwardProblem {
     const __half* q;
@@ -106,6 +111,7 @@ struct AttentionBackwardProblem {
     int heads, M, N, d;
     float score_scale;
     bool causal;
+    bool lse_ready;
 };
 cudaError_t launch_attention_backward(const AttentionBackwardProblem& problem, cudaStream_t stream);
 cudaError_t read_and_clear_backward_status(unsigned int* status);

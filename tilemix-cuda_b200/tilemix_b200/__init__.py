@@ -109,8 +109,10 @@ def _load():
     lib.tilemix_read_and_clear_status.argtypes = [ctypes.POINTER(ctypes.c_uint)]
     lib.tilemix_read_and_clear_status.restype = _I
     lib.tilemix_attention_backward_c.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I,
-                                                 ctypes.c_float, _I, _P]
+                                                 ctypes.c_float, _I, _I, _P]
     lib.tilemix_attention_backward_c.restype = _I
+    lib.tilemix_attention_batched_lse_c.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P]
+    lib.tilemix_attention_batched_lse_c.restype = _I
     return lib
 
 
@@ -144,6 +146,7 @@ C_ABI_SYMBOLS = (
     "tilemix_routing_word_count_c", "tilemix_routing_words_per_row_c",
     "tilemix_reference_shared_bytes", "tilemix_b200_shared_bytes_c",
     "tilemix_read_and_clear_status", "tilemix_watchdog_selftest", "tilemix_attention_backward_c",
+    "tilemix_attention_batched_lse_c",
 )
 
 
@@ -420,14 +423,25 @@ def watchdog_selftest(Q, K, V, O, heads: int, M: int, N: int, d: int, score_scal
                                                float(score_scale), int(wait_limit_us), _stream(stream))
 
 
+def tilemix_attention_batched_lse(Q, K, V, O, lse, heads: int, M: int, N: int, d: int, score_scale: float,
+                                  causal: bool = False, stream=None) -> int:
+    """Unrouted attention that also writes each row's base-2 log-sum-exp
+    (fp32 [heads, M]) for the backward pass. Returns a cudaError_t code."""
+    return _native().tilemix_attention_batched_lse_c(_addr(Q), _addr(K), _addr(V), _addr(O), _addr(lse), heads, M,
+                                                     N, d, float(score_scale), int(bool(causal)), _stream(stream))
+
+
 def tilemix_attention_backward(Q, K, V, O, dO, dQ, dK, dV, lse, dsum, heads: int, M: int, N: int, d: int,
-                               score_scale: float, causal: bool = False, stream=None) -> int:
+                               score_scale: float, causal: bool = False, stream=None,
+                               lse_from_forward: bool = False) -> int:
     """Backward of the unrouted attention through the C-ABI: fp16 Q, K, V, dO,
     fp32 O (the forward's output), fp32 dQ, dK, dV outputs, fp32 [heads, M]
-    lse / dsum workspaces. Returns a cudaError_t code."""
+    lse / dsum (lse read when lse_from_forward, else written). Returns a
+    cudaError_t code."""
     return _native().tilemix_attention_backward_c(_addr(Q), _addr(K), _addr(V), _addr(O), _addr(dO), _addr(dQ),
                                                   _addr(dK), _addr(dV), _addr(lse), _addr(dsum), heads, M, N, d,
-                                                  float(score_scale), int(bool(causal)), _stream(stream))
+                                                  float(score_scale), int(bool(causal)), int(bool(lse_from_forward)),
+                                                  _stream(stream))
 
 
 def read_and_clear_status() -> tuple[int, int]:

@@ -2,8 +2,10 @@
 ``.attention``, ``.attention_bshd``, ``.quantize_qkv`` + ``.attention_hinted``
 (single-term P from V statistics), ``.quantize_k`` + ``.attention_qfused`` (Q
 quantized inside the kernel), ``.routing_policy`` (routing words chosen on
-the device) and ``.attention_backward`` (gradients of the unrouted attention,
-registered as the autograd formula of ``.attention``).
+the device), ``.attention_backward`` (gradients of the unrouted attention,
+registered as the autograd formula of ``.attention``) and ``.attention_lse``
+(the training forward: output and row log-sum-exp, whose autograd formula
+reuses the saved statistics).
 
 They call the same extern "C" entry points as the ctypes functions in
 ``tilemix_b200`` (``tilemix_quantize_qk_batched``, ``tilemix_attention_batched``)
@@ -24,7 +26,7 @@ import torch
 
 from . import (TileMixOutput, TileMixQuantized, TileMixRouting, _require, check, quantize_tilemix_k_batched,
                quantize_tilemix_qk_batched, quantize_tilemix_qkv_batched, tilemix_attention_batched,
-               tilemix_attention_backward, tilemix_attention_batched_hinted, tilemix_attention_batched_out,
+               tilemix_attention_backward, tilemix_attention_batched_hinted, tilemix_attention_batched_lse, tilemix_attention_batched_out,
                tilemix_attention_batched_qfused,
                tilemix_routing_policy, tilemix_routing_word_count, validate_attention_args, validate_quantize_args)
 
@@ -251,31 +253,81 @@ def _(q_scales, k_scales, m, n, key_tiles_per_group, max_scale_product):
 
 @torch.library.custom_op("tilemix::attention_backward", mutates_args=())
 def attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, do: torch.Tensor,
-                       score_scale: float, causal: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+                       lse: torch.Tensor | None, score_scale: float,
+                       causal: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Gradients (dq, dk, dv), fp32 of q's / k's / v's shapes, of the unrouted
     attention o = softmax(score_scale * q k^T [causal]) v, from fp16 q, k, v,
-    the fp32 forward output o and the output gradient do (fp16)."""
+    the fp32 forward output o, the output gradient do (fp16) and, when given,
+    the forward's row log-sum-exp lse ([heads, M] fp32 from
+    ``attention_lse``; without it the backward recomputes it)."""
     heads, m, n, d = validate_attention_args(q, k, v)
     _require(o.shape == q.shape and o.dtype == torch.float32 and o.device == q.device,
              "o must be a float32 tensor of q's shape on q's device")
     _require(do.shape == q.shape and do.dtype == torch.float16 and do.device == q.device,
              "do must be a float16 tensor of q's shape on q's device")
+    if lse is not None:
+        _require(lse.numel() == heads * m and lse.dtype == torch.float32 and lse.device == q.device,
+                 "lse must be a float32 tensor of heads * M elements on q's device")
     q3, k3, v3 = _heads3(q).contiguous(), _heads3(k).contiguous(), _heads3(v).contiguous()
     o3, do3 = _heads3(o).contiguous(), _heads3(do).contiguous()
     dq = torch.empty(q.shape, dtype=torch.float32, device=q.device)
     dk = torch.empty(k.shape, dtype=torch.float32, device=q.device)
     dv = torch.empty(v.shape, dtype=torch.float32, device=q.device)
     stats = torch.empty((2, heads, m), dtype=torch.float32, device=q.device)
-    check(tilemix_attention_backward(q3, k3, v3, o3, do3, dq, dk, dv, stats[0], stats[1], heads, m, n, d,
-                                     score_scale, causal, torch.cuda.current_stream(q.device)),
+    lse_buf = stats[0] if lse is None else lse.contiguous()
+    check(tilemix_attention_backward(q3, k3, v3, o3, do3, dq, dk, dv, lse_buf, stats[1], heads, m, n, d,
+                                     score_scale, causal, torch.cuda.current_stream(q.device),
+                                     lse_from_forward=lse is not None),
           "tilemix::attention_backward")
     return dq, dk, dv
 
 
 @attention_backward.register_fake
-def _(q, k, v, o, do, score_scale, causal):
+def _(q, k, v, o, do, lse, score_scale, causal):
     return (q.new_empty(q.shape, dtype=torch.float32), k.new_empty(k.shape, dtype=torch.float32),
             v.new_empty(v.shape, dtype=torch.float32))
+
+
+@torch.library.custom_op("tilemix::attention_lse", mutates_args=())
+def attention_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, score_scale: float,
+                  causal: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """Unrouted attention for training: (o fp32 of q's shape, lse fp32
+    [heads, M], each row's base-2 log-sum-exp). Its autograd formula runs the
+    backward on the saved lse (no recomputation of the row statistics)."""
+    heads, m, n, d = validate_attention_args(q, k, v)
+    q3, k3, v3 = _heads3(q).contiguous(), _heads3(k).contiguous(), _heads3(v).contiguous()
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    lse = torch.empty((heads, m), dtype=torch.float32, device=q.device)
+    check(tilemix_attention_batched_lse(q3, k3, v3, out, lse, heads, m, n, d, score_scale, causal,
+                                        torch.cuda.current_stream(q.device)), "tilemix::attention_lse")
+    return out, lse
+
+
+@attention_lse.register_fake
+def _(q, k, v, score_scale, causal):
+    heads = 1 if q.dim() == 2 else q.shape[0]
+    return q.new_empty(q.shape, dtype=torch.float32), q.new_empty((heads, q.shape[-2]), dtype=torch.float32)
+
+
+def _attention_lse_setup_context(ctx, inputs, output):
+    q, k, v, score_scale, causal = inputs
+    ctx.set_materialize_grads(False)   # an unused lse gets no gradient tensor
+    ctx.score_scale = score_scale
+    ctx.causal = causal
+    ctx.save_for_backward(q, k, v, *output)
+
+
+def _attention_lse_backward(ctx, grad, grad_lse):
+    if grad_lse is not None:
+        raise NotImplementedError("tilemix::attention_lse has no gradient with respect to lse")
+    if grad is None:
+        return None, None, None, None, None
+    q, k, v, o, lse = ctx.saved_tensors
+    dq, dk, dv = attention_backward(q, k, v, o, grad.to(torch.float16), lse, ctx.score_scale, ctx.causal)
+    return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None
+
+
+attention_lse.register_autograd(_attention_lse_backward, setup_context=_attention_lse_setup_context)
 
 
 def _attention_setup_context(ctx, inputs, output):
@@ -290,7 +342,7 @@ def _attention_backward(ctx, grad):
     if ctx.routed:
         raise NotImplementedError("tilemix::attention has a gradient for the unrouted (all-FP16) call only")
     q, k, v, o = ctx.saved_tensors
-    dq, dk, dv = attention_backward(q, k, v, o, grad.to(torch.float16), ctx.score_scale, ctx.causal)
+    dq, dk, dv = attention_backward(q, k, v, o, grad.to(torch.float16), None, ctx.score_scale, ctx.causal)
     return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None, None, None, None, None, None
 
 
