@@ -26,8 +26,12 @@
 // PV. Warps 0-7 do the elementwise work (warp w owns TMEM lanes 32 (w % 4) ..,
 // one thread per row of the CTA's tile, and column half w / 4 of every
 // sub-block), warp 8 issues the TMA loads, warp 9 allocates TMEM and issues
-// every MMA from one elected lane (the in-order tensor pipe then orders an MMA
-// that overwrites a TMEM tile after the MMAs that read it). Every wait is
+// the S / dP products, warp 10 the accumulation products, each from one
+// elected lane. Two issuing warps keep either kind of product from queueing
+// behind the other: an accumulation can start as soon as its P / dS is
+// written, and the S / dP products that overwrite a TMEM buffer wait (on a
+// barrier committed by warp 10) until the accumulation that read it has
+// completed. Every wait is
 // bounded (1 s); a wait that runs out records a status bit (read with
 // tilemix_read_and_clear_status), all roles stop, drain their own in-flight
 // copies and MMAs, and return.
@@ -53,8 +57,9 @@ constexpr int kRows = 128;                    // tile rows of either kernel (tcg
 constexpr int kSub = 64;                      // sub-block columns
 constexpr int kElemWarps = 8;                 // two per TMEM lane quadrant
 constexpr int kProducer = 8;
-constexpr int kMma = 9;
-constexpr int kBwdThreads = 320;
+constexpr int kMma = 9;                       // S / dP products; allocates TMEM
+constexpr int kMmaAcc = 10;                   // the accumulation products (dQ; dV, dK)
+constexpr int kBwdThreads = 352;
 constexpr uint32_t kAtom = 128 * 128;         // one 64-column fp16 atom of a 128-row tile
 constexpr uint32_t kHalfRows16 = kSub * 128 / 16;   // 64 tile rows, in 16-byte descriptor units
 constexpr uint64_t kLimitNs = 1000000000ull;
@@ -127,7 +132,7 @@ struct BwdSmem {
     static constexpr uint32_t kB1 = kB0 + 2 * kTile;         // [2] row kernel: V;  column kernel: dO
     static constexpr uint32_t kStats = kB1 + 2 * kTile;      // 1024 floats
     static constexpr uint32_t kBars = kStats + 1024 * 4;
-    static constexpr uint32_t kNumBars = 24;
+    static constexpr uint32_t kNumBars = 32;
     static constexpr uint32_t kMisc = kBars + kNumBars * 8;  // TMEM base, abort flag
     static constexpr uint32_t kBytes = kMisc + 16 + 1024;    // + alignment slack
     static_assert(kBytes <= 232448, "shared memory");
@@ -136,11 +141,14 @@ struct BwdSmem {
 // Barriers (same indices in both kernels):
 //   A-full (resident pair); B-full / B-empty [stage]; S-full [buffer] (S and
 //   dP of a sub-block in TMEM); P-ready [buffer] (the elementwise warps have
-//   written P / dS of it); done (last accumulation MMA complete); drain (the
-//   MMA warp's own drain); row kernel pass 1: S1-full / S1-free [ring slot],
-//   stats (LSE and D of every row known).
-enum : int { kBarA = 0, kBarBFull = 1, kBarBEmpty = 3, kBarS = 5, kBarP = 7, kBarDone = 9, kBarDrain = 10,
-             kBarS1 = 11, kBarS1Free = 15, kBarStats = 19 };
+//   written P / dS of it); acc-done [buffer] (the accumulation that read it
+//   has completed); done (last accumulation complete); drain [issuing warp];
+//   row kernel pass 1: S1-full / S1-free [ring slot], stats (LSE and D of
+//   every row known); operands (the row kernel's Q and dO copied into TMEM);
+//   A-free (the row kernel's Q / dO shared-memory tiles no longer read: the
+//   region becomes a third K / V stage).
+enum : int { kBarA = 0, kBarBFull = 1, kBarBEmpty = 4, kBarS = 7, kBarP = 9, kBarAcc = 11, kBarDone = 13,
+             kBarDrain = 14, kBarS1 = 16, kBarS1Free = 20, kBarStats = 24, kBarOps = 25, kBarAFree = 26 };
 constexpr int kRing = 4;                      // pass-1 S slots (64 columns each)
 
 // Common prologue: barriers (one per lane of warp 0), abort flag, TMEM (512
@@ -154,7 +162,7 @@ __device__ __forceinline__ uint32_t bwd_setup(uint8_t* smem, uint32_t sbase) {
         if (lane < L::kNumBars) {
             const int i = static_cast<int>(lane);
             const bool many = (i >= kBarP && i < kBarP + 2) || (i >= kBarS1Free && i < kBarS1Free + kRing) ||
-                              i == kBarStats;
+                              i == kBarStats || i == kBarOps || i == kBarAFree;
             mbar_init(sbase + L::kBars + 8u * lane, many ? kElemWarps : 1);
         }
         if (lane == 0) *reinterpret_cast<volatile int*>(smem + L::kMisc + 4) = 0;
@@ -172,14 +180,69 @@ __device__ __forceinline__ uint32_t bwd_setup(uint8_t* smem, uint32_t sbase) {
 }
 
 // D (128 x 64, fp32 in TMEM) = A B^T over d: A a 128-row K-major tile, B 64
-// rows of one (b_lo already offset to the half).
+// rows of one (b_lo already offset to the half). One thread issues every MMA
+// back to back, so each instruction on that path adds to the issue time: with
+// kSteps > 0 (d = 16 kSteps known at compile time) the loop is unrolled and the
+// descriptor offsets are constants; kSteps = 0 takes d / 16 at run time.
+template <int kSteps>
 __device__ __forceinline__ void mma_sub(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t dhi, int ksteps) {
     const uint32_t none[4] = {0u, 0u, 0u, 0u};
-    const uint32_t idesc = idesc_f16_f32(kRows, kSub, false);
-    mma_f16_ss_w<0>(d_tmem, a_lo, b_lo, dhi, idesc, none);
-    for (int ks = 1; ks < ksteps; ++ks) {
-        const uint32_t ko = static_cast<uint32_t>((ks >> 2) * (kAtom >> 4) + (ks & 3) * 2);
-        mma_f16_ss_w<1>(d_tmem, a_lo + ko, b_lo + ko, dhi, idesc, none);
+    constexpr uint32_t idesc = idesc_f16_f32(kRows, kSub, false);
+    if constexpr (kSteps > 0) {
+        mma_f16_ss_w<0>(d_tmem, a_lo, b_lo, dhi, idesc, none);
+        #pragma unroll
+        for (int ks = 1; ks < kSteps; ++ks) {
+            const uint32_t ko = static_cast<uint32_t>((ks >> 2) * (kAtom >> 4) + (ks & 3) * 2);
+            mma_f16_ss_w<1>(d_tmem, a_lo + ko, b_lo + ko, dhi, idesc, none);
+        }
+    } else {
+        mma_f16_ss_w<0>(d_tmem, a_lo, b_lo, dhi, idesc, none);
+        for (int ks = 1; ks < ksteps; ++ks) {
+            const uint32_t ko = static_cast<uint32_t>((ks >> 2) * (kAtom >> 4) + (ks & 3) * 2);
+            mma_f16_ss_w<1>(d_tmem, a_lo + ko, b_lo + ko, dhi, idesc, none);
+        }
+    }
+}
+
+// D (128 x 64) = A B^T over d with A in TMEM (128 lanes, two fp16 per
+// column: the 16 values of K step ks in columns 8 ks ..) and B 64 rows of a
+// K-major shared-memory tile: only B is read from shared memory.
+template <int kSteps>
+__device__ __forceinline__ void mma_sub_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t dhi,
+                                           int ksteps) {
+    constexpr uint32_t idesc = idesc_f16_f32(kRows, kSub, false);
+    if constexpr (kSteps > 0) {
+        #pragma unroll
+        for (int ks = 0; ks < kSteps; ++ks) {
+            const uint32_t ko = static_cast<uint32_t>((ks >> 2) * (kAtom >> 4) + (ks & 3) * 2);
+            mma_f16_ts_w(d_tmem, a_tmem + 8u * ks, b_lo + ko, dhi, idesc, ks > 0 ? 1u : 0u);
+        }
+    } else {
+        for (int ks = 0; ks < ksteps; ++ks) {
+            const uint32_t ko = static_cast<uint32_t>((ks >> 2) * (kAtom >> 4) + (ks & 3) * 2);
+            mma_f16_ts_w(d_tmem, a_tmem + 8u * static_cast<uint32_t>(ks), b_lo + ko, dhi, idesc, ks > 0 ? 1u : 0u);
+        }
+    }
+}
+
+// Row r of a 128-row, 128-byte-swizzled fp16 tile (kAtoms atoms of 64
+// columns) into this thread's TMEM lane at columns [col, col + 32 kAtoms):
+// column c holds elements 2c (low half) and 2c + 1, the layout of a TMEM A
+// operand.
+template <int kAtoms>
+__device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int r, uint32_t taddr) {
+    #pragma unroll
+    for (int a = 0; a < kAtoms; ++a) {
+        uint32_t v[32];
+        #pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 h = *reinterpret_cast<const uint4*>(tile + a * kAtom + r * 128 + ((c ^ (r & 7)) << 4));
+            v[4 * c] = h.x;
+            v[4 * c + 1] = h.y;
+            v[4 * c + 2] = h.z;
+            v[4 * c + 3] = h.w;
+        }
+        tmem_st32(taddr + 32u * a, v);
     }
 }
 
@@ -198,8 +261,10 @@ __device__ __forceinline__ void mma_acc(uint32_t d_tmem, uint32_t t_tmem, uint32
 // Row kernel: one CTA per (head, 128-row query tile); heaviest causal tiles
 // first. TMEM: pass 1 S slots at 64 s (s < 4); pass 2 buffers at 0 and 128
 // (S in the first 64 columns, dS written over it; dP in the next 64); dQ at
-// 256.
-template <int kAtoms, bool kHaveLse>
+// 256; Q at 384 and dO at 448 (fp16 pairs): the S and dP products take their
+// A operand from TMEM, so shared memory only streams the K / V halves.
+constexpr uint32_t kColDq = 256, kColQ = 384, kColDo = 448;
+template <int kAtoms, bool kHaveLse, int kSteps>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -222,9 +287,15 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     const int npass1 = kHaveLse ? 0 : nblk;       // K blocks loaded for pass 1
     const uint32_t tmem = bwd_setup<kAtoms>(smem, sbase);
 
+    // K / V stage s: the two B stages, and the A region (Q / dO) as the third
+    // once the elementwise warps have copied those into TMEM and read dO
+    auto k_at = [&](int st) -> uint32_t { return st < 2 ? L::kB0 + st * L::kTile : L::kA0; };
+    auto v_at = [&](int st) -> uint32_t { return st < 2 ? L::kB1 + st * L::kTile : L::kA1; };
+    constexpr int kStages = 3;
+
     if (warp == kProducer) {
         // Q and dO once; K (pass 1, unless the forward's LSE is given), then
-        // K and V (pass 2) through two stages.
+        // K and V (pass 2) through the three stages.
         if (elect_one()) {
             mbar_arrive_expect_tx(bar(kBarA), 2 * L::kTile);
             for (int a = 0; a < kAtoms; ++a) {
@@ -235,18 +306,23 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         __syncwarp();
         int issued = 0;
         for (int l = 0; l < npass1 + nblk; ++l) {
-            const int s = l & 1;
+            const int st = l % kStages, n = l / kStages;
             const bool pass2 = l >= npass1;
             const int j = pass2 ? l - npass1 : l;
-            if (!bw_wait(bar(kBarBEmpty + s), ((l >> 1) & 1) ^ 1, abort_flag)) break;
+            bool free_ok = true;
+            if (n > 0) {
+                free_ok = bw_wait(bar(kBarBEmpty + st), (n - 1) & 1, abort_flag);
+            } else if (st == 2) {
+                free_ok = bw_wait(bar(kBarAFree), 0, abort_flag);
+            }
+            if (!free_ok) break;
             if (elect_one()) {
-                mbar_arrive_expect_tx(bar(kBarBFull + s), (pass2 ? 2u : 1u) * L::kTile);
+                mbar_arrive_expect_tx(bar(kBarBFull + st), (pass2 ? 2u : 1u) * L::kTile);
                 for (int a = 0; a < kAtoms; ++a) {
-                    tma_load_3d(sbase + L::kB0 + s * L::kTile + a * kAtom, &tm_k, bar(kBarBFull + s), a * 64,
-                                j * kRows, head);
+                    tma_load_3d(sbase + k_at(st) + a * kAtom, &tm_k, bar(kBarBFull + st), a * 64, j * kRows, head);
                     if (pass2) {
-                        tma_load_3d(sbase + L::kB1 + s * L::kTile + a * kAtom, &tm_v, bar(kBarBFull + s), a * 64,
-                                    j * kRows, head);
+                        tma_load_3d(sbase + v_at(st) + a * kAtom, &tm_v, bar(kBarBFull + st), a * 64, j * kRows,
+                                    head);
                     }
                 }
             }
@@ -254,68 +330,75 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             issued = l + 1;
         }
         bw_drain(bar(kBarA), 0);
-        for (int l = max(0, issued - 2); l < issued; ++l) bw_drain(bar(kBarBFull + (l & 1)), (l >> 1) & 1);
+        for (int l = max(0, issued - kStages); l < issued; ++l) {
+            bw_drain(bar(kBarBFull + l % kStages), (l / kStages) & 1);
+        }
     } else if (warp == kMma) {
+        // S and dP products (and pass 1's S)
         const uint32_t dhi = smem_desc_sw128_hi(1024);
-        const uint32_t idesc_o = idesc_f16_f32(kRows, p.d, true);
         const int ksteps = p.d / 16;
-        const uint32_t q_lo = smem_desc_sw128_lo(sbase + L::kA0, 16);
-        const uint32_t do_lo = smem_desc_sw128_lo(sbase + L::kA1, 16);
-        auto k_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, lbo); };
-        auto v_lo = [&](int s) { return smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, 16); };
-        bool ok = bw_wait(bar(kBarA), 0, abort_flag);
+        // Q and dO are in TMEM once the elementwise warps have copied them
+        bool ok = bw_wait(bar(kBarOps), 0, abort_flag);
         // pass 1: S of sub-block v (keys 64 v ..) into ring slot v % kRing
         for (int v = 0; ok && v < 2 * npass1; ++v) {
-            const int j = v >> 1, h = v & 1, s = j & 1;
-            if (h == 0) ok = bw_wait(bar(kBarBFull + s), (j >> 1) & 1, abort_flag);
+            const int j = v >> 1, h = v & 1, st = j % kStages;
+            if (h == 0) ok = bw_wait(bar(kBarBFull + st), (j / kStages) & 1, abort_flag);
             if (ok && v >= kRing) ok = bw_wait(bar(kBarS1Free + v % kRing), ((v - kRing) / kRing) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
             if (elect_one()) {
-                mma_sub(tmem + 64u * static_cast<uint32_t>(v % kRing), q_lo, k_lo(s, 16) + kHalfRows16 * h, dhi,
-                        ksteps);
+                mma_sub_ts<kSteps>(tmem + 64u * static_cast<uint32_t>(v % kRing), tmem + kColQ,
+                                   smem_desc_sw128_lo(sbase + k_at(st), 16) + kHalfRows16 * h, dhi, ksteps);
                 tc_commit(bar(kBarS1 + v % kRing));
-                if (h == 1) tc_commit(bar(kBarBEmpty + s));
+                if (h == 1) tc_commit(bar(kBarBEmpty + st));
             }
             __syncwarp();
         }
         // pass 2 starts once every row's LSE is known (the pass-1 slots have
-        // then been read). S(v + 1) and dP(v + 1) go into the other buffer
-        // before dQ += dS(v) K, so the tensor core works while the
-        // elementwise warps form dS(v + 1).
+        // then been read). S(v) and dP(v) go into buffer v & 1 once the dQ
+        // product that read sub-block v - 2 from it has completed.
         if (!kHaveLse && ok) ok = bw_wait(bar(kBarStats), 0, abort_flag);
-        for (int v = -1; ok && v < nsub; ++v) {
-            const int nv = v + 1;
-            if (nv < nsub) {
-                const int l = npass1 + (nv >> 1), s = l & 1, h = nv & 1;
-                if (h == 0) ok = bw_wait(bar(kBarBFull + s), (l >> 1) & 1, abort_flag);
-                if (!ok) break;
-                tc_fence_after();
-                if (elect_one()) {
-                    const uint32_t buf = tmem + 128u * static_cast<uint32_t>(nv & 1);
-                    mma_sub(buf, q_lo, k_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
-                    mma_sub(buf + 64u, do_lo, v_lo(s) + kHalfRows16 * h, dhi, ksteps);
-                    tc_commit(bar(kBarS + (nv & 1)));
-                }
-                __syncwarp();
+        for (int v = 0; ok && v < nsub; ++v) {
+            const int l = npass1 + (v >> 1), st = l % kStages, h = v & 1;
+            if (h == 0) ok = bw_wait(bar(kBarBFull + st), (l / kStages) & 1, abort_flag);
+            if (ok && v >= 2) ok = bw_wait(bar(kBarAcc + (v & 1)), ((v - 2) >> 1) & 1, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            if (elect_one()) {
+                const uint32_t buf = tmem + 128u * static_cast<uint32_t>(v & 1);
+                mma_sub_ts<kSteps>(buf, tmem + kColQ, smem_desc_sw128_lo(sbase + k_at(st), 16) + kHalfRows16 * h,
+                                   dhi, ksteps);
+                mma_sub_ts<kSteps>(buf + 64u, tmem + kColDo,
+                                   smem_desc_sw128_lo(sbase + v_at(st), 16) + kHalfRows16 * h, dhi, ksteps);
+                tc_commit(bar(kBarS + (v & 1)));
             }
-            if (v >= 0) {
-                const int l = npass1 + (v >> 1), s = l & 1, h = v & 1;
-                ok = bw_wait(bar(kBarP + (v & 1)), (v >> 1) & 1, abort_flag);
-                if (!ok) break;
-                tc_fence_after();
-                if (elect_one()) {
-                    mma_acc(tmem + 256u, tmem + 128u * static_cast<uint32_t>(v & 1),
-                            k_lo(s, kAtom) + kHalfRows16 * h, dhi, idesc_o, v > 0);
-                    if (h == 1) tc_commit(bar(kBarBEmpty + s));
-                    if (v == nsub - 1) tc_commit(bar(kBarDone));
-                }
-                __syncwarp();
-            }
+            __syncwarp();
         }
         if (lane == 0) tc_commit(bar(kBarDrain));
         __syncwarp();
         bw_drain(bar(kBarDrain), 0);
+    } else if (warp == kMmaAcc) {
+        // dQ += dS(v) K as soon as the elementwise warps have written dS(v)
+        const uint32_t dhi = smem_desc_sw128_hi(1024);
+        const uint32_t idesc_o = idesc_f16_f32(kRows, p.d, true);
+        bool ok = true;
+        for (int v = 0; ok && v < nsub; ++v) {
+            const int l = npass1 + (v >> 1), st = l % kStages, h = v & 1;
+            ok = bw_wait(bar(kBarP + (v & 1)), (v >> 1) & 1, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            if (elect_one()) {
+                mma_acc(tmem + kColDq, tmem + 128u * static_cast<uint32_t>(v & 1),
+                        smem_desc_sw128_lo(sbase + k_at(st), kAtom) + kHalfRows16 * h, dhi, idesc_o, v > 0);
+                tc_commit(bar(kBarAcc + (v & 1)));
+                if (h == 1) tc_commit(bar(kBarBEmpty + st));
+                if (v == nsub - 1) tc_commit(bar(kBarDone));
+            }
+            __syncwarp();
+        }
+        if (lane == 0) tc_commit(bar(kBarDrain + 1));
+        __syncwarp();
+        bw_drain(bar(kBarDrain + 1), 0);
     } else {
         // elementwise: thread = (query row = TMEM lane, column half ch)
         const int quad = warp & 3, ch = warp >> 2;
@@ -325,6 +408,14 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const uint32_t lb = static_cast<uint32_t>(quad * 32) << 16;
         float* stats = reinterpret_cast<float*>(smem + L::kStats);   // [ch][max, sum, D][128]
         bool ok = bw_wait(bar(kBarA), 0, abort_flag);
+        // the MMA operands: half 0 copies this row of Q into TMEM, half 1 of dO
+        if (ok) {
+            tile_row_to_tmem<kAtoms>(smem + (ch == 0 ? L::kA0 : L::kA1), r, tmem + lb + (ch == 0 ? kColQ : kColDo));
+            tc_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kBarOps));
         // D = rowsum(dO * O) over this half's columns: dO from the swizzled
         // tile, O (fp32) from global
         float dsum = 0.0f;
@@ -346,6 +437,10 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 dsum = fmaf(f3.x, o1.z, dsum); dsum = fmaf(f3.y, o1.w, dsum);
             }
         }
+        // the Q / dO tiles in shared memory are no longer read: the producer
+        // may load K / V there
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kBarAFree));
         // A sub-block needs no mask when all its keys exist and (causal) lie
         // at or before the tile's first row.
         auto full_sub = [&](int v) {
@@ -468,7 +563,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             #pragma unroll 1
             for (int c = 32 * ch; c < p.d; c += 64) {
                 uint32_t x[32];
-                tmem_ld32(tmem + lb + 256u + static_cast<uint32_t>(c), x);
+                tmem_ld32(tmem + lb + kColDq + static_cast<uint32_t>(c), x);
                 tc_wait_ld();
                 if (row_ok) {
                     #pragma unroll
@@ -496,7 +591,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 // 64-query sub-blocks. TMEM: buffers at 0 and 128 (S^T in the first 64
 // columns with P^T written over it, dP^T in the next 64 with dS^T over it), dV
 // at 256, dK at 384.
-template <int kAtoms>
+template <int kAtoms, int kSteps>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -551,49 +646,62 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
     } else if (warp == kMma) {
         if (nq > 0) {
+            // S^T and dP^T products
             const uint32_t dhi = smem_desc_sw128_hi(1024);
-            const uint32_t idesc_o = idesc_f16_f32(kRows, p.d, true);
             const int ksteps = p.d / 16;
             const uint32_t k_lo = smem_desc_sw128_lo(sbase + L::kA0, 16);
             const uint32_t v_lo = smem_desc_sw128_lo(sbase + L::kA1, 16);
             auto q_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, lbo); };
             auto do_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, lbo); };
             bool ok = bw_wait(bar(kBarA), 0, abort_flag);
-            // S^T(u + 1), dP^T(u + 1) into the other buffer, then dV, dK
-            // from sub-block u once its P^T / dS^T are written
-            for (int u = -1; ok && u < nsub; ++u) {
-                const int nu = u + 1;
-                if (nu < nsub) {
-                    const int b = nu >> 1, s = b & 1, h = nu & 1;
-                    if (h == 0) ok = bw_wait(bar(kBarBFull + s), (b >> 1) & 1, abort_flag);
-                    if (!ok) break;
-                    tc_fence_after();
-                    if (elect_one()) {
-                        const uint32_t buf = tmem + 128u * static_cast<uint32_t>(nu & 1);
-                        mma_sub(buf, k_lo, q_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
-                        mma_sub(buf + 64u, v_lo, do_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
-                        tc_commit(bar(kBarS + (nu & 1)));
-                    }
-                    __syncwarp();
+            // S^T(u), dP^T(u) into buffer u & 1 once the dV / dK products that
+            // read sub-block u - 2 from it have completed
+            for (int u = 0; ok && u < nsub; ++u) {
+                const int b = u >> 1, s = b & 1, h = u & 1;
+                if (h == 0) ok = bw_wait(bar(kBarBFull + s), (b >> 1) & 1, abort_flag);
+                if (ok && u >= 2) ok = bw_wait(bar(kBarAcc + (u & 1)), ((u - 2) >> 1) & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                if (elect_one()) {
+                    const uint32_t buf = tmem + 128u * static_cast<uint32_t>(u & 1);
+                    mma_sub<kSteps>(buf, k_lo, q_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
+                    mma_sub<kSteps>(buf + 64u, v_lo, do_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
+                    tc_commit(bar(kBarS + (u & 1)));
                 }
-                if (u >= 0) {
-                    const int b = u >> 1, s = b & 1, h = u & 1;
-                    ok = bw_wait(bar(kBarP + (u & 1)), (u >> 1) & 1, abort_flag);
-                    if (!ok) break;
-                    tc_fence_after();
-                    if (elect_one()) {
-                        const uint32_t buf = tmem + 128u * static_cast<uint32_t>(u & 1);
-                        mma_acc(tmem + 256u, buf, do_lo(s, kAtom) + kHalfRows16 * h, dhi, idesc_o, u > 0);
-                        mma_acc(tmem + 384u, buf + 64u, q_lo(s, kAtom) + kHalfRows16 * h, dhi, idesc_o, u > 0);
-                        if (h == 1) tc_commit(bar(kBarBEmpty + s));
-                        if (u == nsub - 1) tc_commit(bar(kBarDone));
-                    }
-                    __syncwarp();
-                }
+                __syncwarp();
             }
             if (lane == 0) tc_commit(bar(kBarDrain));
             __syncwarp();
             bw_drain(bar(kBarDrain), 0);
+        }
+    } else if (warp == kMmaAcc) {
+        if (nq > 0) {
+            // dV += P^T(u) dO, dK += dS^T(u) Q as soon as sub-block u's P^T
+            // and dS^T are written
+            const uint32_t dhi = smem_desc_sw128_hi(1024);
+            const uint32_t idesc_o = idesc_f16_f32(kRows, p.d, true);
+            bool ok = true;
+            for (int u = 0; ok && u < nsub; ++u) {
+                const int b = u >> 1, s = b & 1, h = u & 1;
+                ok = bw_wait(bar(kBarP + (u & 1)), (u >> 1) & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                if (elect_one()) {
+                    const uint32_t buf = tmem + 128u * static_cast<uint32_t>(u & 1);
+                    mma_acc(tmem + 256u, buf, smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, kAtom) + kHalfRows16 * h,
+                            dhi, idesc_o, u > 0);
+                    mma_acc(tmem + 384u, buf + 64u,
+                            smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, kAtom) + kHalfRows16 * h, dhi, idesc_o,
+                            u > 0);
+                    tc_commit(bar(kBarAcc + (u & 1)));
+                    if (h == 1) tc_commit(bar(kBarBEmpty + s));
+                    if (u == nsub - 1) tc_commit(bar(kBarDone));
+                }
+                __syncwarp();
+            }
+            if (lane == 0) tc_commit(bar(kBarDrain + 1));
+            __syncwarp();
+            bw_drain(bar(kBarDrain + 1), 0);
         }
     } else {
         // elementwise: thread = (key row = TMEM lane, query half ch)
@@ -739,10 +847,10 @@ bool encode_tile_map(CUtensorMap* map, const __half* base, int heads, int rows, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int kAtoms, bool kHaveLse>
+template <int kAtoms, bool kHaveLse, int kSteps>
 cudaError_t launch_backward_atoms(const CUtensorMap* maps, const BwdParams& p, cudaStream_t stream) {
-    auto rows = backward_rows_kernel<kAtoms, kHaveLse>;
-    auto cols = backward_cols_kernel<kAtoms>;
+    auto rows = backward_rows_kernel<kAtoms, kHaveLse, kSteps>;
+    auto cols = backward_cols_kernel<kAtoms, kSteps>;
     // at least half the SM's shared memory: one CTA per SM, since each CTA
     // takes all 512 TMEM columns (a second one would only wait in its alloc)
     const int smem = static_cast<int>(BwdSmem<kAtoms>::kBytes > 120u * 1024u ? BwdSmem<kAtoms>::kBytes
@@ -800,10 +908,21 @@ cudaError_t launch_attention_backward(const AttentionBackwardProblem& prob, cuda
         !encode_tile_map(&maps[2], prob.k, p.heads, p.N, p.d) || !encode_tile_map(&maps[3], prob.v, p.heads, p.N, p.d)) {
         return cudaErrorInvalidValue;
     }
-    if (prob.lse_ready) {
-        return p.d <= 64 ? launch_backward_atoms<1, true>(maps, p, stream) : launch_backward_atoms<2, true>(maps, p, stream);
+    // d = 64 and d = 128 take the builds with the K loops unrolled
+    if (p.d == 64) {
+        return prob.lse_ready ? launch_backward_atoms<1, true, 4>(maps, p, stream)
+                              : launch_backward_atoms<1, false, 4>(maps, p, stream);
     }
-    return p.d <= 64 ? launch_backward_atoms<1, false>(maps, p, stream) : launch_backward_atoms<2, false>(maps, p, stream);
+    if (p.d == 128) {
+        return prob.lse_ready ? launch_backward_atoms<2, true, 8>(maps, p, stream)
+                              : launch_backward_atoms<2, false, 8>(maps, p, stream);
+    }
+    if (p.d < 64) {
+        return prob.lse_ready ? launch_backward_atoms<1, true, 0>(maps, p, stream)
+                              : launch_backward_atoms<1, false, 0>(maps, p, stream);
+    }
+    return prob.lse_ready ? launch_backward_atoms<2, true, 0>(maps, p, stream)
+                          : launch_backward_atoms<2, false, 0>(maps, p, stream);
 }
 
 cudaError_t read_and_clear_backward_status(unsigned int* status) {
