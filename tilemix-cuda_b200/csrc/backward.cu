@@ -105,6 +105,20 @@ __device__ __forceinline__ void bw_drain(uint32_t bar, uint32_t parity) {
 // Named barrier of the eight elementwise warps.
 __device__ __forceinline__ void elem_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+constexpr int kHeadGroup = 8;   // heads scheduled together: their streamed operands stay in L2
+
+// Work item of CTA `bid` over tiles x heads: heads in groups of kHeadGroup;
+// inside a group, tile index `order` (0 first) runs for every head of the
+// group before order + 1.
+__device__ __forceinline__ void work_item(int bid, int heads, int tiles, int& head, int& order) {
+    const int per_group = kHeadGroup * tiles;
+    const int group0 = (bid / per_group) * kHeadGroup;
+    const int group_heads = min(kHeadGroup, heads - group0);
+    const int in_group = bid - (bid / per_group) * per_group;
+    order = in_group / group_heads;
+    head = group0 + in_group % group_heads;
+}
+
 struct BwdParams {
     const float* o;            // [heads][M][d] fp32 forward output
     float* dq;                 // [heads][M][d]
@@ -139,16 +153,19 @@ struct BwdSmem {
 };
 
 // Barriers (same indices in both kernels):
-//   A-full (resident pair); B-full / B-empty [stage]; S-full [buffer] (S and
-//   dP of a sub-block in TMEM); P-ready [buffer] (the elementwise warps have
-//   written P / dS of it); acc-done [buffer] (the accumulation that read it
-//   has completed); done (last accumulation complete); drain [issuing warp];
-//   row kernel pass 1: S1-full / S1-free [ring slot], stats (LSE and D of
-//   every row known); operands (the row kernel's Q and dO copied into TMEM);
-//   A-free (the row kernel's Q / dO shared-memory tiles no longer read: the
-//   region becomes a third K / V stage).
-enum : int { kBarA = 0, kBarBFull = 1, kBarBEmpty = 4, kBarS = 7, kBarP = 9, kBarAcc = 11, kBarDone = 13,
-             kBarDrain = 14, kBarS1 = 16, kBarS1Free = 20, kBarStats = 24, kBarOps = 25, kBarAFree = 26 };
+//   A-full (resident pair); B-full / B-empty [stage]; S-full [slot] (S and dP
+//   of a sub-block in TMEM); P-ready [slot] (the elementwise warps have
+//   written P / dS); acc-done [slot] (the accumulation products that read it
+//   have completed); done (last accumulation complete); drain [issuing warp];
+//   dP-free (the elementwise warps have loaded the S / dP slot that the next
+//   sub-block's products overwrite); row kernel pass 1: S1-full / S1-free
+//   [ring slot], stats (LSE and D of every row known); operands (the row
+//   kernel's Q and dO copied into TMEM); A-free (the row kernel's Q / dO
+//   shared-memory tiles no longer read: the region becomes a third K / V
+//   stage).
+enum : int { kBarA = 0, kBarBFull = 1, kBarBEmpty = 4, kBarS = 7, kBarP = 10, kBarAcc = 13, kBarDone = 16,
+             kBarDrain = 17, kBarDpFree = 19, kBarS1 = 20, kBarS1Free = 24, kBarStats = 28, kBarOps = 29,
+             kBarAFree = 30 };
 constexpr int kRing = 4;                      // pass-1 S slots (64 columns each)
 
 // Common prologue: barriers (one per lane of warp 0), abort flag, TMEM (512
@@ -161,8 +178,8 @@ __device__ __forceinline__ uint32_t bwd_setup(uint8_t* smem, uint32_t sbase) {
     if (warp == 0) {
         if (lane < L::kNumBars) {
             const int i = static_cast<int>(lane);
-            const bool many = (i >= kBarP && i < kBarP + 2) || (i >= kBarS1Free && i < kBarS1Free + kRing) ||
-                              i == kBarStats || i == kBarOps || i == kBarAFree;
+            const bool many = (i >= kBarP && i < kBarP + 3) || (i >= kBarS1Free && i < kBarS1Free + kRing) ||
+                              i == kBarStats || i == kBarOps || i == kBarAFree || i == kBarDpFree;
             mbar_init(sbase + L::kBars + 8u * lane, many ? kElemWarps : 1);
         }
         if (lane == 0) *reinterpret_cast<volatile int*>(smem + L::kMisc + 4) = 0;
@@ -246,24 +263,29 @@ __device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int r, uin
     }
 }
 
-// D (128 x d) (+)= T B over a 64-column sub-block: T fp16 in TMEM as the
-// elementwise warps write it (column half ch at +32 ch, 16 values per 8
-// columns), B 64 rows of a tile read MN-major (b_lo offset to the half).
+// D (128 x d) (+)= T B over a 64-column sub-block: T fp16 in TMEM, 16 values
+// (one K step) per 8 columns, the two 32-value halves kHalfStride columns
+// apart (32: written over the columns of S the two warps read, row kernel;
+// 16: packed, column kernel); B 64 rows of a tile read MN-major (b_lo offset
+// to the half).
+template <uint32_t kHalfStride>
 __device__ __forceinline__ void mma_acc(uint32_t d_tmem, uint32_t t_tmem, uint32_t b_lo, uint32_t dhi,
                                         uint32_t idesc, bool accumulate) {
     #pragma unroll
     for (int t = 0; t < kSub / 16; ++t) {
-        mma_f16_ts_w(d_tmem, t_tmem + 32u * static_cast<uint32_t>(t >> 1) + 8u * static_cast<uint32_t>(t & 1),
+        mma_f16_ts_w(d_tmem, t_tmem + kHalfStride * static_cast<uint32_t>(t >> 1) + 8u * static_cast<uint32_t>(t & 1),
                      b_lo + 128u * static_cast<uint32_t>(t), dhi, idesc, (accumulate || t > 0) ? 1u : 0u);
     }
 }
 
 // Row kernel: one CTA per (head, 128-row query tile); heaviest causal tiles
-// first. TMEM: pass 1 S slots at 64 s (s < 4); pass 2 buffers at 0 and 128
-// (S in the first 64 columns, dS written over it; dP in the next 64); dQ at
-// 256; Q at 384 and dO at 448 (fp16 pairs): the S and dP products take their
-// A operand from TMEM, so shared memory only streams the K / V halves.
-constexpr uint32_t kColDq = 256, kColQ = 384, kColDo = 448;
+// first. TMEM: pass 1 S slots at 64 s (s < 4); pass 2 S slots at 0, 64, 128
+// (sub-block v in slot v % 3, dS written over it), one dP slot at 192 (free
+// again as soon as the elementwise warps have loaded it); dQ at 256; Q at 384
+// and dO at 448 (fp16 pairs): the S and dP products take their A operand from
+// TMEM, so shared memory only streams the K / V halves.
+constexpr uint32_t kColDq = 256, kColQ = 384, kColDo = 448, kColDp = 192;
+constexpr int kSSlots = 3;
 template <int kAtoms, bool kHaveLse, int kSteps>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
@@ -280,8 +302,9 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     const int warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31u;
     const int bid = static_cast<int>(blockIdx.x);
-    const int qt = p.q_tiles - 1 - bid / p.heads;
-    const int head = bid % p.heads;
+    int head = 0, order = 0;
+    work_item(bid, p.heads, p.q_tiles, head, order);
+    const int qt = p.q_tiles - 1 - order;
     const int nblk = p.causal ? min(p.k_tiles, qt + 1) : p.k_tiles;
     const int nsub = 2 * nblk;                    // 64-key sub-blocks
     const int npass1 = kHaveLse ? 0 : nblk;       // K blocks loaded for pass 1
@@ -317,6 +340,16 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             }
             if (!free_ok) break;
             if (elect_one()) {
+                // L2 prefetch of the block kStages loads ahead
+                const int la = l + kStages;
+                if (la < npass1 + nblk) {
+                    const bool p2 = la >= npass1;
+                    const int ja = p2 ? la - npass1 : la;
+                    for (int a = 0; a < kAtoms; ++a) {
+                        tma_prefetch_l2_3d(&tm_k, a * 64, ja * kRows, head);
+                        if (p2) tma_prefetch_l2_3d(&tm_v, a * 64, ja * kRows, head);
+                    }
+                }
                 mbar_arrive_expect_tx(bar(kBarBFull + st), (pass2 ? 2u : 1u) * L::kTile);
                 for (int a = 0; a < kAtoms; ++a) {
                     tma_load_3d(sbase + k_at(st) + a * kAtom, &tm_k, bar(kBarBFull + st), a * 64, j * kRows, head);
@@ -359,18 +392,25 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         // product that read sub-block v - 2 from it has completed.
         if (!kHaveLse && ok) ok = bw_wait(bar(kBarStats), 0, abort_flag);
         for (int v = 0; ok && v < nsub; ++v) {
-            const int l = npass1 + (v >> 1), st = l % kStages, h = v & 1;
+            const int l = npass1 + (v >> 1), st = l % kStages, h = v & 1, slot = v % kSSlots;
             if (h == 0) ok = bw_wait(bar(kBarBFull + st), (l / kStages) & 1, abort_flag);
-            if (ok && v >= 2) ok = bw_wait(bar(kBarAcc + (v & 1)), ((v - 2) >> 1) & 1, abort_flag);
+            // S(v) once dQ(v - 3) has read the slot
+            if (ok && v >= kSSlots) ok = bw_wait(bar(kBarAcc + slot), ((v - kSSlots) / kSSlots) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
             if (elect_one()) {
-                const uint32_t buf = tmem + 128u * static_cast<uint32_t>(v & 1);
-                mma_sub_ts<kSteps>(buf, tmem + kColQ, smem_desc_sw128_lo(sbase + k_at(st), 16) + kHalfRows16 * h,
-                                   dhi, ksteps);
-                mma_sub_ts<kSteps>(buf + 64u, tmem + kColDo,
+                mma_sub_ts<kSteps>(tmem + kSub * static_cast<uint32_t>(slot), tmem + kColQ,
+                                   smem_desc_sw128_lo(sbase + k_at(st), 16) + kHalfRows16 * h, dhi, ksteps);
+            }
+            __syncwarp();
+            // dP(v) once the elementwise warps have loaded dP(v - 1)
+            if (v >= 1) ok = bw_wait(bar(kBarDpFree), (v - 1) & 1, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            if (elect_one()) {
+                mma_sub_ts<kSteps>(tmem + kColDp, tmem + kColDo,
                                    smem_desc_sw128_lo(sbase + v_at(st), 16) + kHalfRows16 * h, dhi, ksteps);
-                tc_commit(bar(kBarS + (v & 1)));
+                tc_commit(bar(kBarS + slot));
             }
             __syncwarp();
         }
@@ -383,14 +423,14 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const uint32_t idesc_o = idesc_f16_f32(kRows, p.d, true);
         bool ok = true;
         for (int v = 0; ok && v < nsub; ++v) {
-            const int l = npass1 + (v >> 1), st = l % kStages, h = v & 1;
-            ok = bw_wait(bar(kBarP + (v & 1)), (v >> 1) & 1, abort_flag);
+            const int l = npass1 + (v >> 1), st = l % kStages, h = v & 1, slot = v % kSSlots;
+            ok = bw_wait(bar(kBarP + slot), (v / kSSlots) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
             if (elect_one()) {
-                mma_acc(tmem + kColDq, tmem + 128u * static_cast<uint32_t>(v & 1),
-                        smem_desc_sw128_lo(sbase + k_at(st), kAtom) + kHalfRows16 * h, dhi, idesc_o, v > 0);
-                tc_commit(bar(kBarAcc + (v & 1)));
+                mma_acc<32>(tmem + kColDq, tmem + kSub * static_cast<uint32_t>(slot),
+                            smem_desc_sw128_lo(sbase + k_at(st), kAtom) + kHalfRows16 * h, dhi, idesc_o, v > 0);
+                tc_commit(bar(kBarAcc + slot));
                 if (h == 1) tc_commit(bar(kBarBEmpty + st));
                 if (v == nsub - 1) tc_commit(bar(kBarDone));
             }
@@ -524,14 +564,19 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const float2 sc2 = make_float2(p.scale, p.scale);
         const float2 nd2 = make_float2(-dsum * p.scale, -dsum * p.scale);
         for (int v = 0; ok && v < nsub; ++v) {
-            ok = bw_wait(bar(kBarS + (v & 1)), (v >> 1) & 1, abort_flag);
+            const int slot = v % kSSlots;
+            ok = bw_wait(bar(kBarS + slot), (v / kSSlots) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t buf = tmem + lb + 128u * static_cast<uint32_t>(v & 1) + 32u * ch;
+            const uint32_t buf = tmem + lb + kSub * static_cast<uint32_t>(slot) + 32u * ch;
             uint32_t x[32], y[32];
             tmem_ld32(buf, x);
-            tmem_ld32(buf + 64u, y);
+            tmem_ld32(tmem + lb + kColDp + 32u * ch, y);
             tc_wait_ld();
+            // the dP slot may take the next sub-block's product
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarDpFree));
             const int key0 = v * kSub + 32 * ch;
             const bool full = full_sub(v);
             uint32_t ds[16];
@@ -553,7 +598,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarP + (v & 1)));
+            if (lane == 0) mbar_arrive(bar(kBarP + slot));
         }
         // dQ out: 32-column chunks alternate between the two halves
         if (ok) ok = bw_wait(bar(kBarDone), 0, abort_flag);
@@ -588,9 +633,10 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 
 // Column kernel: one CTA per (head, 128-key tile); K and V stay resident, the
 // query blocks that see the tile stream through (Q, dO) stages, each as two
-// 64-query sub-blocks. TMEM: buffers at 0 and 128 (S^T in the first 64
-// columns with P^T written over it, dP^T in the next 64 with dS^T over it), dV
-// at 256, dK at 384.
+// 64-query sub-blocks. TMEM: S^T at 0 and dP^T at 64 (free again once the
+// elementwise warps have loaded them), two operand slots at 128 and 192 (P^T
+// packed in the first 32 columns, dS^T in the next 32; sub-block u in slot
+// u & 1), dV at 256, dK at 384.
 template <int kAtoms, int kSteps>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
@@ -608,8 +654,9 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     const uint32_t lane = threadIdx.x & 31u;
     const int bid = static_cast<int>(blockIdx.x);
     // causal: the key tiles with the most query blocks first
-    const int kt = p.causal ? bid / p.heads : p.k_tiles - 1 - bid / p.heads;
-    const int head = bid % p.heads;
+    int head = 0, order = 0;
+    work_item(bid, p.heads, p.k_tiles, head, order);
+    const int kt = p.causal ? order : p.k_tiles - 1 - order;
     const int i0 = p.causal ? kt : 0;             // first query block that sees the tile
     const int nq = p.q_tiles - i0;                // may be <= 0 (causal, keys past the last query)
     const int nsub = nq > 0 ? 2 * nq : 0;         // 64-query sub-blocks
@@ -630,6 +677,13 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 const int s = b & 1, i = i0 + b;
                 if (!bw_wait(bar(kBarBEmpty + s), ((b >> 1) & 1) ^ 1, abort_flag)) break;
                 if (elect_one()) {
+                    // L2 prefetch of the block two loads ahead
+                    if (b + 2 < nq) {
+                        for (int a = 0; a < kAtoms; ++a) {
+                            tma_prefetch_l2_3d(&tm_q, a * 64, (i + 2) * kRows, head);
+                            tma_prefetch_l2_3d(&tm_do, a * 64, (i + 2) * kRows, head);
+                        }
+                    }
                     mbar_arrive_expect_tx(bar(kBarBFull + s), 2 * L::kTile);
                     for (int a = 0; a < kAtoms; ++a) {
                         tma_load_3d(sbase + L::kB0 + s * L::kTile + a * kAtom, &tm_q, bar(kBarBFull + s), a * 64,
@@ -654,19 +708,17 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             auto q_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, lbo); };
             auto do_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, lbo); };
             bool ok = bw_wait(bar(kBarA), 0, abort_flag);
-            // S^T(u), dP^T(u) into buffer u & 1 once the dV / dK products that
-            // read sub-block u - 2 from it have completed
+            // S^T(u), dP^T(u) once the elementwise warps have loaded u - 1
             for (int u = 0; ok && u < nsub; ++u) {
                 const int b = u >> 1, s = b & 1, h = u & 1;
                 if (h == 0) ok = bw_wait(bar(kBarBFull + s), (b >> 1) & 1, abort_flag);
-                if (ok && u >= 2) ok = bw_wait(bar(kBarAcc + (u & 1)), ((u - 2) >> 1) & 1, abort_flag);
+                if (ok && u >= 1) ok = bw_wait(bar(kBarDpFree), (u - 1) & 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
                 if (elect_one()) {
-                    const uint32_t buf = tmem + 128u * static_cast<uint32_t>(u & 1);
-                    mma_sub<kSteps>(buf, k_lo, q_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
-                    mma_sub<kSteps>(buf + 64u, v_lo, do_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
-                    tc_commit(bar(kBarS + (u & 1)));
+                    mma_sub<kSteps>(tmem, k_lo, q_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
+                    mma_sub<kSteps>(tmem + 64u, v_lo, do_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
+                    tc_commit(bar(kBarS));
                 }
                 __syncwarp();
             }
@@ -687,12 +739,13 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 if (!ok) break;
                 tc_fence_after();
                 if (elect_one()) {
-                    const uint32_t buf = tmem + 128u * static_cast<uint32_t>(u & 1);
-                    mma_acc(tmem + 256u, buf, smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, kAtom) + kHalfRows16 * h,
-                            dhi, idesc_o, u > 0);
-                    mma_acc(tmem + 384u, buf + 64u,
-                            smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, kAtom) + kHalfRows16 * h, dhi, idesc_o,
-                            u > 0);
+                    const uint32_t op = tmem + 128u + 64u * static_cast<uint32_t>(u & 1);
+                    mma_acc<16>(tmem + 256u, op,
+                                smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, kAtom) + kHalfRows16 * h, dhi, idesc_o,
+                                u > 0);
+                    mma_acc<16>(tmem + 384u, op + 32u,
+                                smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, kAtom) + kHalfRows16 * h, dhi, idesc_o,
+                                u > 0);
                     tc_commit(bar(kBarAcc + (u & 1)));
                     if (h == 1) tc_commit(bar(kBarBEmpty + s));
                     if (u == nsub - 1) tc_commit(bar(kBarDone));
@@ -731,14 +784,22 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 stats[(b & 1) * 2 * kRows + t] = val;
                 elem_sync();
             }
-            if (ok) ok = bw_wait(bar(kBarS + (u & 1)), (u >> 1) & 1, abort_flag);
+            if (ok) ok = bw_wait(bar(kBarS), u & 1, abort_flag);
             if (!ok) continue;
             tc_fence_after();
-            const uint32_t buf = tmem + lb + 128u * static_cast<uint32_t>(u & 1) + 32u * ch;
             uint32_t x[32], y[32];
-            tmem_ld32(buf, x);
-            tmem_ld32(buf + 64u, y);
+            tmem_ld32(tmem + lb + 32u * ch, x);
+            tmem_ld32(tmem + lb + 64u + 32u * ch, y);
             tc_wait_ld();
+            // S^T / dP^T may take the next sub-block's products
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarDpFree));
+            // the operand slot is free once the products of u - 2 have read it
+            if (u >= 2) ok = bw_wait(bar(kBarAcc + (u & 1)), ((u - 2) >> 1) & 1, abort_flag);
+            if (!ok) continue;
+            tc_fence_after();
+            const uint32_t op = tmem + lb + 128u + 64u * static_cast<uint32_t>(u & 1) + 16u * ch;
             const int col0 = kSub * h + 32 * ch;          // query within the block
             const int q0 = i * kRows + col0;
             // no mask when every query of the sub-block exists and (causal)
@@ -766,8 +827,8 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                     dst[e + f] = pack_half2(dv.x, dv.y);
                 }
             }
-            tmem_st16(buf, pt);
-            tmem_st16(buf + 64u, dst);
+            tmem_st16(op, pt);
+            tmem_st16(op + 32u, dst);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
