@@ -765,6 +765,19 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         float* stats = reinterpret_cast<float*>(smem + L::kStats);   // [block & 1][-LSE, -D scale][128]
         const float2 c2 = make_float2(p.c, p.c), sc2 = make_float2(p.scale, p.scale);
         bool ok = true;
+        // Row statistics of query block i, staged once per block: thread
+        // t < 128 holds -LSE of query t, thread 128 + t its -D * scale. Each
+        // thread loads its raw value one block ahead and transforms it only
+        // when it stores it, so nothing waits on the load in between and the
+        // global-load latency overlaps the previous block's work.
+        const int t = static_cast<int>(threadIdx.x);
+        const float* stat_src = t < kRows ? p.lse : p.dsum;
+        const float stat_mul = t < kRows ? -1.0f : -p.scale;
+        auto stat_of = [&](int i) -> float {
+            const int q = i * kRows + (t & (kRows - 1));
+            return q < p.M ? stat_src[static_cast<std::size_t>(head) * p.M + q] : 0.0f;
+        };
+        float next_stat = nq > 0 ? stat_of(i0) : 0.0f;
         // Every elementwise warp runs all iterations (the named barrier needs
         // all eight); after an abort they only pass the barrier.
         for (int u = 0; u < nsub; ++u) {
@@ -772,17 +785,9 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             const float* nl_s = stats + (b & 1) * 2 * kRows;
             const float* nd_s = nl_s + kRows;
             if (h == 0) {
-                // the block's row statistics, staged once: thread t < 128
-                // stores -LSE of query t, thread 128 + t its -D * scale
-                const int t = static_cast<int>(threadIdx.x);
-                const int q = i * kRows + (t & (kRows - 1));
-                float val = 0.0f;
-                if (q < p.M) {
-                    const std::size_t at = static_cast<std::size_t>(head) * p.M + q;
-                    val = t < kRows ? -p.lse[at] : -p.dsum[at] * p.scale;
-                }
-                stats[(b & 1) * 2 * kRows + t] = val;
+                stats[(b & 1) * 2 * kRows + t] = next_stat * stat_mul;
                 elem_sync();
+                if (b + 1 < nq) next_stat = stat_of(i + 1);
             }
             if (ok) ok = bw_wait(bar(kBarS), u & 1, abort_flag);
             if (!ok) continue;
