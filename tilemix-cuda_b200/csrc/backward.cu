@@ -23,14 +23,16 @@
 // operands); the P / dS products as TS MMAs with the fp16 tile in TMEM (two
 // values per 32-bit column; the 16 values of a K step in 8 consecutive
 // columns) and an MN-major shared-memory B operand, exactly like the forward's
-// PV. Warps 0-7 do the elementwise work (warp w owns TMEM lanes 32 (w % 4) ..,
-// one thread per row of the CTA's tile, and column half w / 4 of every
-// sub-block), warp 8 issues the TMA loads, warp 9 allocates TMEM and issues
-// the S / dP products, warp 10 the accumulation products, each from one
+// PV. Warps 0-15 do the elementwise work (warp w owns TMEM lanes 32 (w % 4)
+// .., one thread per row of the CTA's tile, and the 16-column quarter w / 4
+// of every sub-block: four warps per scheduler hide the latency of the TMEM
+// loads and the exponentials), warp 16 issues the TMA loads, warp 17
+// allocates TMEM and issues the S / dP products, warp 18 the accumulation
+// products, each from one
 // elected lane. Two issuing warps keep either kind of product from queueing
 // behind the other: an accumulation can start as soon as its P / dS is
 // written, and the S / dP products that overwrite a TMEM buffer wait (on a
-// barrier committed by warp 10) until the accumulation that read it has
+// barrier committed by warp 18) until the accumulation that read it has
 // completed. Every wait is
 // bounded (1 s); a wait that runs out records a status bit (read with
 // tilemix_read_and_clear_status), all roles stop, drain their own in-flight
@@ -55,11 +57,14 @@ using namespace sm100;
 
 constexpr int kRows = 128;                    // tile rows of either kernel (tcgen05 M)
 constexpr int kSub = 64;                      // sub-block columns
-constexpr int kElemWarps = 8;                 // two per TMEM lane quadrant
-constexpr int kProducer = 8;
-constexpr int kMma = 9;                       // S / dP products; allocates TMEM
-constexpr int kMmaAcc = 10;                   // the accumulation products (dQ; dV, dK)
-constexpr int kBwdThreads = 352;
+constexpr int kSplit = 4;                     // elementwise warps per TMEM lane quadrant
+constexpr int kColsPer = kSub / kSplit;       // sub-block columns of one elementwise warp
+static_assert(kColsPer == 16, "one elementwise warp produces exactly one K step of the P / dS operands");
+constexpr int kElemWarps = 4 * kSplit;
+constexpr int kProducer = kElemWarps;
+constexpr int kMma = kElemWarps + 1;          // S / dP products; allocates TMEM
+constexpr int kMmaAcc = kElemWarps + 2;       // the accumulation products (dQ; dV, dK)
+constexpr int kBwdThreads = 32 * (kElemWarps + 3);
 constexpr uint32_t kAtom = 128 * 128;         // one 64-column fp16 atom of a 128-row tile
 constexpr uint32_t kHalfRows16 = kSub * 128 / 16;   // 64 tile rows, in 16-byte descriptor units
 constexpr uint64_t kLimitNs = 1000000000ull;
@@ -102,8 +107,8 @@ __device__ __forceinline__ void bw_drain(uint32_t bar, uint32_t parity) {
     __syncwarp();
 }
 
-// Named barrier of the eight elementwise warps.
-__device__ __forceinline__ void elem_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Named barrier of the elementwise warps.
+__device__ __forceinline__ void elem_sync() { asm volatile("bar.sync 1, %0;" :: "n"(32 * kElemWarps) : "memory"); }
 
 constexpr int kHeadGroup = 8;   // heads scheduled together: their streamed operands stay in L2
 
@@ -144,8 +149,8 @@ struct BwdSmem {
     static constexpr uint32_t kA1 = kA0 + kTile;             // row kernel: dO; column kernel: V
     static constexpr uint32_t kB0 = kA1 + kTile;             // [2] row kernel: K;  column kernel: Q
     static constexpr uint32_t kB1 = kB0 + 2 * kTile;         // [2] row kernel: V;  column kernel: dO
-    static constexpr uint32_t kStats = kB1 + 2 * kTile;      // 1024 floats
-    static constexpr uint32_t kBars = kStats + 1024 * 4;
+    static constexpr uint32_t kStats = kB1 + 2 * kTile;      // 2048 floats
+    static constexpr uint32_t kBars = kStats + 2048 * 4;
     static constexpr uint32_t kNumBars = 32;
     static constexpr uint32_t kMisc = kBars + kNumBars * 8;  // TMEM base, abort flag
     static constexpr uint32_t kBytes = kMisc + 16 + 1024;    // + alignment slack
@@ -242,39 +247,34 @@ __device__ __forceinline__ void mma_sub_ts(uint32_t d_tmem, uint32_t a_tmem, uin
     }
 }
 
-// Row r of a 128-row, 128-byte-swizzled fp16 tile (kAtoms atoms of 64
-// columns) into this thread's TMEM lane at columns [col, col + 32 kAtoms):
-// column c holds elements 2c (low half) and 2c + 1, the layout of a TMEM A
-// operand.
-template <int kAtoms>
-__device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int r, uint32_t taddr) {
+// Row r of atom `a` (64 columns) of a 128-row, 128-byte-swizzled fp16 tile
+// into this thread's TMEM lane at columns [col, col + 32): column c holds
+// elements 2c (low half) and 2c + 1, the layout of a TMEM A operand.
+__device__ __forceinline__ void atom_row_to_tmem(const uint8_t* tile, int a, int r, uint32_t taddr) {
+    uint32_t v[32];
     #pragma unroll
-    for (int a = 0; a < kAtoms; ++a) {
-        uint32_t v[32];
-        #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const uint4 h = *reinterpret_cast<const uint4*>(tile + a * kAtom + r * 128 + ((c ^ (r & 7)) << 4));
-            v[4 * c] = h.x;
-            v[4 * c + 1] = h.y;
-            v[4 * c + 2] = h.z;
-            v[4 * c + 3] = h.w;
-        }
-        tmem_st32(taddr + 32u * a, v);
+    for (int c = 0; c < 8; ++c) {
+        const uint4 h = *reinterpret_cast<const uint4*>(tile + a * kAtom + r * 128 + ((c ^ (r & 7)) << 4));
+        v[4 * c] = h.x;
+        v[4 * c + 1] = h.y;
+        v[4 * c + 2] = h.z;
+        v[4 * c + 3] = h.w;
     }
+    tmem_st32(taddr, v);
 }
 
-// D (128 x d) (+)= T B over a 64-column sub-block: T fp16 in TMEM, 16 values
-// (one K step) per 8 columns, the two 32-value halves kHalfStride columns
-// apart (32: written over the columns of S the two warps read, row kernel;
-// 16: packed, column kernel); B 64 rows of a tile read MN-major (b_lo offset
-// to the half).
-template <uint32_t kHalfStride>
+// D (128 x d) (+)= T B over a 64-column sub-block: T fp16 in TMEM, the 16
+// values of K step t (the columns one elementwise warp produced) in 8 columns
+// starting at t_tmem + kStepStride t (16: written over the S columns that warp
+// read, row kernel; 8: packed, column kernel); B 64 rows of a tile read
+// MN-major (b_lo offset to the half).
+template <uint32_t kStepStride>
 __device__ __forceinline__ void mma_acc(uint32_t d_tmem, uint32_t t_tmem, uint32_t b_lo, uint32_t dhi,
                                         uint32_t idesc, bool accumulate) {
     #pragma unroll
     for (int t = 0; t < kSub / 16; ++t) {
-        mma_f16_ts_w(d_tmem, t_tmem + kHalfStride * static_cast<uint32_t>(t >> 1) + 8u * static_cast<uint32_t>(t & 1),
-                     b_lo + 128u * static_cast<uint32_t>(t), dhi, idesc, (accumulate || t > 0) ? 1u : 0u);
+        mma_f16_ts_w(d_tmem, t_tmem + kStepStride * static_cast<uint32_t>(t), b_lo + 128u * static_cast<uint32_t>(t),
+                     dhi, idesc, (accumulate || t > 0) ? 1u : 0u);
     }
 }
 
@@ -428,7 +428,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             if (!ok) break;
             tc_fence_after();
             if (elect_one()) {
-                mma_acc<32>(tmem + kColDq, tmem + kSub * static_cast<uint32_t>(slot),
+                mma_acc<16>(tmem + kColDq, tmem + kSub * static_cast<uint32_t>(slot),
                             smem_desc_sw128_lo(sbase + k_at(st), kAtom) + kHalfRows16 * h, dhi, idesc_o, v > 0);
                 tc_commit(bar(kBarAcc + slot));
                 if (h == 1) tc_commit(bar(kBarBEmpty + st));
@@ -440,7 +440,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         __syncwarp();
         bw_drain(bar(kBarDrain + 1), 0);
     } else {
-        // elementwise: thread = (query row = TMEM lane, column half ch)
+        // elementwise: thread = (query row = TMEM lane, column quarter ch)
         const int quad = warp & 3, ch = warp >> 2;
         const int r = quad * 32 + static_cast<int>(lane);
         const int row = qt * kRows + r;
@@ -448,21 +448,23 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const uint32_t lb = static_cast<uint32_t>(quad * 32) << 16;
         float* stats = reinterpret_cast<float*>(smem + L::kStats);   // [ch][max, sum, D][128]
         bool ok = bw_wait(bar(kBarA), 0, abort_flag);
-        // the MMA operands: half 0 copies this row of Q into TMEM, half 1 of dO
-        if (ok) {
-            tile_row_to_tmem<kAtoms>(smem + (ch == 0 ? L::kA0 : L::kA1), r, tmem + lb + (ch == 0 ? kColQ : kColDo));
+        // the MMA operands: warp quarter ch copies this row's atom ch % kAtoms
+        // of Q (ch < kAtoms) or of dO (kAtoms <= ch < 2 kAtoms) into TMEM
+        if (ok && ch < 2 * kAtoms) {
+            const int which = ch / kAtoms, atom = ch % kAtoms;
+            atom_row_to_tmem(smem + (which == 0 ? L::kA0 : L::kA1), atom, r,
+                             tmem + lb + (which == 0 ? kColQ : kColDo) + 32u * atom);
             tc_wait_st();
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(kBarOps));
-        // D = rowsum(dO * O) over this half's columns: dO from the swizzled
-        // tile, O (fp32) from global
+        // D = rowsum(dO * O) over this quarter's 8-column chunks: dO from the
+        // swizzled tile, O (fp32) from global
         float dsum = 0.0f;
         if (ok && row_ok) {
             const float* orow = p.o + (static_cast<std::size_t>(head) * p.M + row) * p.d;
-            const int h8 = p.d / 16;   // 8-column chunks per half (d % 16 == 0)
-            for (int c8 = ch * h8; c8 < (ch + 1) * h8; ++c8) {
+            for (int c8 = ch; c8 < p.d / 8; c8 += kSplit) {
                 const int atom = c8 >> 3, c = c8 & 7;
                 const uint4 hv = *reinterpret_cast<const uint4*>(smem + L::kA1 + atom * kAtom + r * 128 +
                                                                  ((c ^ (r & 7)) << 4));
@@ -489,24 +491,25 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         };
         float lse = 0.0f;
         if constexpr (!kHaveLse) {
-            // pass 1: running max and sum of 2^(c S) over this half's visible keys
+            // pass 1: running max and sum of 2^(c S) over this quarter's
+            // visible keys
             float m = -INFINITY, l = 0.0f;
             for (int v = 0; ok && v < nsub; ++v) {
                 ok = bw_wait(bar(kBarS1 + v % kRing), (v / kRing) & 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
-                uint32_t x[32];
-                tmem_ld32(tmem + lb + 64u * static_cast<uint32_t>(v % kRing) + 32u * ch, x);
+                uint32_t x[kColsPer];
+                tmem_ld16(tmem + lb + 64u * static_cast<uint32_t>(v % kRing) + kColsPer * ch, x);
                 tc_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(kBarS1Free + v % kRing));
-                const int key0 = v * kSub + 32 * ch;
+                const int key0 = v * kSub + kColsPer * ch;
                 const bool full = full_sub(v);
-                float s2[32];
+                float s2[kColsPer];
                 float cm = -INFINITY;
                 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
+                for (int i = 0; i < kColsPer; i += 2) {
                     const float2 t = __fmul2_rn(make_float2(__uint_as_float(x[i]), __uint_as_float(x[i + 1])),
                                                 make_float2(p.c, p.c));
                     s2[i] = t.x;
@@ -514,18 +517,20 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 }
                 if (!full) {
                     #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
+                    for (int i = 0; i < kColsPer; ++i) {
                         const int key = key0 + i;
                         if (!(key < p.N && (!p.causal || key <= row))) s2[i] = -INFINITY;
                     }
                 }
                 #pragma unroll
-                for (int i = 0; i < 32; i += 4) cm = fmaxf(cm, max3f(s2[i], s2[i + 1], fmaxf(s2[i + 2], s2[i + 3])));
+                for (int i = 0; i < kColsPer; i += 4) {
+                    cm = fmaxf(cm, max3f(s2[i], s2[i + 1], fmaxf(s2[i + 2], s2[i + 3])));
+                }
                 const float mn = fmaxf(m, cm);
                 if (mn > -INFINITY) {
                     float sum0 = 0.0f, sum1 = 0.0f;
                     #pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
+                    for (int i = 0; i < kColsPer; i += 2) {
                         sum0 += ex2(s2[i] - mn);
                         sum1 += ex2(s2[i + 1] - mn);
                     }
@@ -533,32 +538,39 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                     m = mn;
                 }
             }
-            // combine the two halves of each row; every elementwise warp
-            // reaches this barrier exactly once, aborted or not
+            // combine the quarters of each row (in a fixed order, so every
+            // warp gets the same values); every elementwise warp reaches this
+            // barrier exactly once, aborted or not
             stats[(ch * 3 + 0) * kRows + r] = m;
             stats[(ch * 3 + 1) * kRows + r] = l;
             stats[(ch * 3 + 2) * kRows + r] = dsum;
             elem_sync();
-            const int other = 1 - ch;
-            const float m2 = stats[(other * 3 + 0) * kRows + r];
-            const float l2 = stats[(other * 3 + 1) * kRows + r];
-            const float mm = fmaxf(m, m2);
-            const float lsum =
-                (m > -INFINITY ? l * ex2(m - mm) : 0.0f) + (m2 > -INFINITY ? l2 * ex2(m2 - mm) : 0.0f);
+            float mm = -INFINITY;
+            #pragma unroll
+            for (int k = 0; k < kSplit; ++k) mm = fmaxf(mm, stats[(k * 3 + 0) * kRows + r]);
+            float lsum = 0.0f;
+            dsum = 0.0f;
+            #pragma unroll
+            for (int k = 0; k < kSplit; ++k) {
+                const float mk = stats[(k * 3 + 0) * kRows + r];
+                lsum += mk > -INFINITY ? stats[(k * 3 + 1) * kRows + r] * ex2(mk - mm) : 0.0f;
+                dsum += stats[(k * 3 + 2) * kRows + r];
+            }
             lse = mm + log2f(lsum);
-            dsum += stats[(other * 3 + 2) * kRows + r];
             if (ok && row_ok && ch == 0) p.lse[static_cast<std::size_t>(head) * p.M + row] = lse;
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarStats));
         } else {
-            // the forward's LSE; D's two halves combined
+            // the forward's LSE; D's quarters combined in a fixed order
             stats[(ch * 3 + 2) * kRows + r] = dsum;
             elem_sync();
-            dsum += stats[((1 - ch) * 3 + 2) * kRows + r];
+            dsum = 0.0f;
+            #pragma unroll
+            for (int k = 0; k < kSplit; ++k) dsum += stats[(k * 3 + 2) * kRows + r];
             if (row_ok) lse = p.lse[static_cast<std::size_t>(head) * p.M + row];
         }
         if (ok && row_ok && ch == 0) p.dsum[static_cast<std::size_t>(head) * p.M + row] = dsum;
-        // pass 2: dS = P (dP - D) * score_scale, fp16, over this half's S
+        // pass 2: dS = P (dP - D) * score_scale, fp16, over this quarter's S
         // columns; P = 2^(c S - LSE)
         const float2 c2 = make_float2(p.c, p.c), nl2 = make_float2(-lse, -lse);
         const float2 sc2 = make_float2(p.scale, p.scale);
@@ -568,20 +580,20 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             ok = bw_wait(bar(kBarS + slot), (v / kSSlots) & 1, abort_flag);
             if (!ok) break;
             tc_fence_after();
-            const uint32_t buf = tmem + lb + kSub * static_cast<uint32_t>(slot) + 32u * ch;
-            uint32_t x[32], y[32];
-            tmem_ld32(buf, x);
-            tmem_ld32(tmem + lb + kColDp + 32u * ch, y);
+            const uint32_t buf = tmem + lb + kSub * static_cast<uint32_t>(slot) + kColsPer * ch;
+            uint32_t x[kColsPer], y[kColsPer];
+            tmem_ld16(buf, x);
+            tmem_ld16(tmem + lb + kColDp + kColsPer * ch, y);
             tc_wait_ld();
             // the dP slot may take the next sub-block's product
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarDpFree));
-            const int key0 = v * kSub + 32 * ch;
+            const int key0 = v * kSub + kColsPer * ch;
             const bool full = full_sub(v);
-            uint32_t ds[16];
+            uint32_t ds[kColsPer / 2];
             #pragma unroll
-            for (int i = 0; i < 16; ++i) {
+            for (int i = 0; i < kColsPer / 2; ++i) {
                 float2 t = __ffma2_rn(make_float2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])), c2, nl2);
                 if (!full) {
                     const int key = key0 + 2 * i;
@@ -594,19 +606,20 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 const float2 dv = __fmul2_rn(pr, g);
                 ds[i] = pack_half2(dv.x, dv.y);
             }
-            tmem_st16(buf, ds);
+            // packed over the first 8 of the S columns this warp read
+            tmem_st8(buf, ds);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarP + slot));
         }
-        // dQ out: 32-column chunks alternate between the two halves
+        // dQ out: 32-column chunks shared round-robin by the quarters
         if (ok) ok = bw_wait(bar(kBarDone), 0, abort_flag);
         if (ok) {
             tc_fence_after();
             float* out = p.dq + (static_cast<std::size_t>(head) * p.M + row) * p.d;
             #pragma unroll 1
-            for (int c = 32 * ch; c < p.d; c += 64) {
+            for (int c = 32 * ch; c < p.d; c += 32 * kSplit) {
                 uint32_t x[32];
                 tmem_ld32(tmem + lb + kColDq + static_cast<uint32_t>(c), x);
                 tc_wait_ld();
@@ -740,10 +753,10 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 tc_fence_after();
                 if (elect_one()) {
                     const uint32_t op = tmem + 128u + 64u * static_cast<uint32_t>(u & 1);
-                    mma_acc<16>(tmem + 256u, op,
+                    mma_acc<8>(tmem + 256u, op,
                                 smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, kAtom) + kHalfRows16 * h, dhi, idesc_o,
                                 u > 0);
-                    mma_acc<16>(tmem + 384u, op + 32u,
+                    mma_acc<8>(tmem + 384u, op + 32u,
                                 smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, kAtom) + kHalfRows16 * h, dhi, idesc_o,
                                 u > 0);
                     tc_commit(bar(kBarAcc + (u & 1)));
@@ -757,7 +770,7 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             bw_drain(bar(kBarDrain + 1), 0);
         }
     } else {
-        // elementwise: thread = (key row = TMEM lane, query half ch)
+        // elementwise: thread = (key row = TMEM lane, query quarter ch)
         const int quad = warp & 3, ch = warp >> 2;
         const int r = quad * 32 + static_cast<int>(lane);
         const int key = kt * kRows + r;
@@ -771,30 +784,31 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         // when it stores it, so nothing waits on the load in between and the
         // global-load latency overlaps the previous block's work.
         const int t = static_cast<int>(threadIdx.x);
+        const bool stager = t < 2 * kRows;
         const float* stat_src = t < kRows ? p.lse : p.dsum;
         const float stat_mul = t < kRows ? -1.0f : -p.scale;
         auto stat_of = [&](int i) -> float {
             const int q = i * kRows + (t & (kRows - 1));
-            return q < p.M ? stat_src[static_cast<std::size_t>(head) * p.M + q] : 0.0f;
+            return stager && q < p.M ? stat_src[static_cast<std::size_t>(head) * p.M + q] : 0.0f;
         };
         float next_stat = nq > 0 ? stat_of(i0) : 0.0f;
         // Every elementwise warp runs all iterations (the named barrier needs
-        // all eight); after an abort they only pass the barrier.
+        // all of them); after an abort they only pass the barrier.
         for (int u = 0; u < nsub; ++u) {
             const int b = u >> 1, h = u & 1, i = i0 + b;
             const float* nl_s = stats + (b & 1) * 2 * kRows;
             const float* nd_s = nl_s + kRows;
             if (h == 0) {
-                stats[(b & 1) * 2 * kRows + t] = next_stat * stat_mul;
+                if (stager) stats[(b & 1) * 2 * kRows + t] = next_stat * stat_mul;
                 elem_sync();
                 if (b + 1 < nq) next_stat = stat_of(i + 1);
             }
             if (ok) ok = bw_wait(bar(kBarS), u & 1, abort_flag);
             if (!ok) continue;
             tc_fence_after();
-            uint32_t x[32], y[32];
-            tmem_ld32(tmem + lb + 32u * ch, x);
-            tmem_ld32(tmem + lb + 64u + 32u * ch, y);
+            uint32_t x[kColsPer], y[kColsPer];
+            tmem_ld16(tmem + lb + kColsPer * ch, x);
+            tmem_ld16(tmem + lb + 64u + kColsPer * ch, y);
             tc_wait_ld();
             // S^T / dP^T may take the next sub-block's products
             tc_fence_before();
@@ -804,15 +818,17 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             if (u >= 2) ok = bw_wait(bar(kBarAcc + (u & 1)), ((u - 2) >> 1) & 1, abort_flag);
             if (!ok) continue;
             tc_fence_after();
-            const uint32_t op = tmem + lb + 128u + 64u * static_cast<uint32_t>(u & 1) + 16u * ch;
-            const int col0 = kSub * h + 32 * ch;          // query within the block
+            // this quarter's K step, packed: P^T at +8 ch, dS^T at 32 + 8 ch
+            const uint32_t op = tmem + lb + 128u + 64u * static_cast<uint32_t>(u & 1) + (kColsPer / 2) * ch;
+            const int col0 = kSub * h + kColsPer * ch;     // query within the block
             const int q0 = i * kRows + col0;
             // no mask when every query of the sub-block exists and (causal)
             // sees every key of the tile
-            const bool full = i * kRows + kSub * (h + 1) <= p.M && (!p.causal || kt * kRows + kRows - 1 <= i * kRows + kSub * h);
-            uint32_t pt[16], dst[16];
+            const bool full = i * kRows + kSub * (h + 1) <= p.M &&
+                              (!p.causal || kt * kRows + kRows - 1 <= i * kRows + kSub * h);
+            uint32_t pt[kColsPer / 2], dst[kColsPer / 2];
             #pragma unroll
-            for (int e = 0; e < 16; e += 2) {
+            for (int e = 0; e < kColsPer / 2; e += 2) {
                 const float4 nl = *reinterpret_cast<const float4*>(nl_s + col0 + 2 * e);
                 const float4 nd = *reinterpret_cast<const float4*>(nd_s + col0 + 2 * e);
                 #pragma unroll
@@ -832,22 +848,21 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                     dst[e + f] = pack_half2(dv.x, dv.y);
                 }
             }
-            tmem_st16(op, pt);
-            tmem_st16(op + 32u, dst);
+            tmem_st8(op, pt);
+            tmem_st8(op + 32u, dst);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarP + (u & 1)));
         }
-        if (key < p.N) {
+        // dV / dK out: 32-column chunks shared round-robin by the quarters
+        if (key < p.N && nq <= 0) {
             float* dv_out = p.dv + (static_cast<std::size_t>(head) * p.N + key) * p.d;
             float* dk_out = p.dk + (static_cast<std::size_t>(head) * p.N + key) * p.d;
-            if (nq <= 0) {
-                for (int c = 32 * ch; c < p.d; c += 64) {
-                    for (int e = 0; e < 32 && c + e < p.d; e += 4) {
-                        *reinterpret_cast<float4*>(dv_out + c + e) = make_float4(0.f, 0.f, 0.f, 0.f);
-                        *reinterpret_cast<float4*>(dk_out + c + e) = make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
+            for (int c = 32 * ch; c < p.d; c += 32 * kSplit) {
+                for (int e = 0; e < 32 && c + e < p.d; e += 4) {
+                    *reinterpret_cast<float4*>(dv_out + c + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    *reinterpret_cast<float4*>(dk_out + c + e) = make_float4(0.f, 0.f, 0.f, 0.f);
                 }
             }
         }
@@ -858,7 +873,7 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             for (int part = 0; part < 2; ++part) {
                 float* out = (part == 0 ? p.dv : p.dk) + (static_cast<std::size_t>(head) * p.N + key) * p.d;
                 #pragma unroll 1
-                for (int c = 32 * ch; c < p.d; c += 64) {
+                for (int c = 32 * ch; c < p.d; c += 32 * kSplit) {
                     uint32_t x[32];
                     tmem_ld32(tmem + lb + 256u + 128u * part + static_cast<uint32_t>(c), x);
                     tc_wait_ld();

@@ -320,6 +320,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
         :: "r"(taddr), TILEMIX_W8(r, 0), TILEMIX_W8(r, 8) : "memory");
 }
 
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+        :: "r"(taddr), TILEMIX_W8(r, 0) : "memory");
+}
+
 #undef TILEMIX_R8
 #undef TILEMIX_W8
 
