@@ -10,6 +10,8 @@ quoted on.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--p P]
   python bench.py --impl reference ...   (the reference's CPU path, rank 0)
+  python bench.py --op backward ...      (the unrouted attention's backward on the
+                                          config's shapes; no reference counterpart)
 
 Multi-GPU (torchrun, one process per GPU): the batch's B*H heads are split
 into contiguous per-rank shards (strong scaling: the job is one config-3 batch
@@ -60,6 +62,9 @@ def parse_args():
                          "single-term fp16 P where it is <= 3.5 (tilemix_attention_batched_hinted)")
     ap.add_argument("--scaling", default="strong", choices=["weak", "strong"],
                     help="strong (default): the batch's heads are split over ranks; weak: every rank runs a full batch")
+    ap.add_argument("--op", default="attention", choices=["attention", "backward"],
+                    help="attention (default): the routed forward hot path; backward: dQ, dK, dV of the unrouted "
+                         "attention (tilemix_attention_backward on the training forward's row LSE)")
     return ap.parse_args()
 
 
@@ -507,6 +512,180 @@ def run_tilemix(args, rank, world, local):
     emit(line)
 
 
+# ------------------------------------------------------------ backward arm
+def cpu_backward_sample(S: int, D: int, scale: float, causal: bool, target_s: float) -> dict:
+    """The same gradient formula in float32 torch autograd on the host cores,
+    on whole heads at the config's S and D: the CPU baseline of the backward
+    line (the reference has no backward to time)."""
+    import torch
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(7)
+    q, k, v, do = (torch.randn((1, S, D), generator=g) for _ in range(4))
+
+    def one():
+        qg, kg, vg = (t.clone().requires_grad_() for t in (q, k, v))
+        s = scale * qg @ kg.transpose(-1, -2)
+        if causal:
+            s = s.masked_fill(torch.ones(S, S, dtype=torch.bool).triu(1), float("-inf"))
+        o = torch.softmax(s, -1) @ vg
+        o.backward(do)
+    t0 = time.perf_counter()
+    one()
+    per_head = time.perf_counter() - t0
+    heads = max(1, min(64, int(target_s / max(per_head, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(heads):
+        one()
+    secs = time.perf_counter() - t0
+    flops = 2.5 * 4.0 * heads * S * S * D * (0.5 if causal else 1.0)
+    return {"value": round(flops / secs / 1e12, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{heads} head(s) of S={S}, D={D}{' causal' if causal else ''} through float32 torch autograd "
+                      f"of softmax(score_scale q k^T) v on {threads} threads ({secs:.1f} s); the reference has no "
+                      f"backward, so this is the formula, not the reference's code"}
+
+
+def run_backward(args, rank, world, local):
+    """dQ, dK, dV of the unrouted attention on the config's shapes: setup runs
+    the training forward once (tilemix_attention_batched_lse: O and the row
+    LSE); one step = tilemix_attention_backward on that LSE (row kernel: dQ
+    and D = rowsum(dO * O); column kernel: dK, dV). Work counted as the five
+    gradient products, 10 * S^2 * D per head (2.5x the forward), halved for
+    causal."""
+    import torch
+    import tilemix_b200 as tm
+    from tilemix_b200 import sharding, workloads
+
+    cfg0 = workloads.config(args.config)
+    total_heads = cfg0["B"] * cfg0["H"]
+    if args.scaling == "strong":
+        _, my_heads = sharding.shard_heads(total_heads, world, rank)
+    else:
+        my_heads = total_heads
+    w = workloads.make_inputs(args.config, batch=1, heads=my_heads, seed=sharding.rank_seed(cfg0["seed"], rank),
+                              device="cuda")
+    cfg, H, S, D = w["cfg"], w["heads"], w["S"], w["D"]
+    causal, scale = cfg["causal"], w["score_scale"]
+    q, k, v = w["q"], w["k"], w["v"]
+    g = torch.Generator(device="cuda").manual_seed(cfg0["seed"] + 101 + rank)
+    do = torch.randn((H, S, D), generator=g, device="cuda").half()
+    o = torch.empty((H, S, D), dtype=torch.float32, device="cuda")
+    dq, dk, dv = (torch.empty((H, S, D), dtype=torch.float32, device="cuda") for _ in range(3))
+    lse = torch.empty((H, S), dtype=torch.float32, device="cuda")
+    dsum = torch.empty((H, S), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def forward():
+        tm.check(tm.tilemix_attention_batched_lse(q, k, v, o, lse, H, S, S, D, scale, causal, stream), "forward")
+
+    def backward():
+        tm.check(tm.tilemix_attention_backward(q, k, v, o, do, dq, dk, dv, lse, dsum, H, S, S, D, scale, causal,
+                                               stream, lse_from_forward=True), "backward")
+
+    forward()
+    for _ in range(args.warmup):
+        backward()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    n = args.steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    t_start = time.time()
+    e0.record(stream)
+    for _ in range(n):
+        backward()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks.mark(t_start, time.time())
+    barrier(world)
+    clk = clocks.stop()
+    step_ms = reduce_max(e0.elapsed_time(e1) / n, world)
+    # the forward that produces O and the LSE, timed alone for the training step
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(5):
+        forward()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    fwd_ms = reduce_max(f0.elapsed_time(f1) / 5, world)
+    err, status = tm.read_and_clear_status()
+    tm.check(err, "status")
+    if status:
+        raise SystemExit(f"kernel watchdog reported status {status:#x}")
+
+    # end to end through the C-ABI with host buffers: per step the H2D copies of
+    # Q, K, V and dO from pinned memory, the training forward, the backward and
+    # the D2H copies of dQ, dK, dV
+    hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
+    hdq, hdk, hdv = (torch.empty((H, S, D), dtype=torch.float32).pin_memory() for _ in range(3))
+
+    def e2e_step():
+        for dst, src in ((q, hq), (k, hk), (v, hv), (do, hdo)):
+            dst.copy_(src, non_blocking=True)
+        forward()
+        backward()
+        for dst, src in ((hdq, dq), (hdk, dk), (hdv, dv)):
+            dst.copy_(src, non_blocking=True)
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_steps = max(1, min(n, 3))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = reduce_max(a.elapsed_time(b) / e2e_steps, world)
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_backward_sample(S, D, scale, causal, args.cpu_seconds)
+    if rank != 0:
+        return
+    peaks = measured_peaks()
+    f_bwd = 2.5 * workloads.effective_flops(cfg, H)          # this rank's gradient products
+    job = 2.5 * (workloads.effective_flops(cfg0) * (world if args.scaling == "weak" else 1))
+    achieved = f_bwd / (step_ms * 1e-3) / 1e12
+    value = job / (step_ms * 1e-3) / 1e12
+    line = {
+        "metric": "attention backward effective TFLOP/s (dQ, dK, dV; 10*S^2*D per head, causal halved), B200",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": n, "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+        "dtype": "f16 (f32 accumulate)", "data": "synthetic",
+        "config": {"workload": f"{args.config} shapes, unrouted: B{cfg0['B']} H{cfg0['H']} S{S} D{D}"
+                               f"{' causal' if causal else ''}, backward from the training forward's LSE",
+                   "B": cfg0["B"], "H": cfg0["H"], "S": S, "D": D, "causal": causal,
+                   "parallelism": f"heads over {world} GPU rank(s) ({args.scaling}), no collective",
+                   "l2": "inputs larger than L2 (126 MiB); no flush"},
+        "per_gpu_heads": H,
+        "training_forward_ms": round(fwd_ms, 4),
+        "training_step_tflops": round(3.5 * workloads.effective_flops(cfg, H) / ((fwd_ms + step_ms) * 1e-3) / 1e12, 2),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                     "peak_source": f"{peaks['source']} bf16 dense (burst), MEASURED_PEAKS.json (fp16 runs at the "
+                                    f"bf16 rate)",
+                     "traffic": None,
+                     "kernel": "backward_rows_kernel + backward_cols_kernel",
+                     "work": "five gradient products (S recomputed counts once): 10*S^2*D per head, causal halved; "
+                             "the kernels execute seven (S and dP in both kernels)"},
+        "e2e": {"value": round(job * (3.5 / 2.5) / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 4 * q.numel() * 2, "d2h_bytes_per_step": 3 * dq.numel() * 4,
+                "ms_per_step": round(e2e_ms, 3),
+                "api": "H2D of Q, K, V, dO; tilemix_attention_batched_lse; tilemix_attention_backward; D2H of dQ, "
+                       "dK, dV (C-ABI, pinned host buffers); value counts forward + backward work"},
+        "clocks": clk,
+        "gpu_launches": 2 * n,
+        "repo_native_so": repo_libraries(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    emit(line)
+
+
 # ----------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
     """The reference's own CPU implementation of the path on the host cores,
@@ -609,7 +788,13 @@ def main():
     claim_stdout()
     rank, world, local = dist_setup(args)
     try:
-        if args.impl == "reference":
+        if args.op == "backward":
+            if args.impl == "reference":
+                if rank == 0:
+                    emit({"impl": "reference", "unavailable": "the reference has no backward pass (forward only)"})
+            else:
+                run_backward(args, rank, world, local)
+        elif args.impl == "reference":
             run_reference(args, rank, world)
         else:
             run_tilemix(args, rank, world, local)

@@ -101,3 +101,22 @@ def test_int8_bias_constants():
     bits = (0x4B400000 + dots).astype(np.uint32)
     back = bits.view(np.float32).astype(np.float64) - 12582912.0
     assert np.array_equal(back, dots.astype(np.float64))
+
+
+def test_backward_reference_arm_says_unavailable():
+    """The reference is forward only: `--op backward --impl reference` prints
+    its one `unavailable` line and exits 0."""
+    env = dict(os.environ, WORLD_SIZE="1", RANK="0", LOCAL_RANK="0")
+    proc = subprocess.run([sys.executable, str(REPO / "bench.py"), "--op", "backward", "--impl", "reference"],
+                          cwd=REPO, env=env, capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = proc.stdout.splitlines()
+    assert len(lines) == 1, proc.stdout
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and "backward" in line["unavailable"]
+
+
+def test_backward_cpu_sample_is_bounded_and_positive():
+    bench = _bench_module()
+    c = bench.cpu_backward_sample(256, 64, 0.125, True, 0.2)
+    assert c["value"] > 0 and c["kind"] == "port" and c["cores"] >= 1

@@ -3,20 +3,23 @@
 //   O = softmax(score_scale * Q K^T [+ causal mask]) V
 // given dO, for the fp16 Q, K, V the forward takes. Two kernels, no atomics:
 //
-//   row kernel (one CTA per 128-row query tile): pass 1 recomputes S = Q K^T
-//     for the row log-sum-exp (log2 units), D = rowsum(dO * O) comes from the
-//     fp32 O; pass 2 recomputes S and dP = dO V^T, forms
-//     dS = P * (dP - D) * score_scale and accumulates dQ += dS K. It writes
-//     dQ and the per-row statistics (LSE, D) the column kernel reads.
+//   row kernel (one CTA per 128-row query tile): unless the forward's row
+//     log-sum-exp is given, pass 1 recomputes S = Q K^T for it (log2 units);
+//     D = rowsum(dO * O) comes from the fp32 O; pass 2 recomputes S and
+//     dP = dO V^T, forms dS = P * (dP - D) * score_scale and accumulates
+//     dQ += dS K. It writes dQ and the per-row statistics (LSE, D) the column
+//     kernel reads.
 //   column kernel (one CTA per 128-key tile): for every query block that can
 //     see the tile, S^T = K Q^T and dP^T = V dO^T, P^T and dS^T from the row
 //     statistics, then dV += P^T dO and dK += dS^T Q.
 //
 // Both kernels work in sub-blocks of 64 columns (keys for the row kernel,
-// queries for the column kernel) so that the products of two sub-blocks fit in
-// TMEM next to the accumulators: while the elementwise warps turn sub-block u
-// into P / dS, the tensor core already computes the S and dP of sub-block u + 1
-// into the other buffer, then the accumulation products of u.
+// queries for the column kernel) so that the products of more than one
+// sub-block fit in TMEM next to the accumulators: while the elementwise warps
+// turn sub-block u into P / dS, the tensor core already computes the S and dP
+// of sub-block u + 1 (each TMEM slot is released as soon as its last reader is
+// done), and the accumulation products of u follow. The row kernel keeps Q and
+// dO in TMEM, so its S and dP products read only K / V from shared memory.
 //
 // Conventions follow the forward: operand tiles loaded by TMA 128-byte
 // swizzled; S-like products as SS MMAs (kind::f16, fp32 in TMEM, K-major
@@ -141,7 +144,8 @@ struct BwdParams {
 // Shared memory of both kernels: one resident 128-row tile pair (A0, A1) and
 // two stages of a streamed pair (B0, B1), each tile kAtoms atoms of 16 KB,
 // 1024-byte aligned for the 128-byte swizzle; then row statistics, barriers
-// and the TMEM base / abort flag.
+// and the TMEM base / abort flag. The row kernel turns A0 / A1 into a third
+// K / V stage once Q and dO are in TMEM.
 template <int kAtoms>
 struct BwdSmem {
     static constexpr uint32_t kTile = kAtoms * kAtom;
