@@ -58,7 +58,7 @@ def _worker(rank, world, port, results):
 def test_gloo_world2_max_and_shards():
     world = 2
     port = _free_port()
-    manager = mp.Manager()
+    manager = mp.get_context("spawn").Manager()   # no fork of this (multi-threaded) process
     results = manager.dict()
     mp.spawn(_worker, args=(world, port, results), nprocs=world, join=True)
     assert results[0][0] == results[1][0] == 2.5          # slowest rank
