@@ -62,6 +62,8 @@ def parse_args():
                          "single-term fp16 P where it is <= 3.5 (tilemix_attention_batched_hinted)")
     ap.add_argument("--scaling", default="strong", choices=["weak", "strong"],
                     help="strong (default): the batch's heads are split over ranks; weak: every rank runs a full batch")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="--op backward only: run this many of the config's B*H heads (small profiling captures)")
     ap.add_argument("--op", default="attention", choices=["attention", "backward"],
                     help="attention (default): the routed forward hot path; backward: dQ, dK, dV of the unrouted "
                          "attention (tilemix_attention_backward on the training forward's row LSE)")
@@ -529,6 +531,7 @@ def cpu_backward_sample(S: int, D: int, scale: float, causal: bool, target_s: fl
             s = s.masked_fill(torch.ones(S, S, dtype=torch.bool).triu(1), float("-inf"))
         o = torch.softmax(s, -1) @ vg
         o.backward(do)
+    one()                                  # warm-up: thread pool, allocator
     t0 = time.perf_counter()
     one()
     per_head = time.perf_counter() - t0
@@ -556,6 +559,8 @@ def run_backward(args, rank, world, local):
     from tilemix_b200 import sharding, workloads
 
     cfg0 = workloads.config(args.config)
+    if args.heads is not None:
+        cfg0 = workloads.config(args.config, B=1, H=args.heads)
     total_heads = cfg0["B"] * cfg0["H"]
     if args.scaling == "strong":
         _, my_heads = sharding.shard_heads(total_heads, world, rank)
