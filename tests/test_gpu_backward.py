@@ -231,3 +231,20 @@ def test_autograd_through_the_training_operator():
     for got, ref, name in ((qg.grad, dq_ref, "dQ"), (kg.grad, dk_ref, "dK"), (vg.grad, dv_ref, "dV")):
         assert got.dtype == torch.float16
         assert_close(got.float(), ref, name)
+
+
+@pytest.mark.gpu
+def test_backward_at_config3_sequence_length():
+    """Two heads at config 3's S = 4096, d = 128, causal, from the forward's
+    LSE (the training path bench.py --op backward measures), against float64
+    autograd: the accumulations run over 32 key or query blocks here."""
+    heads, m, n, d = 2, 4096, 4096, 128
+    q, k, v, do = inputs(heads, m, n, d, seed=4096)
+    scale = 1.0 / math.sqrt(d)
+    o, lse_fwd = forward_lse(q, k, v, scale, True)
+    _, dq_ref, dk_ref, dv_ref = reference_grads(q, k, v, do, scale, True)
+    dq, dk, dv, _, _ = backward(q, k, v, o, do, scale, True, lse_in=lse_fwd)
+    assert_close(dq, dq_ref, "dQ")
+    assert_close(dk, dk_ref, "dK")
+    assert_close(dv, dv_ref, "dV")
+    assert tm.read_and_clear_status() == (0, 0)
