@@ -148,6 +148,32 @@ def test_fake_shapes_of_the_newer_operators():
         assert w.shape == (3 * 19,) and w.dtype == torch.int64
 
 
+def test_fake_shapes_of_the_training_operators():
+    with FakeTensorMode():
+        q = torch.empty((3, 300, 128), dtype=torch.float16)
+        k = torch.empty((3, 257, 128), dtype=torch.float16)
+        v = torch.empty((3, 257, 128), dtype=torch.float16)
+        o, lse = torch.ops.tilemix.attention_lse(q, k, v, 0.088, True)
+        assert o.shape == q.shape and o.dtype == torch.float32
+        assert lse.shape == (3, 300) and lse.dtype == torch.float32
+        do = torch.empty((3, 300, 128), dtype=torch.float16)
+        dq, dk, dv = torch.ops.tilemix.attention_backward(q, k, v, o, do, lse, 0.088, True)
+        assert dq.shape == q.shape and dk.shape == k.shape and dv.shape == v.shape
+        assert dq.dtype == dk.dtype == dv.dtype == torch.float32
+        dq2, _, _ = torch.ops.tilemix.attention_backward(q, k, v, o, do, None, 0.088, False)
+        assert dq2.shape == q.shape
+
+
+def test_backward_operator_rejects_bad_tensors_before_the_c_abi():
+    q = torch.zeros((2, 64, 64), dtype=torch.float16)
+    o = torch.zeros((2, 64, 64), dtype=torch.float32)
+    # host tensors (no CUDA device): rejected by the checks, not by a kernel
+    with pytest.raises(ValueError):
+        torch.ops.tilemix.attention_backward(q, q, q, o, q, None, 0.125, False)
+    with pytest.raises(ValueError):
+        torch.ops.tilemix.attention_lse(q, q, q, 0.125, False)
+
+
 @pytest.mark.gpu
 def test_newer_operators_match_the_c_abi():
     import tilemix_b200 as tm
