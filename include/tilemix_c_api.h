@@ -240,6 +240,20 @@ int tilemix_read_and_clear_status(unsigned int* status);
 int tilemix_watchdog_selftest(const void* Q, const void* K, const void* V, float* O, int heads, int M,
                               int N, int d, float score_scale, unsigned int wait_limit_us, void* stream);
 
+/* Backward watchdog self-test (no counterpart in the reference; for tests
+ * only): tilemix_attention_backward_c (recomputing the row LSE, not causal)
+ * with the column kernel built so that one elementwise warp of each CTA
+ * withholds its first "P ready" arrival and every wait of that kernel is
+ * limited to wait_limit_us microseconds (1..1000000). The accumulation warp's
+ * wait runs out, the kernel records bit 16 in the status word that
+ * tilemix_read_and_clear_status returns, every role drains its own copies and
+ * MMAs and returns. dQ, dK, dV are not valid afterwards. d must be 128
+ * (cudaErrorNotSupported otherwise). */
+int tilemix_backward_watchdog_selftest(const void* Q, const void* K, const void* V, const float* O, const void* dO,
+                                       float* dQ, float* dK, float* dV, float* lse, float* dsum, int heads,
+                                       int M, int N, int d, float score_scale, unsigned int wait_limit_us,
+                                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,3 +57,48 @@ def test_selftest_rejects_bad_limits_without_a_gpu():
     fake = 1 << 20
     assert tm.watchdog_selftest(fake, fake, fake, fake, 1, 128, 128, 128, 0.1, 0) == tm.cudaErrorInvalidValue
     assert tm.watchdog_selftest(fake, fake, fake, fake, 1, 128, 128, 128, 0.1, 2_000_000) == tm.cudaErrorInvalidValue
+
+
+@pytest.mark.gpu
+def test_backward_withheld_arrival_times_out_drains_and_the_next_launch_is_correct():
+    """The backward's bounded waits, exercised the same way: its column kernel
+    withholds one P-ready arrival per CTA with waits limited to 2 ms."""
+    heads, m, d = 2, 512, 128
+    g = torch.Generator(device="cpu").manual_seed(13)
+    q, k, v, do = (torch.randn((heads, m, d), generator=g).half().cuda() for _ in range(4))
+    scale = 1.0 / math.sqrt(d)
+    o = torch.empty((heads, m, d), dtype=torch.float32, device="cuda")
+    tm.check(tm.tilemix_attention_batched(q, k, v, o, heads, m, m, d, scale), "forward")
+    dq, dk, dv = (torch.empty((heads, m, d), dtype=torch.float32, device="cuda") for _ in range(3))
+    stats = torch.empty((2, heads, m), dtype=torch.float32, device="cuda")
+    assert tm.read_and_clear_status() == (0, 0)
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    assert tm.backward_watchdog_selftest(q, k, v, o, do, dq, dk, dv, stats[0], stats[1], heads, m, m, d, scale,
+                                         2000) == 0
+    err, status = tm.read_and_clear_status()          # synchronises
+    elapsed = time.perf_counter() - t0
+    assert err == 0, err
+    assert status & tm.STATUS_BACKWARD_WAIT, status
+    assert not status & tm.STATUS_BACKWARD_DRAIN, status
+    assert status & ~(tm.STATUS_BACKWARD_WAIT | tm.STATUS_BACKWARD_DRAIN) == 0, status
+    assert 0.002 <= elapsed < 0.5, elapsed
+
+    # the context is fine: a normal backward on the same stream is correct
+    tm.check(tm.tilemix_attention_backward(q, k, v, o, do, dq, dk, dv, stats[0], stats[1], heads, m, m, d, scale),
+             "backward")
+    torch.cuda.synchronize()
+    assert tm.read_and_clear_status() == (0, 0)
+    qd, kd, vd = (t.double().requires_grad_() for t in (q, k, v))
+    (torch.softmax(scale * qd @ kd.transpose(-1, -2), -1) @ vd).backward(do.double())
+    for got, ref in ((dq, qd.grad), (dk, kd.grad), (dv, vd.grad)):
+        assert float((got.double() - ref).norm() / ref.norm()) <= 4e-3
+
+
+def test_backward_selftest_rejects_bad_arguments_without_a_gpu():
+    fake = 1 << 20
+    args = [fake] * 10 + [1, 128, 128, 128, 0.1]
+    assert tm.backward_watchdog_selftest(*args, 0) == tm.cudaErrorInvalidValue
+    assert tm.backward_watchdog_selftest(*args, 2_000_000) == tm.cudaErrorInvalidValue
+    assert tm.backward_watchdog_selftest(*(args[:13] + [64, 0.1]), 2000) == tm.cudaErrorNotSupported

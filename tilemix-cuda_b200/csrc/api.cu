@@ -620,6 +620,28 @@ int tilemix_attention_backward_c(const void* Q, const void* K, const void* V, co
         lse_from_forward != 0, static_cast<cudaStream_t>(stream)));
 }
 
+int tilemix_backward_watchdog_selftest(const void* Q, const void* K, const void* V, const float* O, const void* dO,
+                                       float* dQ, float* dK, float* dV, float* lse, float* dsum, int heads, int M,
+                                       int N, int d, float score_scale, unsigned int wait_limit_us, void* stream) {
+    if (wait_limit_us == 0 || wait_limit_us > 1000000u) return static_cast<int>(cudaErrorInvalidValue);
+    if (!Q || !K || !V || !O || !dO || !dQ || !dK || !dV || !lse || !dsum || heads <= 0 || M <= 0 || N <= 0 ||
+        d <= 0 || !std::isfinite(score_scale)) {
+        return static_cast<int>(cudaErrorInvalidValue);
+    }
+    if (d != 128) return static_cast<int>(cudaErrorNotSupported);
+    if (!fits(heads, M, d) || !fits(heads, N, d)) return static_cast<int>(cudaErrorInvalidValue);
+    const cudaError_t status = check_device();
+    if (status != cudaSuccess) return static_cast<int>(status);
+    tilemix::AttentionBackwardProblem prob{};
+    prob.q = static_cast<const __half*>(Q); prob.k = static_cast<const __half*>(K);
+    prob.v = static_cast<const __half*>(V); prob.o = O; prob.dout = static_cast<const __half*>(dO);
+    prob.dq = dQ; prob.dk = dK; prob.dv = dV; prob.lse = lse; prob.dsum = dsum;
+    prob.heads = heads; prob.M = M; prob.N = N; prob.d = d;
+    prob.score_scale = score_scale;
+    prob.watchdog_limit_ns = 1000ull * wait_limit_us;
+    return static_cast<int>(tilemix::launch_attention_backward(prob, static_cast<cudaStream_t>(stream)));
+}
+
 int tilemix_read_and_clear_status(unsigned int* status) {
     if (!status) return static_cast<int>(cudaErrorInvalidValue);
     return static_cast<int>(tilemix::read_and_clear_status(status));

@@ -78,14 +78,15 @@ enum : unsigned int { kBwdStatusWait = 1u << 4, kBwdStatusDrain = 1u << 5 };
 
 // Bounded wait by all 32 lanes; warp-uniform result. A wait that runs out
 // raises the CTA's abort flag and records the status bit.
-__device__ __forceinline__ bool bw_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool bw_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                        uint64_t limit_ns = kLimitNs) {
     bool ok = mbar_try_wait(bar, parity);
     if (!ok) {
         const uint64_t start = global_timer_ns();
         while (true) {
             if (mbar_try_wait_suspend(bar, parity, kSuspend)) { ok = true; break; }
             if (*abort_flag) break;
-            if (global_timer_ns() - start > kLimitNs) {
+            if (global_timer_ns() - start > limit_ns) {
                 *abort_flag = 1;
                 atomicOr(&g_backward_status, kBwdStatusWait);
                 break;
@@ -139,6 +140,7 @@ struct BwdParams {
     float c;                   // score_scale * log2(e)
     float scale;               // score_scale
     int causal;
+    uint64_t limit_ns;         // limit of one pipeline wait (1 s; shorter only in the watchdog self-test)
 };
 
 // Shared memory of both kernels: one resident 128-row tile pair (A0, A1) and
@@ -338,9 +340,9 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             const int j = pass2 ? l - npass1 : l;
             bool free_ok = true;
             if (n > 0) {
-                free_ok = bw_wait(bar(kBarBEmpty + st), (n - 1) & 1, abort_flag);
+                free_ok = bw_wait(bar(kBarBEmpty + st), (n - 1) & 1, abort_flag, p.limit_ns);
             } else if (st == 2) {
-                free_ok = bw_wait(bar(kBarAFree), 0, abort_flag);
+                free_ok = bw_wait(bar(kBarAFree), 0, abort_flag, p.limit_ns);
             }
             if (!free_ok) break;
             if (elect_one()) {
@@ -375,12 +377,12 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const uint32_t dhi = smem_desc_sw128_hi(1024);
         const int ksteps = p.d / 16;
         // Q and dO are in TMEM once the elementwise warps have copied them
-        bool ok = bw_wait(bar(kBarOps), 0, abort_flag);
+        bool ok = bw_wait(bar(kBarOps), 0, abort_flag, p.limit_ns);
         // pass 1: S of sub-block v (keys 64 v ..) into ring slot v % kRing
         for (int v = 0; ok && v < 2 * npass1; ++v) {
             const int j = v >> 1, h = v & 1, st = j % kStages;
-            if (h == 0) ok = bw_wait(bar(kBarBFull + st), (j / kStages) & 1, abort_flag);
-            if (ok && v >= kRing) ok = bw_wait(bar(kBarS1Free + v % kRing), ((v - kRing) / kRing) & 1, abort_flag);
+            if (h == 0) ok = bw_wait(bar(kBarBFull + st), (j / kStages) & 1, abort_flag, p.limit_ns);
+            if (ok && v >= kRing) ok = bw_wait(bar(kBarS1Free + v % kRing), ((v - kRing) / kRing) & 1, abort_flag, p.limit_ns);
             if (!ok) break;
             tc_fence_after();
             if (elect_one()) {
@@ -394,12 +396,12 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         // pass 2 starts once every row's LSE is known (the pass-1 slots have
         // then been read). S(v) and dP(v) go into buffer v & 1 once the dQ
         // product that read sub-block v - 2 from it has completed.
-        if (!kHaveLse && ok) ok = bw_wait(bar(kBarStats), 0, abort_flag);
+        if (!kHaveLse && ok) ok = bw_wait(bar(kBarStats), 0, abort_flag, p.limit_ns);
         for (int v = 0; ok && v < nsub; ++v) {
             const int l = npass1 + (v >> 1), st = l % kStages, h = v & 1, slot = v % kSSlots;
-            if (h == 0) ok = bw_wait(bar(kBarBFull + st), (l / kStages) & 1, abort_flag);
+            if (h == 0) ok = bw_wait(bar(kBarBFull + st), (l / kStages) & 1, abort_flag, p.limit_ns);
             // S(v) once dQ(v - 3) has read the slot
-            if (ok && v >= kSSlots) ok = bw_wait(bar(kBarAcc + slot), ((v - kSSlots) / kSSlots) & 1, abort_flag);
+            if (ok && v >= kSSlots) ok = bw_wait(bar(kBarAcc + slot), ((v - kSSlots) / kSSlots) & 1, abort_flag, p.limit_ns);
             if (!ok) break;
             tc_fence_after();
             if (elect_one()) {
@@ -408,7 +410,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             }
             __syncwarp();
             // dP(v) once the elementwise warps have loaded dP(v - 1)
-            if (v >= 1) ok = bw_wait(bar(kBarDpFree), (v - 1) & 1, abort_flag);
+            if (v >= 1) ok = bw_wait(bar(kBarDpFree), (v - 1) & 1, abort_flag, p.limit_ns);
             if (!ok) break;
             tc_fence_after();
             if (elect_one()) {
@@ -428,7 +430,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         bool ok = true;
         for (int v = 0; ok && v < nsub; ++v) {
             const int l = npass1 + (v >> 1), st = l % kStages, h = v & 1, slot = v % kSSlots;
-            ok = bw_wait(bar(kBarP + slot), (v / kSSlots) & 1, abort_flag);
+            ok = bw_wait(bar(kBarP + slot), (v / kSSlots) & 1, abort_flag, p.limit_ns);
             if (!ok) break;
             tc_fence_after();
             if (elect_one()) {
@@ -451,7 +453,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const bool row_ok = row < p.M;
         const uint32_t lb = static_cast<uint32_t>(quad * 32) << 16;
         float* stats = reinterpret_cast<float*>(smem + L::kStats);   // [ch][max, sum, D][128]
-        bool ok = bw_wait(bar(kBarA), 0, abort_flag);
+        bool ok = bw_wait(bar(kBarA), 0, abort_flag, p.limit_ns);
         // the MMA operands: warp quarter ch copies this row's atom ch % kAtoms
         // of Q (ch < kAtoms) or of dO (kAtoms <= ch < 2 kAtoms) into TMEM
         if (ok && ch < 2 * kAtoms) {
@@ -499,7 +501,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             // visible keys
             float m = -INFINITY, l = 0.0f;
             for (int v = 0; ok && v < nsub; ++v) {
-                ok = bw_wait(bar(kBarS1 + v % kRing), (v / kRing) & 1, abort_flag);
+                ok = bw_wait(bar(kBarS1 + v % kRing), (v / kRing) & 1, abort_flag, p.limit_ns);
                 if (!ok) break;
                 tc_fence_after();
                 uint32_t x[kColsPer];
@@ -581,7 +583,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const float2 nd2 = make_float2(-dsum * p.scale, -dsum * p.scale);
         for (int v = 0; ok && v < nsub; ++v) {
             const int slot = v % kSSlots;
-            ok = bw_wait(bar(kBarS + slot), (v / kSSlots) & 1, abort_flag);
+            ok = bw_wait(bar(kBarS + slot), (v / kSSlots) & 1, abort_flag, p.limit_ns);
             if (!ok) break;
             tc_fence_after();
             const uint32_t buf = tmem + lb + kSub * static_cast<uint32_t>(slot) + kColsPer * ch;
@@ -618,7 +620,7 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             if (lane == 0) mbar_arrive(bar(kBarP + slot));
         }
         // dQ out: 32-column chunks shared round-robin by the quarters
-        if (ok) ok = bw_wait(bar(kBarDone), 0, abort_flag);
+        if (ok) ok = bw_wait(bar(kBarDone), 0, abort_flag, p.limit_ns);
         if (ok) {
             tc_fence_after();
             float* out = p.dq + (static_cast<std::size_t>(head) * p.M + row) * p.d;
@@ -654,7 +656,10 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 // elementwise warps have loaded them), two operand slots at 128 and 192 (P^T
 // packed in the first 32 columns, dS^T in the next 32; sub-block u in slot
 // u & 1), dV at 256, dK at 384.
-template <int kAtoms, int kSteps>
+// kWithhold: watchdog self-test build: elementwise warp 0 withholds its first
+// P-ready arrival, so the accumulation warp's wait for it runs out (the
+// output is then not valid; the status word is).
+template <int kAtoms, int kSteps, bool kWithhold = false>
 __global__ void __launch_bounds__(kBwdThreads, 1)
 backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -692,7 +697,7 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             int issued = 0;
             for (int b = 0; b < nq; ++b) {
                 const int s = b & 1, i = i0 + b;
-                if (!bw_wait(bar(kBarBEmpty + s), ((b >> 1) & 1) ^ 1, abort_flag)) break;
+                if (!bw_wait(bar(kBarBEmpty + s), ((b >> 1) & 1) ^ 1, abort_flag, p.limit_ns)) break;
                 if (elect_one()) {
                     // L2 prefetch of the block two loads ahead
                     if (b + 2 < nq) {
@@ -724,12 +729,12 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             const uint32_t v_lo = smem_desc_sw128_lo(sbase + L::kA1, 16);
             auto q_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, lbo); };
             auto do_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, lbo); };
-            bool ok = bw_wait(bar(kBarA), 0, abort_flag);
+            bool ok = bw_wait(bar(kBarA), 0, abort_flag, p.limit_ns);
             // S^T(u), dP^T(u) once the elementwise warps have loaded u - 1
             for (int u = 0; ok && u < nsub; ++u) {
                 const int b = u >> 1, s = b & 1, h = u & 1;
-                if (h == 0) ok = bw_wait(bar(kBarBFull + s), (b >> 1) & 1, abort_flag);
-                if (ok && u >= 1) ok = bw_wait(bar(kBarDpFree), (u - 1) & 1, abort_flag);
+                if (h == 0) ok = bw_wait(bar(kBarBFull + s), (b >> 1) & 1, abort_flag, p.limit_ns);
+                if (ok && u >= 1) ok = bw_wait(bar(kBarDpFree), (u - 1) & 1, abort_flag, p.limit_ns);
                 if (!ok) break;
                 tc_fence_after();
                 if (elect_one()) {
@@ -752,7 +757,7 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             bool ok = true;
             for (int u = 0; ok && u < nsub; ++u) {
                 const int b = u >> 1, s = b & 1, h = u & 1;
-                ok = bw_wait(bar(kBarP + (u & 1)), (u >> 1) & 1, abort_flag);
+                ok = bw_wait(bar(kBarP + (u & 1)), (u >> 1) & 1, abort_flag, p.limit_ns);
                 if (!ok) break;
                 tc_fence_after();
                 if (elect_one()) {
@@ -807,7 +812,7 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 elem_sync();
                 if (b + 1 < nq) next_stat = stat_of(i + 1);
             }
-            if (ok) ok = bw_wait(bar(kBarS), u & 1, abort_flag);
+            if (ok) ok = bw_wait(bar(kBarS), u & 1, abort_flag, p.limit_ns);
             if (!ok) continue;
             tc_fence_after();
             uint32_t x[kColsPer], y[kColsPer];
@@ -819,7 +824,7 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarDpFree));
             // the operand slot is free once the products of u - 2 have read it
-            if (u >= 2) ok = bw_wait(bar(kBarAcc + (u & 1)), ((u - 2) >> 1) & 1, abort_flag);
+            if (u >= 2) ok = bw_wait(bar(kBarAcc + (u & 1)), ((u - 2) >> 1) & 1, abort_flag, p.limit_ns);
             if (!ok) continue;
             tc_fence_after();
             // this quarter's K step, packed: P^T at +8 ch, dS^T at 32 + 8 ch
@@ -857,7 +862,8 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kBarP + (u & 1)));
+            const bool withheld = kWithhold && u == 0 && warp == 0;
+            if (lane == 0 && !withheld) mbar_arrive(bar(kBarP + (u & 1)));
         }
         // dV / dK out: 32-column chunks shared round-robin by the quarters
         if (key < p.N && nq <= 0) {
@@ -870,7 +876,7 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 }
             }
         }
-        if (ok && nq > 0) ok = bw_wait(bar(kBarDone), 0, abort_flag);
+        if (ok && nq > 0) ok = bw_wait(bar(kBarDone), 0, abort_flag, p.limit_ns);
         if (ok && nq > 0) {
             tc_fence_after();
             #pragma unroll 1
@@ -932,10 +938,11 @@ bool encode_tile_map(CUtensorMap* map, const __half* base, int heads, int rows, 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int kAtoms, bool kHaveLse, int kSteps>
-cudaError_t launch_backward_atoms(const CUtensorMap* maps, const BwdParams& p, cudaStream_t stream) {
+template <int kAtoms, bool kHaveLse, int kSteps, bool kWithhold = false>
+cudaError_t launch_backward_atoms(const CUtensorMap* maps, const BwdParams& p, cudaStream_t stream,
+                                  uint64_t cols_limit_ns = kLimitNs) {
     auto rows = backward_rows_kernel<kAtoms, kHaveLse, kSteps>;
-    auto cols = backward_cols_kernel<kAtoms, kSteps>;
+    auto cols = backward_cols_kernel<kAtoms, kSteps, kWithhold>;
     // at least half the SM's shared memory: one CTA per SM, since each CTA
     // takes all 512 TMEM columns (a second one would only wait in its alloc)
     const int smem = static_cast<int>(BwdSmem<kAtoms>::kBytes > 120u * 1024u ? BwdSmem<kAtoms>::kBytes
@@ -957,7 +964,9 @@ cudaError_t launch_backward_atoms(const CUtensorMap* maps, const BwdParams& p, c
     rows<<<static_cast<unsigned>(row_grid), kBwdThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], p);
     status = cudaGetLastError();
     if (status != cudaSuccess) return status;
-    cols<<<static_cast<unsigned>(col_grid), kBwdThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], p);
+    BwdParams pc = p;
+    pc.limit_ns = cols_limit_ns;
+    cols<<<static_cast<unsigned>(col_grid), kBwdThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], pc);
     return cudaGetLastError();
 }
 
@@ -987,11 +996,18 @@ cudaError_t launch_attention_backward(const AttentionBackwardProblem& prob, cuda
     p.scale = prob.score_scale;
     p.c = prob.score_scale * kLog2e;
     p.causal = prob.causal ? 1 : 0;
+    p.limit_ns = kLimitNs;
     CUtensorMap maps[4];
     std::memset(maps, 0, sizeof(maps));
     if (!encode_tile_map(&maps[0], prob.q, p.heads, p.M, p.d) || !encode_tile_map(&maps[1], prob.dout, p.heads, p.M, p.d) ||
         !encode_tile_map(&maps[2], prob.k, p.heads, p.N, p.d) || !encode_tile_map(&maps[3], prob.v, p.heads, p.N, p.d)) {
         return cudaErrorInvalidValue;
+    }
+    if (prob.watchdog_limit_ns != 0) {
+        // self-test build (d = 128): the row kernel runs normally, the column
+        // kernel withholds one arrival with its waits limited as asked
+        if (p.d != 128) return cudaErrorNotSupported;
+        return launch_backward_atoms<2, false, 8, true>(maps, p, stream, prob.watchdog_limit_ns);
     }
     // d = 64 and d = 128 take the builds with the K loops unrolled
     if (p.d == 64) {

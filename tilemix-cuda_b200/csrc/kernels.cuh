@@ -112,6 +112,11 @@ struct AttentionBackwardProblem {
     float score_scale;
     bool causal;
     bool lse_ready;
+    // Watchdog self-test (d = 128 only): nonzero = the column kernel build in
+    // which one elementwise warp withholds its first P-ready arrival, its
+    // waits limited to this many ns (the gradients are not valid; the status
+    // word is).
+    unsigned long long watchdog_limit_ns;
 };
 cudaError_t launch_attention_backward(const AttentionBackwardProblem& problem, cudaStream_t stream);
 cudaError_t read_and_clear_backward_status(unsigned int* status);

@@ -113,6 +113,9 @@ def _load():
     lib.tilemix_attention_backward_c.restype = _I
     lib.tilemix_attention_batched_lse_c.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, _I, _P]
     lib.tilemix_attention_batched_lse_c.restype = _I
+    lib.tilemix_backward_watchdog_selftest.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I,
+                                                       ctypes.c_float, ctypes.c_uint, _P]
+    lib.tilemix_backward_watchdog_selftest.restype = _I
     return lib
 
 
@@ -146,7 +149,7 @@ C_ABI_SYMBOLS = (
     "tilemix_routing_word_count_c", "tilemix_routing_words_per_row_c",
     "tilemix_reference_shared_bytes", "tilemix_b200_shared_bytes_c",
     "tilemix_read_and_clear_status", "tilemix_watchdog_selftest", "tilemix_attention_backward_c",
-    "tilemix_attention_batched_lse_c",
+    "tilemix_attention_batched_lse_c", "tilemix_backward_watchdog_selftest",
 )
 
 
@@ -442,6 +445,18 @@ def tilemix_attention_backward(Q, K, V, O, dO, dQ, dK, dV, lse, dsum, heads: int
                                                   _addr(dK), _addr(dV), _addr(lse), _addr(dsum), heads, M, N, d,
                                                   float(score_scale), int(bool(causal)), int(bool(lse_from_forward)),
                                                   _stream(stream))
+
+
+def backward_watchdog_selftest(Q, K, V, O, dO, dQ, dK, dV, lse, dsum, heads: int, M: int, N: int, d: int,
+                               score_scale: float, wait_limit_us: int, stream=None) -> int:
+    """The backward with its column kernel built to withhold one P-ready
+    arrival per CTA, waits limited to wait_limit_us: the watchdog must record
+    STATUS_BACKWARD_WAIT and the kernels return. The gradients are not valid
+    afterwards. Returns a cudaError_t code."""
+    return _native().tilemix_backward_watchdog_selftest(_addr(Q), _addr(K), _addr(V), _addr(O), _addr(dO),
+                                                        _addr(dQ), _addr(dK), _addr(dV), _addr(lse), _addr(dsum),
+                                                        heads, M, N, d, float(score_scale), int(wait_limit_us),
+                                                        _stream(stream))
 
 
 def read_and_clear_status() -> tuple[int, int]:
