@@ -668,7 +668,7 @@ def run_backward(args, rank, world, local):
                    "l2": "inputs larger than L2 (126 MiB); no flush"},
         "per_gpu_heads": H,
         "training_forward_ms": round(fwd_ms, 4),
-        "training_step_tflops": round(3.5 * workloads.effective_flops(cfg, H) / ((fwd_ms + step_ms) * 1e-3) / 1e12, 2),
+        "training_step_tflops": round(job * 3.5 / 2.5 / ((fwd_ms + step_ms) * 1e-3) / 1e12, 2),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                      "peak_source": f"{peaks['source']} bf16 dense (burst), MEASURED_PEAKS.json (fp16 runs at the "
