@@ -521,6 +521,7 @@ def cpu_backward_sample(S: int, D: int, scale: float, causal: bool, target_s: fl
     line (the reference has no backward to time)."""
     import torch
     threads = torch.get_num_threads()
+    S_cfg, S = S, min(S, 4096)     # the S x S matrices of one head stay a few hundred MB
     g = torch.Generator().manual_seed(7)
     q, k, v, do = (torch.randn((1, S, D), generator=g) for _ in range(4))
 
@@ -542,7 +543,8 @@ def cpu_backward_sample(S: int, D: int, scale: float, causal: bool, target_s: fl
     secs = time.perf_counter() - t0
     flops = 2.5 * 4.0 * heads * S * S * D * (0.5 if causal else 1.0)
     return {"value": round(flops / secs / 1e12, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{heads} head(s) of S={S}, D={D}{' causal' if causal else ''} through float32 torch autograd "
+            "sample": f"{heads} head(s) of S={S}{f' (the config has S={S_cfg}; TFLOP/s compared per FLOP)' if S != S_cfg else ''}, "
+                      f"D={D}{' causal' if causal else ''} through float32 torch autograd "
                       f"of softmax(score_scale q k^T) v on {threads} threads ({secs:.1f} s); the reference has no "
                       f"backward, so this is the formula, not the reference's code"}
 
