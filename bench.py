@@ -654,6 +654,8 @@ def run_backward(args, rank, world, local):
     if rank != 0:
         return
     peaks = measured_peaks()
+    # what one step touches: Q, K, V, dO (fp16), O, dQ, dK, dV (fp32)
+    footprint_mib = (4 * q.numel() * 2 + 4 * o.numel() * 4) / 2**20
     f_bwd = 2.5 * workloads.effective_flops(cfg, H)          # this rank's gradient products
     job = 2.5 * (workloads.effective_flops(cfg0) * (world if args.scaling == "weak" else 1))
     achieved = f_bwd / (step_ms * 1e-3) / 1e12
@@ -667,7 +669,10 @@ def run_backward(args, rank, world, local):
                                f"{' causal' if causal else ''}, backward from the training forward's LSE",
                    "B": cfg0["B"], "H": cfg0["H"], "S": S, "D": D, "causal": causal,
                    "parallelism": f"heads over {world} GPU rank(s) ({args.scaling}), no collective",
-                   "l2": "inputs larger than L2 (126 MiB); no flush"},
+                   "l2": (f"inputs and outputs {footprint_mib:.0f} MiB per GPU, larger than L2 (126 MiB); no flush"
+                          if footprint_mib > 126 else
+                          f"inputs and outputs {footprint_mib:.0f} MiB per GPU fit in L2 (126 MiB): warm-L2 timing, "
+                          f"no flush")},
         "per_gpu_heads": H,
         "training_forward_ms": round(fwd_ms, 4),
         "training_step_tflops": round(job * 3.5 / 2.5 / ((fwd_ms + step_ms) * 1e-3) / 1e12, 2),
