@@ -248,3 +248,33 @@ def test_backward_at_config3_sequence_length():
     assert_close(dk, dk_ref, "dK")
     assert_close(dv, dv_ref, "dV")
     assert tm.read_and_clear_status() == (0, 0)
+
+
+EDGE_CASES = [
+    # heads, M, N, d, causal, score_scale (None: 1/sqrt(d))
+    (2, 200, 300, 32, False, None),
+    (1, 130, 257, 48, True, None),
+    (2, 256, 192, 96, False, None),
+    (1, 300, 300, 112, True, None),
+    (1, 1, 1, 64, False, None),        # one query, one key: P = 1, dS = 0
+    (1, 1, 700, 128, False, None),     # one query row against a long key range
+    (1, 700, 1, 64, True, None),       # one key, causal: every row sees only key 0
+    (2, 256, 256, 64, False, 0.0),     # score_scale 0: uniform softmax, dQ = dK = 0
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("heads,m,n,d,causal,scale", EDGE_CASES)
+def test_backward_edge_cases(heads, m, n, d, causal, scale):
+    q, k, v, do = inputs(heads, m, n, d, seed=heads * 7 + m * 3 + n + d)
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    o = forward(q, k, v, scale, causal)
+    _, dq_ref, dk_ref, dv_ref = reference_grads(q, k, v, do, scale, causal)
+    dq, dk, dv, _, _ = backward(q, k, v, o, do, scale, causal)
+    for got, ref, name in ((dq, dq_ref, "dQ"), (dk, dk_ref, "dK"), (dv, dv_ref, "dV")):
+        if float(ref.abs().max()) < 1e-12:
+            # an exactly-zero gradient (one key, or score_scale 0) must come out as (near) zero
+            assert float(got.abs().max()) <= 1e-5, (name, float(got.abs().max()))
+        else:
+            assert_close(got, ref, name)
+    assert tm.read_and_clear_status() == (0, 0)
