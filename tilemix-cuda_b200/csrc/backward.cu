@@ -653,9 +653,12 @@ backward_rows_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 // Column kernel: one CTA per (head, 128-key tile); K and V stay resident, the
 // query blocks that see the tile stream through (Q, dO) stages, each as two
 // 64-query sub-blocks. TMEM: S^T at 0 and dP^T at 64 (free again once the
-// elementwise warps have loaded them), two operand slots at 128 and 192 (P^T
-// packed in the first 32 columns, dS^T in the next 32; sub-block u in slot
-// u & 1), dV at 256, dK at 384.
+// elementwise warps have loaded them), the operand slot at 128 (P^T packed in
+// its first 32 columns, dS^T in the next 32; written once the previous
+// sub-block's accumulation products have read it), K at 192 (fp16 pairs: the
+// S^T product takes its A operand from TMEM, only dP^T = V dO^T reads both
+// operands from shared memory), dV at 256, dK at 384.
+constexpr uint32_t kColOp = 128, kColKc = 192;
 // kWithhold: watchdog self-test build: elementwise warp 0 withholds its first
 // P-ready arrival, so the accumulation warp's wait for it runs out (the
 // output is then not valid; the status word is).
@@ -725,11 +728,12 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             // S^T and dP^T products
             const uint32_t dhi = smem_desc_sw128_hi(1024);
             const int ksteps = p.d / 16;
-            const uint32_t k_lo = smem_desc_sw128_lo(sbase + L::kA0, 16);
             const uint32_t v_lo = smem_desc_sw128_lo(sbase + L::kA1, 16);
             auto q_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, lbo); };
             auto do_lo = [&](int s, uint32_t lbo) { return smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, lbo); };
             bool ok = bw_wait(bar(kBarA), 0, abort_flag, p.limit_ns);
+            // K is in TMEM once the elementwise warps have copied it
+            if (ok) ok = bw_wait(bar(kBarOps), 0, abort_flag, p.limit_ns);
             // S^T(u), dP^T(u) once the elementwise warps have loaded u - 1
             for (int u = 0; ok && u < nsub; ++u) {
                 const int b = u >> 1, s = b & 1, h = u & 1;
@@ -738,7 +742,7 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 if (!ok) break;
                 tc_fence_after();
                 if (elect_one()) {
-                    mma_sub<kSteps>(tmem, k_lo, q_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
+                    mma_sub_ts<kSteps>(tmem, tmem + kColKc, q_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
                     mma_sub<kSteps>(tmem + 64u, v_lo, do_lo(s, 16) + kHalfRows16 * h, dhi, ksteps);
                     tc_commit(bar(kBarS));
                 }
@@ -761,14 +765,14 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                 if (!ok) break;
                 tc_fence_after();
                 if (elect_one()) {
-                    const uint32_t op = tmem + 128u + 64u * static_cast<uint32_t>(u & 1);
+                    const uint32_t op = tmem + kColOp;
                     mma_acc<8>(tmem + 256u, op,
                                 smem_desc_sw128_lo(sbase + L::kB1 + s * L::kTile, kAtom) + kHalfRows16 * h, dhi, idesc_o,
                                 u > 0);
                     mma_acc<8>(tmem + 384u, op + 32u,
                                 smem_desc_sw128_lo(sbase + L::kB0 + s * L::kTile, kAtom) + kHalfRows16 * h, dhi, idesc_o,
                                 u > 0);
-                    tc_commit(bar(kBarAcc + (u & 1)));
+                    tc_commit(bar(kBarAcc));
                     if (h == 1) tc_commit(bar(kBarBEmpty + s));
                     if (u == nsub - 1) tc_commit(bar(kBarDone));
                 }
@@ -787,6 +791,18 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         float* stats = reinterpret_cast<float*>(smem + L::kStats);   // [block & 1][-LSE, -D scale][128]
         const float2 c2 = make_float2(p.c, p.c), sc2 = make_float2(p.scale, p.scale);
         bool ok = true;
+        if (nq > 0) {
+            // the S^T product's A operand: warp quarter ch < kAtoms copies
+            // this key row's atom ch of K into TMEM
+            ok = bw_wait(bar(kBarA), 0, abort_flag, p.limit_ns);
+            if (ok && ch < kAtoms) {
+                atom_row_to_tmem(smem + L::kA0, ch, r, tmem + lb + kColKc + 32u * ch);
+                tc_wait_st();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kBarOps));
+        }
         // Row statistics of query block i, staged once per block: thread
         // t < 128 holds -LSE of query t, thread 128 + t its -D * scale. Each
         // thread loads its raw value one block ahead and transforms it only
@@ -823,12 +839,6 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kBarDpFree));
-            // the operand slot is free once the products of u - 2 have read it
-            if (u >= 2) ok = bw_wait(bar(kBarAcc + (u & 1)), ((u - 2) >> 1) & 1, abort_flag, p.limit_ns);
-            if (!ok) continue;
-            tc_fence_after();
-            // this quarter's K step, packed: P^T at +8 ch, dS^T at 32 + 8 ch
-            const uint32_t op = tmem + lb + 128u + 64u * static_cast<uint32_t>(u & 1) + (kColsPer / 2) * ch;
             const int col0 = kSub * h + kColsPer * ch;     // query within the block
             const int q0 = i * kRows + col0;
             // no mask when every query of the sub-block exists and (causal)
@@ -857,6 +867,12 @@ backward_cols_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                     dst[e + f] = pack_half2(dv.x, dv.y);
                 }
             }
+            // the operand slot is free once the products of u - 1 have read it
+            if (u >= 1) ok = bw_wait(bar(kBarAcc), (u - 1) & 1, abort_flag, p.limit_ns);
+            if (!ok) continue;
+            tc_fence_after();
+            // this quarter's K step, packed: P^T at +8 ch, dS^T at 32 + 8 ch
+            const uint32_t op = tmem + lb + kColOp + (kColsPer / 2) * ch;
             tmem_st8(op, pt);
             tmem_st8(op + 32u, dst);
             tc_wait_st();
