@@ -397,6 +397,7 @@ def run_tilemix(args, rank, world, local):
     if policy:
         f_real = workloads.int8_fraction_from_words(words.cpu().numpy(), H, S, cfg["causal"])
     single_share = (float((v_absmax.float() <= 3.5).float().mean()) if args.v_hint else 0.0)
+    sweep = routing_sweep(args, cfg, w, out, quantized, stream, world) if not policy and not args.v_hint else None
     step_ms = reduce_max(total_ms / n, world)
     attn_avg = reduce_max(sum(attn_ms) / n, world)
     quant_avg = reduce_max(sum(quant_ms) / n, world)
@@ -509,9 +510,58 @@ def run_tilemix(args, rank, world, local):
                     if policy else {"kind": "mask", "note": "the config's Bernoulli 64x64 INT8 mask"}),
         "repo_native_so": repo_libraries(),
     }
+    if sweep is not None:
+        mix = workloads.mix_peak
+        for row in sweep:
+            meas = (mix(f_eff, row["int8_fraction_realised"], p_f16=peaks["bf16_tflops"] * 1e12,
+                        p_i8=i8_meas * 1e12) / 1e12 if i8_meas else None)
+            row["pct_of_mix_peak_measured"] = round(100 * row["attention_tflops"] / meas, 2) if meas else None
+        line["routing_sweep"] = {
+            "note": "attention kernel alone on this run's Q/K/V/Q8/K8, other Bernoulli 64x64 INT8 masks "
+                    "(p = 0.5 is the north star's operating point); device-timed, max over ranks",
+            "points": sweep}
     if cpu is not None:
         line["cpu_baseline"] = cpu
     emit(line)
+
+
+def routing_sweep(args, cfg, w, out, quantized, stream, world, ps=(0.0, 0.5, 1.0), launches=10):
+    """Attention alone at other INT8 routing fractions on the same inputs:
+    a fresh Bernoulli 64x64 mask per point (seeded from the config's seed),
+    `launches` timed launches after one untimed one."""
+    import torch
+    import tilemix_b200 as tm
+    from tilemix_b200 import workloads
+    H, S, D = w["heads"], w["S"], w["D"]
+    qb = (S + 63) // 64
+    f_eff = workloads.effective_flops(cfg, H)
+    points = []
+    for i, p in enumerate(ps):
+        g = torch.Generator().manual_seed(cfg["seed"] * 1000 + i)
+        mask = (torch.rand((H, qb, qb), generator=g) < p).to(torch.uint8)
+        words = torch.from_numpy(workloads.pack_block_mask64(mask.numpy(), S, S)).cuda()
+        routing = tm.TileMixRouting(words, words.numel(), 2)
+
+        def attend():
+            tm.check(tm.tilemix_attention_batched(w["q"], w["k"], w["v"], out, H, S, S, D, w["score_scale"],
+                                                  cfg["causal"], stream, routing, quantized), "attention")
+        attend()
+        barrier(world)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(launches):
+            attend()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = reduce_max(a.elapsed_time(b) / launches, world)
+        points.append({"p": p, "int8_fraction_realised": round(workloads.realised_int8_fraction(mask, cfg["causal"]), 4),
+                       "attention_ms": round(ms, 4), "attention_tflops": round(f_eff / (ms * 1e-3) / 1e12, 1)})
+    err, status = tm.read_and_clear_status()
+    tm.check(err, "status")
+    if status:
+        raise SystemExit(f"kernel watchdog reported status {status:#x}")
+    return points
 
 
 # ------------------------------------------------------------ backward arm
