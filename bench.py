@@ -251,12 +251,15 @@ def config_block(args, world: int) -> dict:
 
 
 # ------------------------------------------------------------- CPU baseline
-def cpu_reference_sample(w_host: dict, cfg: dict, target_s: float) -> dict:
+def cpu_reference_sample(w_host: dict, cfg: dict, target_s: float, gpu_out=None) -> dict:
     """Time the reference's own CPU path (oracle/_ref: reference_quantize and
     reference_tilemix from src/tests/reference_tilemix.h; a causal row runs the
     reference on its key prefix) on a bounded sample of the workload -- whole
     heads, all rows, on all host cores -- and extrapolate to the full batch.
-    Falls back to the C restatement (kind "port") without the reference build."""
+    Falls back to the C restatement (kind "port") without the reference build.
+    With gpu_out ([heads, S, D] fp32 on the host: what the product computed
+    from the same inputs in this run), the sampled heads' reference outputs
+    are also compared with it (the checker, not part of the timed product)."""
     import numpy as np
     import oracle
     if not oracle.ORACLE_SO.exists() or (not oracle.ref_available() and oracle.reference_tree_present()):
@@ -287,11 +290,17 @@ def cpu_reference_sample(w_host: dict, cfg: dict, target_s: float) -> dict:
         t_quant = time.perf_counter() - t
         bits = oracle.decode_routing(w_host["words"][h * wc:(h + 1) * wc], S, S, 2)[None]
         t = time.perf_counter()
-        oracle.tilemix_sampled(q[sl], k[sl], v[sl], q8[None], k8[None], qs[None], ks[None], bits,
-                               np.array([0], np.int32), rows, 1.0 / math.sqrt(D), causal,
-                               use_reference=use_ref)
-        return t_quant, time.perf_counter() - t
+        ref = oracle.tilemix_sampled(q[sl], k[sl], v[sl], q8[None], k8[None], qs[None], ks[None], bits,
+                                     np.array([0], np.int32), rows, 1.0 / math.sqrt(D), causal,
+                                     use_reference=use_ref)
+        elapsed = time.perf_counter() - t
+        if gpu_out is not None:
+            diff = np.abs(gpu_out[h].astype(np.float64) - ref[0])
+            checks.append((float(diff.max()), float(np.sum(diff * diff)), float(np.sum(ref[0] * ref[0])),
+                           int(np.count_nonzero(diff > 2e-3)), int(diff.size)))
+        return t_quant, elapsed
 
+    checks = []
     tq, ta = run_head(0)
     n_heads = int(max(1, min(avail, math.ceil(target_s / max(ta + tq, 1e-6)))))
     for h in range(1, n_heads):
@@ -303,11 +312,22 @@ def cpu_reference_sample(w_host: dict, cfg: dict, target_s: float) -> dict:
     from tilemix_b200 import workloads
     f_eff = workloads.effective_flops(cfg)
     step_s = f_eff / rate + quant_per_head * H / threads   # quantization parallel over heads
-    return {"value": f_eff / step_s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
-            "sample": (f"{n_heads} whole head(s) of S={S} through reference_quantize (1 thread) and "
-                       f"reference_tilemix ({'causal: each row on its key prefix, ' if causal else ''}"
-                       f"{threads} OpenMP threads over rows; {ta + tq:.1f} s), extrapolated to all {H} heads"),
-            "step_seconds": step_s}
+    result = {"value": f_eff / step_s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+              "sample": (f"{n_heads} whole head(s) of S={S} through reference_quantize (1 thread) and "
+                         f"reference_tilemix ({'causal: each row on its key prefix, ' if causal else ''}"
+                         f"{threads} OpenMP threads over rows; {ta + tq:.1f} s), extrapolated to all {H} heads"),
+              "step_seconds": step_s}
+    if checks:
+        max_abs = max(c[0] for c in checks)
+        rel_l2 = math.sqrt(sum(c[1] for c in checks) / max(sum(c[2] for c in checks), 1e-300))
+        result["parity"] = {"heads": len(checks), "max_abs": max_abs, "rel_l2": rel_l2,
+                            "bar": "max_abs <= 2e-3 and rel_l2 <= 1e-3",
+                            "pass": bool(max_abs <= 2e-3 and rel_l2 <= 1e-3),
+                            "elements_over_max_abs": sum(c[3] for c in checks),
+                            "elements": sum(c[4] for c in checks),
+                            "against": f"reference_tilemix ({kind}) on this run's inputs and routing words; the "
+                                       "product's output from the end-to-end leg"}
+    return result
 
 
 # ------------------------------------------------------------------ our arm
@@ -449,12 +469,14 @@ def run_tilemix(args, rank, world, local):
             "ranks_copying_at_once": world}
 
     cpu = None
+    parity = None
     if rank == 0 and world == 1:
         nh = min(H, 32)
         host = {"q": hq.numpy()[:nh].copy(), "k": hk.numpy()[:nh].copy(), "v": hv.numpy()[:nh].copy(),
-                "words": w["words"].numpy()[: nh * (w["words"].numel() // H)].copy()}
-        c = cpu_reference_sample(host, cfg, args.cpu_seconds)
+                "words": hwords.numpy()[: nh * (hwords.numel() // H)].copy()}
+        c = cpu_reference_sample(host, cfg, args.cpu_seconds, gpu_out=hout.numpy()[:nh])
         cpu = {key: c[key] for key in ("value", "unit", "cores", "kind", "sample")}
+        parity = c.get("parity")
 
     if rank != 0:
         return
@@ -522,6 +544,8 @@ def run_tilemix(args, rank, world, local):
             "points": sweep}
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if parity is not None:
+        line["parity_of_timed_inputs"] = parity
     emit(line)
 
 

@@ -5,6 +5,7 @@ so the one-JSON-line-on-stdout contract is checked here; the GPU arm prints
 through the same function.
 """
 import json
+import math
 import os
 import subprocess
 import sys
@@ -120,3 +121,32 @@ def test_backward_cpu_sample_is_bounded_and_positive():
     bench = _bench_module()
     c = bench.cpu_backward_sample(256, 64, 0.125, True, 0.2)
     assert c["value"] > 0 and c["kind"] == "port" and c["cores"] >= 1
+
+
+def test_cpu_reference_sample_checks_the_products_output():
+    """The CPU-baseline leg compares the sampled heads' reference outputs with
+    the output the product computed in the same run: the oracle's own output
+    passes, and an output off by 1e-2 in one element fails the 2e-3 bar."""
+    import numpy as np
+    import oracle
+    from tilemix_b200 import workloads
+    bench = _bench_module()
+    w = workloads.make_inputs("c1", p=0.5, heads=2, seq=128)
+    cfg = w["cfg"]
+    host = {"q": w["q"].numpy(), "k": w["k"].numpy(), "v": w["v"].numpy(), "words": w["words"].numpy()}
+    heads, S, D = w["heads"], w["S"], w["D"]
+    wc = host["words"].size // heads
+    expect = np.empty((heads, S, D), np.float32)
+    for h in range(heads):
+        q8, qs = oracle.quantize(host["q"][h], 128)
+        k8, ks = oracle.quantize(host["k"][h], 64)
+        bits = oracle.decode_routing(host["words"][h * wc:(h + 1) * wc], S, S, 2)[None]
+        expect[h] = oracle.tilemix_sampled(host["q"][h:h + 1], host["k"][h:h + 1], host["v"][h:h + 1], q8[None],
+                                           k8[None], qs[None], ks[None], bits, np.array([0], np.int32),
+                                           np.arange(S, dtype=np.int32), 1.0 / math.sqrt(D), cfg["causal"])[0]
+    good = bench.cpu_reference_sample(host, cfg, 100.0, gpu_out=expect)["parity"]
+    assert good["heads"] == heads and good["pass"] and good["max_abs"] < 1e-6
+    bad_out = expect.copy()
+    bad_out[1, 5, 7] += 1e-2
+    bad = bench.cpu_reference_sample(host, cfg, 100.0, gpu_out=bad_out)["parity"]
+    assert not bad["pass"] and abs(bad["max_abs"] - 1e-2) < 1e-4
