@@ -417,7 +417,8 @@ def run_tilemix(args, rank, world, local):
     if policy:
         f_real = workloads.int8_fraction_from_words(words.cpu().numpy(), H, S, cfg["causal"])
     single_share = (float((v_absmax.float() <= 3.5).float().mean()) if args.v_hint else 0.0)
-    sweep = routing_sweep(args, cfg, w, out, quantized, stream, world) if not policy and not args.v_hint else None
+    sweep = (routing_sweep(args, cfg, w, out, quantized, stream, world, job_flops)
+             if not policy and not args.v_hint else None)
     step_ms = reduce_max(total_ms / n, world)
     attn_avg = reduce_max(sum(attn_ms) / n, world)
     quant_avg = reduce_max(sum(quant_ms) / n, world)
@@ -537,10 +538,11 @@ def run_tilemix(args, rank, world, local):
         for row in sweep:
             meas = (mix(f_eff, row["int8_fraction_realised"], p_f16=peaks["bf16_tflops"] * 1e12,
                         p_i8=i8_meas * 1e12) / 1e12 if i8_meas else None)
-            row["pct_of_mix_peak_measured"] = round(100 * row["attention_tflops"] / meas, 2) if meas else None
+            row["pct_of_mix_peak_measured"] = round(100 * row["attention_tflops_per_gpu"] / meas, 2) if meas else None
         line["routing_sweep"] = {
             "note": "attention kernel alone on this run's Q/K/V/Q8/K8, other Bernoulli 64x64 INT8 masks "
-                    "(p = 0.5 is the north star's operating point); device-timed, max over ranks",
+                    "(p = 0.5 is the north star's operating point); device-timed, max over ranks; attention_tflops "
+                    "job-wide like value, attention_tflops_per_gpu and pct_of_mix_peak_measured per GPU",
             "points": sweep}
     if cpu is not None:
         line["cpu_baseline"] = cpu
@@ -549,10 +551,11 @@ def run_tilemix(args, rank, world, local):
     emit(line)
 
 
-def routing_sweep(args, cfg, w, out, quantized, stream, world, ps=(0.0, 0.5, 1.0), launches=10):
+def routing_sweep(args, cfg, w, out, quantized, stream, world, job_flops, ps=(0.0, 0.5, 1.0), launches=10):
     """Attention alone at other INT8 routing fractions on the same inputs:
     a fresh Bernoulli 64x64 mask per point (seeded from the config's seed),
-    `launches` timed launches after one untimed one."""
+    `launches` timed launches after one untimed one; TFLOP/s per GPU (this
+    rank's heads) and for the whole job (max time over ranks)."""
     import torch
     import tilemix_b200 as tm
     from tilemix_b200 import workloads
@@ -580,7 +583,8 @@ def routing_sweep(args, cfg, w, out, quantized, stream, world, ps=(0.0, 0.5, 1.0
         torch.cuda.synchronize()
         ms = reduce_max(a.elapsed_time(b) / launches, world)
         points.append({"p": p, "int8_fraction_realised": round(workloads.realised_int8_fraction(mask, cfg["causal"]), 4),
-                       "attention_ms": round(ms, 4), "attention_tflops": round(f_eff / (ms * 1e-3) / 1e12, 1)})
+                       "attention_ms": round(ms, 4), "attention_tflops": round(job_flops / (ms * 1e-3) / 1e12, 1),
+                       "attention_tflops_per_gpu": round(f_eff / (ms * 1e-3) / 1e12, 1)})
     err, status = tm.read_and_clear_status()
     tm.check(err, "status")
     if status:
