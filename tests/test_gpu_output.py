@@ -4,7 +4,8 @@ Every element written is exactly the round-to-nearest-even of the fp32 output
 the default entry point (tilemix_attention_batched) writes for the same
 inputs, in BSHD and padded layouts, on the 16-byte store path and the scalar
 one (odd d, odd strides, an unaligned base), and nothing outside the layout's
-elements is touched."""
+elements is touched. The fp16 / bf16 outputs are also checked directly
+against the fp64 oracle."""
 import math
 
 import pytest
@@ -91,3 +92,35 @@ def test_bhsd_strides_equal_default_layout():
     out = torch.full((H, S, D), SENTINEL, dtype=torch.float32, device="cuda")
     run_out(w, True, dev_inputs, tm.TileMixOutput(out, 0, 1, S * D, 0, D))
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_bshd_against_oracle(dtype):
+    """The fp16 / bf16 BSHD output checked directly against the fp64 oracle
+    (not only through the fp32 entry point): every element within the parity
+    bar plus half an ulp of the output type at the expected value (the
+    rounding that storing in that type adds), and the relative L2 error within
+    its bar plus the type's unit roundoff."""
+    import numpy as np
+    import oracle
+    B, H, S, D = 2, 2, 300, 128
+    w = workloads.make_inputs("c3", batch=B, heads=H, seq=S)
+    ref, dev_inputs = default_output(w, True, True, B, H)
+    out = torch.full((B, S, H, D), SENTINEL, dtype=dtype, device="cuda")
+    run_out(w, True, dev_inputs, tm.TileMixOutput.bshd(out, H))
+    heads = B * H
+    q, k, v = (w[n].numpy() for n in ("q", "k", "v"))
+    q8, qs = oracle.quantize(q, 128)
+    k8, ks = oracle.quantize(k, 64)
+    words = w["words"].numpy()
+    wc = words.size // heads
+    bits = np.stack([oracle.decode_routing(words[h * wc:(h + 1) * wc], S, S, 2) for h in range(heads)])
+    expect = oracle.tilemix_attention(q, k, v, q8, k8, qs, ks, bits, w["score_scale"], causal=True)
+    got = out.float().cpu().permute(0, 2, 1, 3).reshape(heads, S, D).numpy().astype(np.float64)
+    unit = {torch.float16: 2.0 ** -11, torch.bfloat16: 2.0 ** -8}[dtype]
+    bound = 2e-3 + unit * np.abs(expect) + 2.0 ** -24      # the last term covers fp16 subnormals
+    assert np.all(np.abs(got - expect) <= bound), float(np.max(np.abs(got - expect) - bound))
+    rel_l2 = float(np.linalg.norm(got - expect) / np.linalg.norm(expect))
+    assert rel_l2 <= 1e-3 + unit, rel_l2
+    err, status = tm.read_and_clear_status()
+    assert err == 0 and status == 0
